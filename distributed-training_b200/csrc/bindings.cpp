@@ -1,0 +1,125 @@
+// Python bindings for the sm_100a kernels (one extension module, `_C`).
+#include <torch/extension.h>
+#include <atomic>
+
+namespace dtb {
+
+static std::atomic<long long> g_launches{0};
+void count_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+int64_t launch_count() { return g_launches.load(std::memory_order_relaxed); }
+
+// gemm.cu
+void gemm(torch::Tensor a, bool a_trans, torch::Tensor b, bool b_trans, torch::Tensor out, int64_t epi,
+          c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> resid, c10::optional<torch::Tensor> aux,
+          double alpha, bool accumulate, int64_t force_bn, int64_t force_splits,
+          c10::optional<torch::Tensor> workspace);
+std::vector<int64_t> gemm_tiling(int64_t M, int64_t N, int64_t K);
+// layernorm.cu
+std::vector<torch::Tensor> layernorm_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor b, double eps);
+torch::Tensor layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor mean,
+                            torch::Tensor rstd, c10::optional<torch::Tensor> dresid, torch::Tensor dw,
+                            torch::Tensor db, bool accumulate);
+void bias_grad(torch::Tensor g, torch::Tensor db, bool accumulate);
+// embed_xent.cu
+torch::Tensor embed_fwd(torch::Tensor idx, torch::Tensor tok, torch::Tensor pos, torch::Tensor bad_flag);
+void embed_bwd(torch::Tensor sorted_ids, torch::Tensor perm, torch::Tensor dx, torch::Tensor dtok,
+               torch::Tensor dpos, int64_t B, int64_t T, bool accumulate);
+std::vector<torch::Tensor> xent_fwd(torch::Tensor logits, torch::Tensor tgt);
+void xent_bwd(torch::Tensor logits, torch::Tensor tgt, torch::Tensor lse, torch::Tensor gscale);
+// optim.cu
+void adamw_step(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, c10::optional<torch::Tensor> p16,
+                double lr, double b1, double b2, double eps, double wd, int64_t t, c10::optional<torch::Tensor> sq,
+                double max_norm);
+void grad_sqnorm(torch::Tensor g, torch::Tensor out, double scale);
+void cast_f32_bf16(torch::Tensor x, torch::Tensor y);
+void scale_f32(torch::Tensor x, double s);
+// attention.cu
+std::vector<torch::Tensor> attn_fwd(torch::Tensor qkv, int64_t B, int64_t T, int64_t H, int64_t D);
+torch::Tensor attn_bwd(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torch::Tensor lse, int64_t B,
+                       int64_t T, int64_t H, int64_t D);
+// comm.cu
+std::tuple<int64_t, torch::Tensor> symm_alloc(int64_t nbytes);
+int64_t symm_open(torch::Tensor handle);
+void symm_close(int64_t peer_ptr);
+void symm_free(int64_t ptr);
+torch::Tensor tensor_from_ptr(int64_t ptr, std::vector<int64_t> sizes, c10::ScalarType dtype, int64_t device);
+int64_t comm_status();
+void comm_status_clear();
+int64_t allreduce(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> bufs,
+                  int64_t byte_offset, int64_t n, int64_t in_dtype, int64_t out_ptr, int64_t out_dtype, int64_t algo,
+                  int64_t order, double scale, double timeout_s, int64_t blocks);
+int64_t reduce_scatter(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> bufs,
+                       int64_t byte_offset, int64_t n, int64_t dtype, int64_t out_ptr, int64_t order, double scale,
+                       int64_t sq_part_ptr, double timeout_s, int64_t blocks);
+int64_t all_gather(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> bufs,
+                   int64_t byte_offset, int64_t n, int64_t dtype, double timeout_s, int64_t blocks);
+int64_t broadcast(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> bufs,
+                  int64_t byte_offset, int64_t nbytes, int64_t root, int64_t cast_src, int64_t out16, int64_t n16,
+                  double timeout_s, int64_t blocks);
+int64_t device_barrier(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, double timeout_s);
+int64_t zero_adamw_allgather(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> sq_parts,
+                             int64_t nparts, torch::Tensor master, torch::Tensor grad, torch::Tensor m,
+                             torch::Tensor v, std::vector<int64_t> work16, std::vector<int64_t> master32, int64_t n,
+                             double lr, double b1, double b2, double eps, double wd, int64_t t, double max_norm,
+                             c10::optional<torch::Tensor> sq_out, bool gather_master, double timeout_s,
+                             int64_t blocks);
+int64_t comm_max_blocks();
+int64_t comm_max_ranks();
+
+int status_gemm();
+int status_layernorm();
+int status_embed_xent();
+int status_optim();
+int status_attention();
+int status_comm();
+
+// First non-zero device status word over all kernel files (and clears them).
+int64_t device_status() {
+  int codes[] = {status_gemm(), status_layernorm(), status_embed_xent(), status_optim(), status_attention(),
+                 status_comm()};
+  for (int c : codes)
+    if (c) return c;
+  return 0;
+}
+
+}  // namespace dtb
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  using namespace dtb;
+  namespace py = pybind11;
+  m.def("launch_count", &launch_count);
+  m.def("device_status", &device_status);
+  m.def("gemm", &gemm, py::arg("a"), py::arg("a_trans"), py::arg("b"), py::arg("b_trans"), py::arg("out"),
+        py::arg("epi"), py::arg("bias") = py::none(), py::arg("resid") = py::none(), py::arg("aux") = py::none(),
+        py::arg("alpha") = 1.0, py::arg("accumulate") = false, py::arg("force_bn") = 0, py::arg("force_splits") = 0,
+        py::arg("workspace") = py::none());
+  m.def("gemm_tiling", &gemm_tiling);
+  m.def("layernorm_fwd", &layernorm_fwd);
+  m.def("layernorm_bwd", &layernorm_bwd);
+  m.def("bias_grad", &bias_grad);
+  m.def("embed_fwd", &embed_fwd);
+  m.def("embed_bwd", &embed_bwd);
+  m.def("xent_fwd", &xent_fwd);
+  m.def("xent_bwd", &xent_bwd);
+  m.def("adamw_step", &adamw_step);
+  m.def("grad_sqnorm", &grad_sqnorm);
+  m.def("cast_f32_bf16", &cast_f32_bf16);
+  m.def("scale_f32", &scale_f32);
+  m.def("attn_fwd", &attn_fwd);
+  m.def("attn_bwd", &attn_bwd);
+  m.def("symm_alloc", &symm_alloc);
+  m.def("symm_open", &symm_open);
+  m.def("symm_close", &symm_close);
+  m.def("symm_free", &symm_free);
+  m.def("tensor_from_ptr", &tensor_from_ptr);
+  m.def("comm_status", &comm_status);
+  m.def("comm_status_clear", &comm_status_clear);
+  m.def("allreduce", &allreduce);
+  m.def("reduce_scatter", &reduce_scatter);
+  m.def("all_gather", &all_gather);
+  m.def("broadcast", &broadcast);
+  m.def("device_barrier", &device_barrier);
+  m.def("zero_adamw_allgather", &zero_adamw_allgather);
+  m.def("comm_max_blocks", &comm_max_blocks);
+  m.def("comm_max_ranks", &comm_max_ranks);
+}

@@ -1,0 +1,577 @@
+// NVLink / NVSwitch collectives over peer-mapped ("symmetric") device buffers.
+//
+// Replaces the reference's TCP collectives (dtrain/comm.py:292-391): ring and
+// direct all-reduce, reduce-scatter, all-gather, broadcast, barrier.  One process
+// per GPU; every rank allocates its buffers with cudaMalloc, exports them with
+// cudaIpcGetMemHandle and maps its peers' buffers (the handles travel through the
+// rendezvous store).  Kernels then read and write peer memory directly with
+// ordinary loads and stores over NVLink - no TMA, no multicast.
+//
+// Summation orders are fixed so results are bit-identical on every rank:
+//   ORDER_RANK   : x_0 + x_1 + ... + x_{W-1}        (dtrain "direct", comm.py:374-391)
+//   ORDER_CYCLIC : chunk c summed x_c + x_{c+1} + ... + x_{c-1}  (dtrain "ring",
+//                  comm.py:342-355: the chunk travels round the ring from rank c)
+// In a two-shot all-reduce the owner of each chunk reduces it in that order and
+// everyone copies the owner's result, so all ranks hold identical bits.
+//
+// Synchronisation: per-CTA flags.  CTA b of rank r writes an epoch number into
+// slot [b][r] of every peer's signal pad (release, system scope) and waits until
+// slot [b][p] of its own pad reaches the epoch for every peer p (acquire).  The
+// same CTA index handles the same slice of every chunk on every rank, so CTA-level
+// barriers are enough.  Each wait gives up after `timeout_ns` (%globaltimer),
+// writes kStatusPeerTimeout into a host-mapped status word and makes the kernel
+// return: a dead peer produces an error on the host, not a hung GPU.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+
+namespace dtb {
+
+constexpr int kMaxRanks = 8;
+constexpr int kMaxCommBlocks = 128;
+constexpr int kCommThreads = 512;
+
+enum : int { ORDER_RANK = 0, ORDER_CYCLIC = 1 };
+enum : int { DT_F32 = 0, DT_BF16 = 1 };
+
+struct Peers {
+  void* p[kMaxRanks];
+};
+struct Sigs {
+  uint32_t* p[kMaxRanks];
+};
+
+struct CommCtx {
+  Sigs sig;           // every rank's signal pad [kMaxCommBlocks][kMaxRanks]
+  int rank, world;
+  uint32_t epoch;     // first epoch this launch may use
+  uint64_t timeout_ns;
+  int* host_status;   // host-mapped status word (device pointer)
+};
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// CTA-level barrier across ranks.  Returns false if a peer did not arrive in time.
+__device__ bool cta_barrier(const CommCtx& c, uint32_t epoch) {
+  __shared__ int failed;
+  __syncthreads();
+  if (threadIdx.x == 0) failed = 0;
+  __syncthreads();
+  if (threadIdx.x < c.world) {
+    const int p = threadIdx.x;
+    __threadfence_system();
+    st_release_sys(c.sig.p[p] + blockIdx.x * kMaxRanks + c.rank, epoch);
+    const uint32_t* mine = c.sig.p[c.rank] + blockIdx.x * kMaxRanks + p;
+    uint64_t t0 = 0;
+    for (uint32_t i = 0;; ++i) {
+      const uint32_t v = ld_acquire_sys(mine);
+      if ((int)(v - epoch) >= 0) break;
+      if ((i & 63u) == 0u) {
+        const uint64_t now = globaltimer_ns();
+        if (t0 == 0) t0 = now;
+        else if (now - t0 > c.timeout_ns) {
+          atomicExch(&failed, 1);
+          atomicCAS(c.host_status, 0, kStatusPeerTimeout);
+          set_status(kStatusPeerTimeout);
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  return failed == 0;
+}
+
+// [lo, hi) of chunk `c` of an n-element buffer split over W ranks: the first
+// n % W chunks get one extra element (dtrain/comm.py:220-226).
+__device__ __forceinline__ void chunk_bounds(long n, int W, int c, long& lo, long& hi) {
+  const long base = n / W, extra = n % W;
+  lo = c * base + min((long)c, extra);
+  hi = lo + base + (c < extra ? 1 : 0);
+}
+
+// Sub-range of [lo, hi) handled by this CTA (same on every rank).
+__device__ __forceinline__ void cta_slice(long lo, long hi, long& a, long& b) {
+  const long len = hi - lo;
+  const long per = (((len + gridDim.x - 1) / gridDim.x) + 63) & ~63L;
+  a = min(hi, lo + (long)blockIdx.x * per);
+  b = min(hi, a + per);
+}
+
+template <typename T>
+__device__ __forceinline__ float ldf(const T* p);
+template <>
+__device__ __forceinline__ float ldf<float>(const float* p) { return __ldcg(p); }
+template <>
+__device__ __forceinline__ float ldf<bf16>(const bf16* p) {
+  unsigned short u = __ldcg(reinterpret_cast<const unsigned short*>(p));
+  return __uint_as_float(((uint32_t)u) << 16);
+}
+template <typename T>
+__device__ __forceinline__ void stf(T* p, float v);
+template <>
+__device__ __forceinline__ void stf<float>(float* p, float v) { *p = v; }
+template <>
+__device__ __forceinline__ void stf<bf16>(bf16* p, float v) { *p = f2bf(v); }
+
+// Reduce x[i] over ranks in the given order (starting rank `first`).
+template <typename TI>
+__device__ __forceinline__ float reduce_elem(const Peers& in, long i, int W, int first) {
+  int r = first;
+  float acc = ldf(reinterpret_cast<const TI*>(in.p[r]) + i);
+  for (int k = 1; k < W; ++k) {
+    r = (r + 1 == W) ? 0 : r + 1;
+    acc += ldf(reinterpret_cast<const TI*>(in.p[r]) + i);
+  }
+  return acc;
+}
+
+// Vectorised fp32 path: 4 elements per thread per step.
+__device__ __forceinline__ float4 reduce_vec4(const Peers& in, long i, int W, int first) {
+  int r = first;
+  float4 acc = __ldcg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(in.p[r]) + i));
+  for (int k = 1; k < W; ++k) {
+    r = (r + 1 == W) ? 0 : r + 1;
+    const float4 v = __ldcg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(in.p[r]) + i));
+    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+  }
+  return acc;
+}
+
+// Reduce elements [a, b) into `out` (index space of the buffer), scaled.
+// If sq != nullptr, also accumulate sum of squares of the written values (fp64).
+// All ranks' buffers share one byte offset from 256-byte aligned bases, so they
+// have the same 16-byte phase; the vector loop runs when `out` shares it too.
+template <typename TI, typename TO>
+__device__ __forceinline__ void reduce_range(const Peers& in, TO* out, long a, long b, int W, int first, float scale,
+                                             double* sq) {
+  double s = 0.0;
+  if (a >= b) { if (sq) *sq += s; return; }
+  if constexpr (std::is_same<TI, float>::value && std::is_same<TO, float>::value) {
+    const uintptr_t ain = reinterpret_cast<uintptr_t>(reinterpret_cast<const float*>(in.p[first]) + a);
+    const uintptr_t aout = reinterpret_cast<uintptr_t>(out + a);
+    long head = a, ve = a;
+    if (((ain ^ aout) & 15) == 0 && (ain & 3) == 0) {
+      head = min(b, a + (long)(((16 - (ain & 15)) & 15) / 4));
+      ve = head + ((b - head) & ~3L);
+    }
+    for (long i = a + threadIdx.x; i < head; i += blockDim.x) {
+      const float v = reduce_elem<TI>(in, i, W, first) * scale;
+      out[i] = v;
+      s += (double)v * v;
+    }
+    for (long i = head + threadIdx.x * 4; i < ve; i += (long)blockDim.x * 4) {
+      float4 v = reduce_vec4(in, i, W, first);
+      v.x *= scale; v.y *= scale; v.z *= scale; v.w *= scale;
+      *reinterpret_cast<float4*>(out + i) = v;
+      s += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
+    }
+    for (long i = max(ve, head) + threadIdx.x; i < b; i += blockDim.x) {
+      const float v = reduce_elem<TI>(in, i, W, first) * scale;
+      out[i] = v;
+      s += (double)v * v;
+    }
+  } else {
+    for (long i = a + threadIdx.x; i < b; i += blockDim.x) {
+      const float v = reduce_elem<TI>(in, i, W, first) * scale;
+      stf<TO>(out + i, v);
+      s += (double)v * v;
+    }
+  }
+  if (sq) *sq += s;
+}
+
+// Copy elements [a, b) from src to dst (typically peer -> local) with 16-byte
+// vectors when both pointers share a 16-byte phase.
+template <typename T>
+__device__ __forceinline__ void copy_range(const T* src, T* dst, long a, long b) {
+  const char* s = reinterpret_cast<const char*>(src + a);
+  char* d = reinterpret_cast<char*>(dst + a);
+  const long nbytes = (b - a) * (long)sizeof(T);
+  if (nbytes <= 0) return;
+  const uintptr_t ps = reinterpret_cast<uintptr_t>(s), pd = reinterpret_cast<uintptr_t>(d);
+  if (((ps ^ pd) & 15) == 0) {
+    const long head = min(nbytes, (long)((16 - (ps & 15)) & 15));
+    const long nv = (nbytes - head) / 16;
+    for (long i = threadIdx.x; i < head; i += blockDim.x) d[i] = s[i];
+    const uint4* sv = reinterpret_cast<const uint4*>(s + head);
+    uint4* dv = reinterpret_cast<uint4*>(d + head);
+    for (long i = threadIdx.x; i < nv; i += blockDim.x) dv[i] = __ldcg(sv + i);
+    for (long i = head + nv * 16 + threadIdx.x; i < nbytes; i += blockDim.x) d[i] = s[i];
+  } else {
+    for (long i = threadIdx.x; i < nbytes; i += blockDim.x) d[i] = s[i];
+  }
+}
+
+// ---------------------------------------------------------------- kernels
+// One-shot all-reduce: every rank reduces the whole buffer from all peers (order
+// ORDER_RANK or ORDER_CYCLIC over the same chunking as the two-shot) into `out`.
+template <typename TI, typename TO>
+__global__ void __launch_bounds__(kCommThreads)
+    allreduce_oneshot_kernel(CommCtx c, Peers in, TO* out, long n, int order, float scale) {
+  if (!cta_barrier(c, c.epoch)) return;
+  for (int ch = 0; ch < c.world; ++ch) {
+    long lo, hi, a, b;
+    chunk_bounds(n, c.world, ch, lo, hi);
+    cta_slice(lo, hi, a, b);
+    reduce_range<TI, TO>(in, out, a, b, c.world, order == ORDER_CYCLIC ? ch : 0, scale, nullptr);
+  }
+  cta_barrier(c, c.epoch + 1);
+}
+
+// Two-shot all-reduce: reduce-scatter into the owner's buffer (in place), then
+// all-gather of the reduced chunks.  `out` is this rank's destination (may be the
+// local input buffer).  in.p[rank] must be this rank's input; in-place is safe
+// because the owner only writes its own chunk, which peers do not read until the
+// middle barrier.
+template <typename T>
+__global__ void __launch_bounds__(kCommThreads)
+    allreduce_twoshot_kernel(CommCtx c, Peers in, T* out, long n, int order, float scale) {
+  if (!cta_barrier(c, c.epoch)) return;
+  long lo, hi, a, b;
+  chunk_bounds(n, c.world, c.rank, lo, hi);
+  cta_slice(lo, hi, a, b);
+  T* mine = reinterpret_cast<T*>(in.p[c.rank]);
+  reduce_range<T, T>(in, mine, a, b, c.world, order == ORDER_CYCLIC ? c.rank : 0, scale, nullptr);
+  if (!cta_barrier(c, c.epoch + 1)) return;
+  for (int k = 0; k < c.world; ++k) {
+    const int p = (c.rank + k) % c.world;
+    chunk_bounds(n, c.world, p, lo, hi);
+    cta_slice(lo, hi, a, b);
+    if (p == c.rank) {
+      if (out != mine) copy_range<T>(mine, out, a, b);
+    } else {
+      copy_range<T>(reinterpret_cast<const T*>(in.p[p]), out, a, b);
+    }
+  }
+  cta_barrier(c, c.epoch + 2);
+}
+
+// Reduce-scatter: chunk `rank` summed in cyclic order from `rank` (bit-equal to
+// dtrain's ring reduce-scatter with rotation, comm.py:310-316,342-362), scaled,
+// written to `out` (this rank's buffer index space).  With sq_part, each CTA also
+// writes the fp64 sum of squares of its slice to sq_part[blockIdx.x].
+template <typename TI, typename TO>
+__global__ void __launch_bounds__(kCommThreads)
+    reduce_scatter_kernel(CommCtx c, Peers in, TO* out, long n, int order, float scale, double* sq_part) {
+  __shared__ double red[kCommThreads / 32];
+  if (!cta_barrier(c, c.epoch)) return;
+  long lo, hi, a, b;
+  chunk_bounds(n, c.world, c.rank, lo, hi);
+  cta_slice(lo, hi, a, b);
+  double s = 0.0;
+  reduce_range<TI, TO>(in, out, a, b, c.world, order == ORDER_CYCLIC ? c.rank : 0, scale, sq_part ? &s : nullptr);
+  if (sq_part) {
+    // fixed-order block reduction
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      double t = 0.0;
+      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+      sq_part[blockIdx.x] = t;
+    }
+  }
+  cta_barrier(c, c.epoch + 1);
+}
+
+// All-gather in place: every rank copies chunk p from rank p into `out`.
+template <typename T>
+__global__ void __launch_bounds__(kCommThreads) all_gather_kernel(CommCtx c, Peers in, T* out, long n) {
+  if (!cta_barrier(c, c.epoch)) return;
+  for (int k = 1; k < c.world; ++k) {
+    const int p = (c.rank + k) % c.world;
+    long lo, hi, a, b;
+    chunk_bounds(n, c.world, p, lo, hi);
+    cta_slice(lo, hi, a, b);
+    copy_range<T>(reinterpret_cast<const T*>(in.p[p]), out, a, b);
+  }
+  cta_barrier(c, c.epoch + 1);
+}
+
+// Broadcast from `root`: non-root ranks pull root's buffer into `out` (with an
+// optional fp32 -> bf16 cast into out16 on every rank, root included).
+__global__ void __launch_bounds__(kCommThreads)
+    broadcast_kernel(CommCtx c, Peers in, void* out, long nbytes, int root, const float* cast_src, bf16* out16,
+                     long n16) {
+  if (!cta_barrier(c, c.epoch)) return;
+  if (c.rank != root && out) {
+    long a, b;
+    cta_slice(0, nbytes, a, b);
+    copy_range<char>(reinterpret_cast<const char*>(in.p[root]), reinterpret_cast<char*>(out), a, b);
+  }
+  if (!cta_barrier(c, c.epoch + 1)) return;
+  if (out16) {
+    long a, b;
+    cta_slice(0, n16, a, b);
+    for (long i = a + threadIdx.x; i < b; i += blockDim.x) out16[i] = f2bf(cast_src[i]);
+  }
+}
+
+__global__ void barrier_kernel(CommCtx c) { cta_barrier(c, c.epoch); }
+
+// ZeRO-1 update, fused with the global-norm exchange and the parameter all-gather.
+// Phase 1: every CTA sums all ranks' per-CTA squared-norm partials (written by
+//          reduce_scatter_kernel into each rank's symmetric sq slot) in rank-then-CTA
+//          order -> identical global norm on every rank, then the clip factor.
+// Phase 2: AdamW on this rank's shard [lo, hi) of the flat fp32 master (dtrain/zero.py:45-62),
+//          writing the fp32 master and the bf16 working copy (symmetric).
+// Phase 3: all-gather of the bf16 working copy (and optionally the fp32 master).
+__global__ void __launch_bounds__(kCommThreads)
+    zero_adamw_allgather_kernel(CommCtx c, Sigs sq_parts, int nparts, float* master, const float* grad,
+                                float* m, float* v, Peers work16, Peers master32, long n, float lr, float b1,
+                                float b2, float eps, float wd, float b1t, float b2t, float max_norm,
+                                double* sq_out, int gather_master) {
+  __shared__ float s_clip;
+  if (!cta_barrier(c, c.epoch)) return;
+  if (threadIdx.x == 0) {
+    double tot = 0.0;
+    for (int r = 0; r < c.world; ++r) {
+      const double* pp = reinterpret_cast<const double*>(sq_parts.p[r]);
+      double rs = 0.0;
+      for (int k = 0; k < nparts; ++k) rs += __ldcg(pp + k);
+      tot += rs;
+    }
+    float cs = 1.f;
+    const double nrm = sqrt(tot);
+    if (max_norm > 0.f && nrm > (double)max_norm && nrm != 0.0) cs = (float)((double)max_norm / (nrm + 1e-6));
+    s_clip = cs;
+    if (blockIdx.x == 0 && sq_out) sq_out[0] = tot;
+  }
+  __syncthreads();
+  const float cs = s_clip;
+  long lo, hi, a, b;
+  chunk_bounds(n, c.world, c.rank, lo, hi);
+  cta_slice(lo, hi, a, b);
+  bf16* w16 = reinterpret_cast<bf16*>(work16.p[c.rank]);
+  for (long i = a + threadIdx.x; i < b; i += blockDim.x) {
+    const long k = i - lo;  // index into the shard-local optimizer state
+    const float gg = grad[i] * cs;
+    float mm = b1 * m[k] + (1.f - b1) * gg;
+    float vv = b2 * v[k] + (1.f - b2) * (gg * gg);
+    float p = master[i];
+    p -= lr * (wd * p);
+    p -= lr * (mm / b1t) / (sqrtf(vv / b2t) + eps);
+    m[k] = mm;
+    v[k] = vv;
+    master[i] = p;
+    if (w16) w16[i] = f2bf(p);
+  }
+  if (!cta_barrier(c, c.epoch + 1)) return;
+  for (int kk = 1; kk < c.world; ++kk) {
+    const int p = (c.rank + kk) % c.world;
+    chunk_bounds(n, c.world, p, lo, hi);
+    cta_slice(lo, hi, a, b);
+    if (w16) copy_range<bf16>(reinterpret_cast<const bf16*>(work16.p[p]), w16, a, b);
+    if (gather_master)
+      copy_range<float>(reinterpret_cast<const float*>(master32.p[p]), master, a, b);
+  }
+  cta_barrier(c, c.epoch + 2);
+}
+
+// ---------------------------------------------------------------- host side
+// Symmetric allocation: cudaMalloc + IPC export.  Returns (ptr, handle bytes).
+std::tuple<int64_t, torch::Tensor> symm_alloc(int64_t nbytes) {
+  void* p = nullptr;
+  C10_CUDA_CHECK(cudaMalloc(&p, (size_t)nbytes));
+  C10_CUDA_CHECK(cudaMemset(p, 0, (size_t)nbytes));
+  cudaIpcMemHandle_t h;
+  C10_CUDA_CHECK(cudaIpcGetMemHandle(&h, p));
+  auto t = torch::empty({(int64_t)sizeof(h)}, torch::kUInt8);
+  std::memcpy(t.data_ptr(), &h, sizeof(h));
+  return {reinterpret_cast<int64_t>(p), t};
+}
+
+int64_t symm_open(torch::Tensor handle) {
+  TORCH_CHECK(handle.numel() == (int64_t)sizeof(cudaIpcMemHandle_t), "symm_open: bad handle size");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle.contiguous().data_ptr(), sizeof(h));
+  void* p = nullptr;
+  C10_CUDA_CHECK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  return reinterpret_cast<int64_t>(p);
+}
+
+void symm_close(int64_t peer_ptr) { cudaIpcCloseMemHandle(reinterpret_cast<void*>(peer_ptr)); }
+void symm_free(int64_t ptr) { cudaFree(reinterpret_cast<void*>(ptr)); }
+
+// A tensor view over raw device memory (no ownership).
+torch::Tensor tensor_from_ptr(int64_t ptr, std::vector<int64_t> sizes, c10::ScalarType dtype, int64_t device) {
+  auto opts = torch::TensorOptions().dtype(dtype).device(torch::kCUDA, device);
+  return torch::from_blob(reinterpret_cast<void*>(ptr), sizes, [](void*) {}, opts);
+}
+
+// Host-mapped status word shared by all comm kernels of this process.
+static int* g_host_status = nullptr;
+static int* g_dev_status = nullptr;
+static void ensure_status() {
+  if (!g_host_status) {
+    C10_CUDA_CHECK(cudaHostAlloc(&g_host_status, sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable));
+    *g_host_status = 0;
+    C10_CUDA_CHECK(cudaHostGetDevicePointer(&g_dev_status, g_host_status, 0));
+  }
+}
+int64_t comm_status() {
+  ensure_status();
+  return *reinterpret_cast<volatile int*>(g_host_status);
+}
+void comm_status_clear() {
+  ensure_status();
+  *reinterpret_cast<volatile int*>(g_host_status) = 0;
+}
+
+static CommCtx make_ctx(const std::vector<int64_t>& sigs, int64_t rank, int64_t epoch, double timeout_s) {
+  ensure_status();
+  CommCtx c{};
+  const int W = (int)sigs.size();
+  TORCH_CHECK(W >= 1 && W <= kMaxRanks, "comm: world size must be 1..8");
+  TORCH_CHECK(rank >= 0 && rank < W, "comm: bad rank");
+  for (int i = 0; i < W; ++i) c.sig.p[i] = reinterpret_cast<uint32_t*>(sigs[i]);
+  c.rank = (int)rank;
+  c.world = W;
+  c.epoch = (uint32_t)epoch;
+  c.timeout_ns = (uint64_t)(timeout_s * 1e9);
+  c.host_status = g_dev_status;
+  return c;
+}
+
+static Peers make_peers(const std::vector<int64_t>& ptrs, int64_t byte_offset) {
+  Peers p{};
+  for (size_t i = 0; i < ptrs.size(); ++i) p.p[i] = reinterpret_cast<char*>(ptrs[i]) + byte_offset;
+  return p;
+}
+
+static int comm_blocks(long bytes, int64_t want) {
+  if (want > 0) return (int)std::min<int64_t>(want, kMaxCommBlocks);
+  const long per = 256 * 1024;  // ~256 KB per CTA before adding more CTAs
+  return (int)std::max<long>(1, std::min<long>(kMaxCommBlocks / 2, (bytes + per - 1) / per));
+}
+
+// Every collective returns the number of epochs it consumed; the caller adds it
+// to its epoch counter (identically on every rank).
+int64_t allreduce(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> bufs,
+                  int64_t byte_offset, int64_t n, int64_t in_dtype, int64_t out_ptr, int64_t out_dtype, int64_t algo,
+                  int64_t order, double scale, double timeout_s, int64_t blocks) {
+  CommCtx c = make_ctx(sigs, rank, epoch, timeout_s);
+  Peers in = make_peers(bufs, byte_offset);
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  const long esz = in_dtype == DT_F32 ? 4 : 2;
+  const int nb = comm_blocks(n * esz, blocks);
+  if (algo == 0) {  // one-shot, out-of-place
+    TORCH_CHECK(out_ptr != 0, "allreduce one-shot needs an output buffer");
+    if (in_dtype == DT_F32 && out_dtype == DT_F32)
+      allreduce_oneshot_kernel<float, float><<<nb, kCommThreads, 0, st>>>(c, in, reinterpret_cast<float*>(out_ptr), n, (int)order, (float)scale);
+    else if (in_dtype == DT_BF16 && out_dtype == DT_F32)
+      allreduce_oneshot_kernel<bf16, float><<<nb, kCommThreads, 0, st>>>(c, in, reinterpret_cast<float*>(out_ptr), n, (int)order, (float)scale);
+    else if (in_dtype == DT_BF16 && out_dtype == DT_BF16)
+      allreduce_oneshot_kernel<bf16, bf16><<<nb, kCommThreads, 0, st>>>(c, in, reinterpret_cast<bf16*>(out_ptr), n, (int)order, (float)scale);
+    else
+      TORCH_CHECK(false, "allreduce: unsupported dtype pair");
+    count_launch();
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return 2;
+  }
+  TORCH_CHECK(in_dtype == out_dtype, "allreduce two-shot: in/out dtypes must match");
+  void* out = out_ptr ? reinterpret_cast<void*>(out_ptr) : in.p[rank];
+  if (in_dtype == DT_F32)
+    allreduce_twoshot_kernel<float><<<nb, kCommThreads, 0, st>>>(c, in, reinterpret_cast<float*>(out), n, (int)order, (float)scale);
+  else
+    allreduce_twoshot_kernel<bf16><<<nb, kCommThreads, 0, st>>>(c, in, reinterpret_cast<bf16*>(out), n, (int)order, (float)scale);
+  count_launch();
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return 3;
+}
+
+int64_t reduce_scatter(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> bufs,
+                       int64_t byte_offset, int64_t n, int64_t dtype, int64_t out_ptr, int64_t order, double scale,
+                       int64_t sq_part_ptr, double timeout_s, int64_t blocks) {
+  CommCtx c = make_ctx(sigs, rank, epoch, timeout_s);
+  Peers in = make_peers(bufs, byte_offset);
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  const int nb = comm_blocks(n * (dtype == DT_F32 ? 4 : 2), blocks);
+  void* out = out_ptr ? reinterpret_cast<void*>(out_ptr) : in.p[rank];
+  double* sq = reinterpret_cast<double*>(sq_part_ptr);
+  if (dtype == DT_F32)
+    reduce_scatter_kernel<float, float><<<nb, kCommThreads, 0, st>>>(c, in, reinterpret_cast<float*>(out), n, (int)order, (float)scale, sq);
+  else
+    reduce_scatter_kernel<bf16, bf16><<<nb, kCommThreads, 0, st>>>(c, in, reinterpret_cast<bf16*>(out), n, (int)order, (float)scale, sq);
+  count_launch();
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return 2;
+}
+
+int64_t all_gather(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> bufs,
+                   int64_t byte_offset, int64_t n, int64_t dtype, double timeout_s, int64_t blocks) {
+  CommCtx c = make_ctx(sigs, rank, epoch, timeout_s);
+  Peers in = make_peers(bufs, byte_offset);
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  const int nb = comm_blocks(n * (dtype == DT_F32 ? 4 : 2), blocks);
+  if (dtype == DT_F32)
+    all_gather_kernel<float><<<nb, kCommThreads, 0, st>>>(c, in, reinterpret_cast<float*>(in.p[rank]), n);
+  else
+    all_gather_kernel<bf16><<<nb, kCommThreads, 0, st>>>(c, in, reinterpret_cast<bf16*>(in.p[rank]), n);
+  count_launch();
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return 2;
+}
+
+int64_t broadcast(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> bufs,
+                  int64_t byte_offset, int64_t nbytes, int64_t root, int64_t cast_src, int64_t out16, int64_t n16,
+                  double timeout_s, int64_t blocks) {
+  CommCtx c = make_ctx(sigs, rank, epoch, timeout_s);
+  Peers in = make_peers(bufs, byte_offset);
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  const int nb = comm_blocks(nbytes, blocks);
+  broadcast_kernel<<<nb, kCommThreads, 0, st>>>(c, in, in.p[rank], nbytes, (int)root,
+                                                reinterpret_cast<const float*>(cast_src),
+                                                reinterpret_cast<bf16*>(out16), n16);
+  count_launch();
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return 2;
+}
+
+int64_t device_barrier(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, double timeout_s) {
+  CommCtx c = make_ctx(sigs, rank, epoch, timeout_s);
+  barrier_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(c);
+  count_launch();
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return 1;
+}
+
+int64_t zero_adamw_allgather(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> sq_parts,
+                             int64_t nparts, torch::Tensor master, torch::Tensor grad, torch::Tensor m,
+                             torch::Tensor v, std::vector<int64_t> work16, std::vector<int64_t> master32, int64_t n,
+                             double lr, double b1, double b2, double eps, double wd, int64_t t, double max_norm,
+                             c10::optional<torch::Tensor> sq_out, bool gather_master, double timeout_s,
+                             int64_t blocks) {
+  CommCtx c = make_ctx(sigs, rank, epoch, timeout_s);
+  Sigs sp{};
+  for (size_t i = 0; i < sq_parts.size(); ++i) sp.p[i] = reinterpret_cast<uint32_t*>(sq_parts[i]);
+  Peers w16 = make_peers(work16, 0), m32 = make_peers(master32, 0);
+  const float b1t = (float)(1.0 - std::pow(b1, (double)t));
+  const float b2t = (float)(1.0 - std::pow(b2, (double)t));
+  double* sqo = (sq_out && sq_out->defined()) ? sq_out->data_ptr<double>() : nullptr;
+  const int nb = comm_blocks(n * 2, blocks);
+  zero_adamw_allgather_kernel<<<nb, kCommThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
+      c, sp, (int)nparts, master.data_ptr<float>(), grad.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
+      w16, m32, n, (float)lr, (float)b1, (float)b2, (float)eps, (float)wd, b1t, b2t, (float)max_norm, sqo,
+      gather_master ? 1 : 0);
+  count_launch();
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return 3;
+}
+
+int64_t comm_max_blocks() { return kMaxCommBlocks; }
+int64_t comm_max_ranks() { return kMaxRanks; }
+
+DTB_DEFINE_STATUS_READER(status_comm)
+
+}  // namespace dtb

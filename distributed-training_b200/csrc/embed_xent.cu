@@ -1,0 +1,289 @@
+// Token/position embedding and softmax cross-entropy kernels.
+//
+// Embedding (dtrain/autograd.py:199-204, dtrain/nn.py:133): forward gathers
+// tok[idx] + pos[t]; the backward is a scatter-add with repeated indices.  The
+// reference uses np.add.at; here the scatter is made deterministic without float
+// atomics: the host sorts the flat token ids stably (ties keep position order),
+// and one warp per vocabulary row sums its positions' gradient rows in that order.
+//
+// Cross-entropy (dtrain/autograd.py:250-266): mean over rows of logsumexp(z) - z[t].
+// The forward keeps the per-row logsumexp; the backward rewrites the logits buffer
+// in place with (softmax - onehot) * g / n, so the V-wide gradient needs no new
+// allocation.  The mean over rows is a fixed-order reduction.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+
+namespace dtb {
+
+__device__ __forceinline__ void ld8f(const bf16* p, float* v) {
+  uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+__device__ __forceinline__ void st8f(bf16* p, const float* v) {
+  uint4 u;
+  u.x = pack_bf16x2(v[0], v[1]);
+  u.y = pack_bf16x2(v[2], v[3]);
+  u.z = pack_bf16x2(v[4], v[5]);
+  u.w = pack_bf16x2(v[6], v[7]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
+// ------------------------------------------------------------------ embedding
+__global__ void embed_fwd_kernel(const int64_t* __restrict__ idx, const bf16* __restrict__ tok,
+                                 const bf16* __restrict__ pos, bf16* __restrict__ out, long ntok, int T, int C, int V,
+                                 int* __restrict__ bad) {
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;  // one thread per 8 channels
+  const int per_row = C / 8;
+  if (i >= ntok * per_row) return;
+  const long r = i / per_row;
+  const int c = (int)(i % per_row) * 8;
+  int64_t t = idx[r];
+  if (t < 0 || t >= V) {  // out-of-range token: record and emit zeros instead of reading out of bounds
+    if (c == 0) atomicExch(bad, 1);
+    float z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    st8f(out + r * C + c, z);
+    return;
+  }
+  float a[8], b[8];
+  ld8f(tok + t * C + c, a);
+  ld8f(pos + (long)(r % T) * C + c, b);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) a[j] += b[j];
+  st8f(out + r * C + c, a);
+}
+
+// dtok[v] = sum over sorted positions p in [lo(v), hi(v)) of dx[perm[p]]  (one warp per v)
+__global__ void embed_bwd_tok_kernel(const int64_t* __restrict__ sorted_ids, const int64_t* __restrict__ perm,
+                                     long ntok, const bf16* __restrict__ dx, float* __restrict__ dtok, int V, int C,
+                                     int accumulate) {
+  const long v = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (v >= V) return;
+  // lower_bound(v) and lower_bound(v+1) in sorted_ids
+  long lo = 0, hi = ntok;
+  while (lo < hi) {
+    long m = (lo + hi) >> 1;
+    if (sorted_ids[m] < v) lo = m + 1; else hi = m;
+  }
+  const long beg = lo;
+  hi = ntok;
+  while (lo < hi) {
+    long m = (lo + hi) >> 1;
+    if (sorted_ids[m] <= v) lo = m + 1; else hi = m;
+  }
+  const long end = lo;
+  float* out = dtok + v * C;
+  for (int c = lane * 4; c < C; c += 128) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (long p = beg; p < end; ++p) {
+      const bf16* s = dx + perm[p] * C + c;
+      __nv_bfloat162 h0 = *reinterpret_cast<const __nv_bfloat162*>(s);
+      __nv_bfloat162 h1 = *reinterpret_cast<const __nv_bfloat162*>(s + 2);
+      float2 f0 = __bfloat1622float2(h0), f1 = __bfloat1622float2(h1);
+      acc.x += f0.x; acc.y += f0.y; acc.z += f1.x; acc.w += f1.y;
+    }
+    float4* o = reinterpret_cast<float4*>(out + c);
+    if (accumulate) {
+      float4 p = *o;
+      acc.x += p.x; acc.y += p.y; acc.z += p.z; acc.w += p.w;
+    }
+    *o = acc;
+  }
+}
+
+// dpos[t] = sum_b dx[b*T + t]  (fixed order over b)
+__global__ void embed_bwd_pos_kernel(const bf16* __restrict__ dx, float* __restrict__ dpos, int B, int T, int C,
+                                     int accumulate) {
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long)T * C) return;
+  const int t = (int)(i / C), c = (int)(i % C);
+  float s = 0.f;
+  for (int b = 0; b < B; ++b) s += bf2f(dx[((long)b * T + t) * C + c]);
+  dpos[i] = accumulate ? dpos[i] + s : s;
+}
+
+// ------------------------------------------------------------------ cross-entropy
+constexpr int kXentThreads = 512;
+
+__device__ __forceinline__ void online_merge(float& m, float& s, float m2, float s2) {
+  if (m2 == -INFINITY) return;
+  if (m == -INFINITY) { m = m2; s = s2; return; }
+  if (m2 > m) { s = s * __expf(m - m2) + s2; m = m2; }
+  else { s = s + s2 * __expf(m2 - m); }
+}
+
+// One block per row: lse[row] = log(sum(exp(z))), loss[row] = lse - z[target].
+__global__ void __launch_bounds__(kXentThreads)
+    xent_fwd_kernel(const bf16* __restrict__ logits, long ld, const int64_t* __restrict__ tgt, int V,
+                    float* __restrict__ lse_out, float* __restrict__ loss_out, int vec_ok) {
+  const long row = blockIdx.x;
+  const bf16* z = logits + row * ld;
+  float m = -INFINITY, s = 0.f;
+  const int nvec = vec_ok ? V / 8 : 0;
+  for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
+    float v[8];
+    ld8f(z + i * 8, v);
+    float lm = v[0];
+#pragma unroll
+    for (int j = 1; j < 8; ++j) lm = fmaxf(lm, v[j]);
+    float ls = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ls += __expf(v[j] - lm);
+    online_merge(m, s, lm, ls);
+  }
+  for (int i = nvec * 8 + threadIdx.x; i < V; i += blockDim.x) online_merge(m, s, bf2f(z[i]), 1.f);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    online_merge(m, s, m2, s2);
+  }
+  __shared__ float sm_m[kXentThreads / 32], sm_s[kXentThreads / 32];
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) { sm_m[w] = m; sm_s[w] = s; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float M = sm_m[0], S = sm_s[0];
+    for (int k = 1; k < kXentThreads / 32; ++k) online_merge(M, S, sm_m[k], sm_s[k]);
+    const float lse = M + __logf(S);
+    lse_out[row] = lse;
+    const int64_t t = tgt[row];
+    loss_out[row] = (t >= 0 && t < V) ? lse - bf2f(z[t]) : 0.f;
+  }
+}
+
+// loss = mean(loss_rows) in a fixed order (single block).
+__global__ void mean_kernel(const float* __restrict__ x, long n, float* __restrict__ out) {
+  __shared__ double sm[1024];
+  double s = 0.0;
+  for (long i = threadIdx.x; i < n; i += blockDim.x) s += (double)x[i];
+  sm[threadIdx.x] = s;
+  __syncthreads();
+  for (int o = blockDim.x / 2; o > 0; o >>= 1) {
+    if (threadIdx.x < o) sm[threadIdx.x] += sm[threadIdx.x + o];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) out[0] = (float)(sm[0] / (double)n);
+}
+
+// In place: z[row, j] <- (exp(z - lse) - [j == t]) * g / n     (g read from device memory)
+__global__ void __launch_bounds__(kXentThreads)
+    xent_bwd_kernel(bf16* __restrict__ logits, long ld, const int64_t* __restrict__ tgt, int V,
+                    const float* __restrict__ lse, const float* __restrict__ gscale, float inv_n, int vec_ok) {
+  const long row = blockIdx.x;
+  bf16* z = logits + row * ld;
+  const float L = lse[row];
+  const float g = gscale[0] * inv_n;
+  const int64_t t = tgt[row];
+  const int nvec = vec_ok ? V / 8 : 0;
+  for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
+    float v[8];
+    ld8f(z + i * 8, v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float p = __expf(v[j] - L);
+      if (i * 8 + j == t) p -= 1.f;
+      v[j] = p * g;
+    }
+    st8f(z + i * 8, v);
+  }
+  for (int i = nvec * 8 + threadIdx.x; i < V; i += blockDim.x) {
+    float p = __expf(bf2f(z[i]) - L);
+    if (i == t) p -= 1.f;
+    z[i] = f2bf(p * g);
+  }
+}
+
+// ------------------------------------------------------------------ host
+torch::Tensor embed_fwd(torch::Tensor idx, torch::Tensor tok, torch::Tensor pos, torch::Tensor bad_flag) {
+  TORCH_CHECK(idx.scalar_type() == at::kLong && idx.is_contiguous() && idx.dim() == 2, "embed_fwd: idx [B,T] int64");
+  TORCH_CHECK(tok.scalar_type() == at::kBFloat16 && pos.scalar_type() == at::kBFloat16, "embed_fwd: bf16 tables");
+  c10::cuda::CUDAGuard guard(idx.device());
+  const int B = (int)idx.size(0), T = (int)idx.size(1);
+  const int V = (int)tok.size(0), C = (int)tok.size(1);
+  TORCH_CHECK(C % 8 == 0 && pos.size(0) >= T && pos.size(1) == C, "embed_fwd: shapes");
+  auto out = torch::empty({B, T, C}, tok.options());
+  const long ntok = (long)B * T;
+  const long work = ntok * (C / 8);
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  embed_fwd_kernel<<<(unsigned)((work + 255) / 256), 256, 0, st>>>(
+      idx.data_ptr<int64_t>(), reinterpret_cast<const bf16*>(tok.data_ptr()),
+      reinterpret_cast<const bf16*>(pos.data_ptr()), reinterpret_cast<bf16*>(out.data_ptr()), ntok, T, C, V,
+      bad_flag.data_ptr<int>());
+  count_launch();
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return out;
+}
+
+// sorted_ids/perm: stable sort of idx.flatten(); dtok [V,C] fp32, dpos [>=T,C] fp32
+void embed_bwd(torch::Tensor sorted_ids, torch::Tensor perm, torch::Tensor dx, torch::Tensor dtok,
+               torch::Tensor dpos, int64_t B, int64_t T, bool accumulate) {
+  TORCH_CHECK(dx.scalar_type() == at::kBFloat16 && dx.is_contiguous(), "embed_bwd: dx");
+  TORCH_CHECK(dtok.scalar_type() == at::kFloat && dpos.scalar_type() == at::kFloat, "embed_bwd: fp32 grads");
+  c10::cuda::CUDAGuard guard(dx.device());
+  const int V = (int)dtok.size(0), C = (int)dtok.size(1);
+  TORCH_CHECK(C % 4 == 0, "embed_bwd: C % 4");
+  const long ntok = B * T;
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  const long threads = (long)V * 32;
+  embed_bwd_tok_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
+      sorted_ids.data_ptr<int64_t>(), perm.data_ptr<int64_t>(), ntok, reinterpret_cast<const bf16*>(dx.data_ptr()),
+      dtok.data_ptr<float>(), V, C, accumulate ? 1 : 0);
+  const long n = T * (long)C;
+  embed_bwd_pos_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(reinterpret_cast<const bf16*>(dx.data_ptr()),
+                                                                    dpos.data_ptr<float>(), (int)B, (int)T, C,
+                                                                    accumulate ? 1 : 0);
+  count_launch(2);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Returns (loss scalar fp32 [1], lse fp32 [rows]).
+std::vector<torch::Tensor> xent_fwd(torch::Tensor logits, torch::Tensor tgt) {
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1 && logits.scalar_type() == at::kBFloat16, "xent_fwd: logits");
+  TORCH_CHECK(tgt.scalar_type() == at::kLong && tgt.numel() == logits.size(0), "xent_fwd: targets");
+  c10::cuda::CUDAGuard guard(logits.device());
+  const long rows = logits.size(0);
+  const int V = (int)logits.size(1);
+  const int vec_ok = (logits.stride(0) % 8 == 0 && (reinterpret_cast<uintptr_t>(logits.data_ptr()) & 15) == 0) ? 1 : 0;
+  auto lse = torch::empty({rows}, logits.options().dtype(at::kFloat));
+  auto lrow = torch::empty({rows}, logits.options().dtype(at::kFloat));
+  auto loss = torch::empty({}, logits.options().dtype(at::kFloat));
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  auto tg = tgt.contiguous();
+  xent_fwd_kernel<<<(unsigned)rows, kXentThreads, 0, st>>>(reinterpret_cast<const bf16*>(logits.data_ptr()),
+                                                          logits.stride(0), tg.data_ptr<int64_t>(), V,
+                                                          lse.data_ptr<float>(), lrow.data_ptr<float>(), vec_ok);
+  mean_kernel<<<1, 1024, 0, st>>>(lrow.data_ptr<float>(), rows, loss.data_ptr<float>());
+  count_launch(2);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {loss, lse};
+}
+
+void xent_bwd(torch::Tensor logits, torch::Tensor tgt, torch::Tensor lse, torch::Tensor gscale) {
+  c10::cuda::CUDAGuard guard(logits.device());
+  const long rows = logits.size(0);
+  const int V = (int)logits.size(1);
+  TORCH_CHECK(gscale.scalar_type() == at::kFloat && gscale.numel() == 1, "xent_bwd: gscale");
+  auto tg = tgt.contiguous();
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  xent_bwd_kernel<<<(unsigned)rows, kXentThreads, 0, st>>>(reinterpret_cast<bf16*>(logits.data_ptr()),
+                                                          logits.stride(0), tg.data_ptr<int64_t>(), V,
+                                                          lse.data_ptr<float>(), gscale.data_ptr<float>(),
+                                                          1.0f / (float)rows,
+                                                          (logits.stride(0) % 8 == 0 && (reinterpret_cast<uintptr_t>(logits.data_ptr()) & 15) == 0) ? 1 : 0);
+  count_launch();
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+DTB_DEFINE_STATUS_READER(status_embed_xent)
+
+}  // namespace dtb

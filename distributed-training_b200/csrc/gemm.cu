@@ -1,0 +1,582 @@
+// Persistent tcgen05 GEMM for sm_100a with fused epilogues.
+//
+//   C[M,N] (+)= op(A)[M,K] . op(B)[K,N]      bf16 operands, fp32 accumulation in TMEM
+//
+// Replaces the reference's NumPy matmuls of the Linear layers (dtrain/nn.py:63-65,
+// dtrain/autograd.py:102-109): forward Y = X W + b, backward dX = dY W^T and
+// dW = X^T dY.  Operand layouts are chosen per call with the descriptor "major"
+// bits, so no transpose is ever materialised:
+//   forward : A = X  (K-major),  B = W stored (in,out)  -> MN-major
+//   dX      : A = dY (K-major),  B = W stored (in,out)  -> K-major (W^T)
+//   dW      : A = X  stored (tokens,in) -> MN-major,  B = dY (tokens,out) -> MN-major
+//
+// Structure (one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer: 128x64 A tile and BNx64 B tile per stage into
+//               128B-swizzled shared memory, one mbarrier per stage.
+//   warp 1      owns TMEM (allocates 2*BN columns = two accumulators) and one
+//               lane issues tcgen05.mma (M=128, N=BN, K=16) for every stage,
+//               then tcgen05.commit to free the stage / publish the accumulator.
+//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time from their TMEM lane
+//               quarter, apply the fused epilogue, store to global memory.
+// The two TMEM accumulators let the epilogue of tile i overlap the main loop of
+// tile i+1.  Every barrier wait is bounded (common.cuh).
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace dtb {
+
+enum GemmEpi : int {
+  EPI_BF16 = 0,     // out(bf16) = alpha*acc [+ bias] [+ resid]
+  EPI_GELU = 1,     // aux(bf16) = acc + bias ; out(bf16) = gelu(aux)
+  EPI_DGELU = 2,    // out(bf16) = acc * gelu'(aux)
+  EPI_F32 = 3,      // out(f32)  = alpha*acc [+ out if accumulate]
+  EPI_PARTIAL = 4,  // ws[split](f32) = acc   (split-K partial, reduced by splitk_reduce)
+};
+
+struct GemmArgs {
+  int M, N, K;
+  int epi;
+  int splits;        // split-K factor (>= 1)
+  void* out;
+  long ldo;
+  const bf16* bias;  // [N] or nullptr
+  const bf16* resid;
+  long ldr;
+  bf16* aux;
+  long ldx;
+  float alpha;
+  int accumulate;
+};
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kThreads = 192;
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int A_BYTES = kBM * kBK * 2;
+  static constexpr int B_BYTES = BN * kBK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+__device__ __forceinline__ void tile_coords(int t, int mt, int nt, int& mi, int& ni) {
+  // Group 16 M-tiles together so CTAs running concurrently share B (and A) tiles in L2.
+  const int G = 16;
+  const int per_group = G * nt;
+  const int g = t / per_group;
+  const int first = g * G;
+  const int gm = min(G, mt - first);
+  const int r = t - g * per_group;
+  mi = first + r % gm;
+  ni = r / gm;
+}
+
+__device__ __forceinline__ void store_bf16x8(bf16* dst, const float* v) {
+  uint4 u;
+  u.x = pack_bf16x2(v[0], v[1]);
+  u.y = pack_bf16x2(v[2], v[3]);
+  u.z = pack_bf16x2(v[4], v[5]);
+  u.w = pack_bf16x2(v[6], v[7]);
+  *reinterpret_cast<uint4*>(dst) = u;
+}
+
+__device__ __forceinline__ void load_bf16x8(const bf16* src, float* v) {
+  uint4 u = *reinterpret_cast<const uint4*>(src);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+// Apply the epilogue to 8 consecutive columns [col, col+8) of one row.
+__device__ __forceinline__ void epi8(const GemmArgs& a, int row, int col, float* v, int split) {
+  const bool full = (col + 8 <= a.N);
+  switch (a.epi) {
+    case EPI_BF16: {
+      float b[8], r[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] *= a.alpha;
+      if (full) {
+        if (a.bias) {
+          load_bf16x8(a.bias + col, b);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[j] += b[j];
+        }
+        if (a.resid) {
+          load_bf16x8(a.resid + (long)row * a.ldr + col, r);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[j] += r[j];
+        }
+        store_bf16x8(reinterpret_cast<bf16*>(a.out) + (long)row * a.ldo + col, v);
+      } else {
+        for (int j = 0; j < 8 && col + j < a.N; ++j) {
+          float x = v[j];
+          if (a.bias) x += bf2f(a.bias[col + j]);
+          if (a.resid) x += bf2f(a.resid[(long)row * a.ldr + col + j]);
+          reinterpret_cast<bf16*>(a.out)[(long)row * a.ldo + col + j] = f2bf(x);
+        }
+      }
+      break;
+    }
+    case EPI_GELU: {
+      float b[8];
+      if (full) {
+        if (a.bias) {
+          load_bf16x8(a.bias + col, b);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[j] += b[j];
+        }
+        // round the pre-activation to bf16 first: backward sees exactly this value
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = bf2f(f2bf(v[j]));
+        store_bf16x8(a.aux + (long)row * a.ldx + col, v);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = gelu_tanh(v[j]);
+        store_bf16x8(reinterpret_cast<bf16*>(a.out) + (long)row * a.ldo + col, v);
+      } else {
+        for (int j = 0; j < 8 && col + j < a.N; ++j) {
+          float x = v[j] + (a.bias ? bf2f(a.bias[col + j]) : 0.f);
+          bf16 xb = f2bf(x);
+          a.aux[(long)row * a.ldx + col + j] = xb;
+          reinterpret_cast<bf16*>(a.out)[(long)row * a.ldo + col + j] = f2bf(gelu_tanh(bf2f(xb)));
+        }
+      }
+      break;
+    }
+    case EPI_DGELU: {
+      float h[8];
+      if (full) {
+        load_bf16x8(a.aux + (long)row * a.ldx + col, h);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] *= gelu_tanh_grad(h[j]);
+        store_bf16x8(reinterpret_cast<bf16*>(a.out) + (long)row * a.ldo + col, v);
+      } else {
+        for (int j = 0; j < 8 && col + j < a.N; ++j) {
+          float g = gelu_tanh_grad(bf2f(a.aux[(long)row * a.ldx + col + j]));
+          reinterpret_cast<bf16*>(a.out)[(long)row * a.ldo + col + j] = f2bf(v[j] * g);
+        }
+      }
+      break;
+    }
+    case EPI_F32: {
+      float* o = reinterpret_cast<float*>(a.out) + (long)row * a.ldo + col;
+      if (full) {
+        float4* o4 = reinterpret_cast<float4*>(o);
+        float4 x0 = make_float4(v[0] * a.alpha, v[1] * a.alpha, v[2] * a.alpha, v[3] * a.alpha);
+        float4 x1 = make_float4(v[4] * a.alpha, v[5] * a.alpha, v[6] * a.alpha, v[7] * a.alpha);
+        if (a.accumulate) {
+          float4 p0 = o4[0], p1 = o4[1];
+          x0.x += p0.x; x0.y += p0.y; x0.z += p0.z; x0.w += p0.w;
+          x1.x += p1.x; x1.y += p1.y; x1.z += p1.z; x1.w += p1.w;
+        }
+        o4[0] = x0;
+        o4[1] = x1;
+      } else {
+        for (int j = 0; j < 8 && col + j < a.N; ++j) o[j] = (a.accumulate ? o[j] : 0.f) + v[j] * a.alpha;
+      }
+      break;
+    }
+    case EPI_PARTIAL: {
+      float* o = reinterpret_cast<float*>(a.out) + (long)split * a.M * a.N + (long)row * a.N + col;
+      if (full && (a.N % 4 == 0)) {
+        reinterpret_cast<float4*>(o)[0] = make_float4(v[0], v[1], v[2], v[3]);
+        reinterpret_cast<float4*>(o)[1] = make_float4(v[4], v[5], v[6], v[7]);
+      } else {
+        for (int j = 0; j < 8 && col + j < a.N; ++j) o[j] = v[j];
+      }
+      break;
+    }
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs args) {
+  using Cfg = GemmCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + Cfg::STAGES * Cfg::STAGE_BYTES);
+  uint64_t* empty_bar = full_bar + Cfg::STAGES;
+  uint64_t* tfull_bar = empty_bar + Cfg::STAGES;  // [2]
+  uint64_t* tempty_bar = tfull_bar + 2;           // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Cfg::STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull_bar[b], 1);
+      mbar_init(&tempty_bar[b], 4);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int M = args.M, N = args.N, K = args.K;
+  const int mt = (M + kBM - 1) / kBM;
+  const int nt = (N + BN - 1) / BN;
+  const int kb_total = (K + kBK - 1) / kBK;
+  const int splits = args.splits;
+  const int units = mt * nt * splits;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ TMA producer
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const int t = u / splits, sp = u % splits;
+        int mi, ni;
+        tile_coords(t, mt, nt, mi, ni);
+        const int m0 = mi * kBM, n0 = ni * BN;
+        const int kb0 = (int)((long)kb_total * sp / splits), kb1 = (int)((long)kb_total * (sp + 1) / splits);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag)) { ok = false; break; }
+          uint8_t* sA = smem + stage * Cfg::STAGE_BYTES;
+          uint8_t* sB = sA + Cfg::A_BYTES;
+          mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
+          const int k0 = kb * kBK;
+          if (!A_MN) {
+            tma_load_2d(&tmA, sA, &full_bar[stage], k0, m0);
+          } else {
+#pragma unroll
+            for (int c = 0; c < kBM / 64; ++c) tma_load_2d(&tmA, sA + c * 8192, &full_bar[stage], m0 + c * 64, k0);
+          }
+          if (!B_MN) {
+            tma_load_2d(&tmB, sB, &full_bar[stage], k0, n0);
+          } else {
+#pragma unroll
+            for (int c = 0; c < BN / 64; ++c) tma_load_2d(&tmB, sB + c * 8192, &full_bar[stage], n0 + c * 64, k0);
+          }
+          if (++stage == Cfg::STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ MMA issuer
+      constexpr uint32_t idesc = make_idesc_bf16(kBM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int ab = 0;
+      uint32_t aphase = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const int sp = u % splits;
+        const int kb0 = (int)((long)kb_total * sp / splits), kb1 = (int)((long)kb_total * (sp + 1) / splits);
+        if (!mbar_wait(&tempty_bar[ab], aphase ^ 1, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(ab * BN);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t aBase = smem_u32(smem + stage * Cfg::STAGE_BYTES);
+          const uint32_t bBase = aBase + Cfg::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            // K-major: step 16 elements (32 B) inside the 128 B swizzle row.
+            // MN-major: step 16 rows (2 KB) of the K dimension.
+            const uint64_t ad = A_MN ? make_sw128_desc(aBase + kk * 2048, 8192, 1024)
+                                     : make_sw128_desc(aBase + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? make_sw128_desc(bBase + kk * 2048, 8192, 1024)
+                                     : make_sw128_desc(bBase + kk * 32, 16, 1024);
+            tc_mma_f16(d_tmem, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(&empty_bar[stage]);
+          if (++stage == Cfg::STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        tc_commit(&tfull_bar[ab]);
+        if (++ab == 2) { ab = 0; aphase ^= 1; }
+      }
+    }
+  } else {
+    // -------------------------------------------------------------- epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int ab = 0;
+    uint32_t aphase = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+      const int t = u / splits, sp = u % splits;
+      int mi, ni;
+      tile_coords(t, mt, nt, mi, ni);
+      const int m0 = mi * kBM, n0 = ni * BN;
+      if (!mbar_wait(&tfull_bar[ab], aphase, abort_flag)) break;
+      tc_fence_after();
+      const int row = m0 + q * 32 + lane;
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        if (n0 + c >= N) break;  // warp-uniform
+        float v[32];
+        tmem_ld32(tbase + c, v);
+        if (row < M) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            if (n0 + c + j < N) epi8(args, row, n0 + c + j, v + j, sp);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty_bar[ab]);
+      if (++ab == 2) { ab = 0; aphase ^= 1; }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+// Deterministic split-K reduction: out = alpha * sum_{s=0..S-1} ws[s] (+ out).
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int S, long MN, int N, float* out_f32,
+                                     bf16* out_bf16, long ldo, float alpha, int accumulate) {
+  long i = ((long)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (i >= MN) return;
+  float4 acc = *reinterpret_cast<const float4*>(ws + i);
+  for (int s = 1; s < S; ++s) {
+    float4 p = *reinterpret_cast<const float4*>(ws + (long)s * MN + i);
+    acc.x += p.x; acc.y += p.y; acc.z += p.z; acc.w += p.w;
+  }
+  const long r = i / N, c = i % N;  // N % 4 == 0 is required by the host
+  if (out_f32) {
+    float4* o = reinterpret_cast<float4*>(out_f32 + r * ldo + c);
+    float4 x = make_float4(acc.x * alpha, acc.y * alpha, acc.z * alpha, acc.w * alpha);
+    if (accumulate) {
+      float4 p = *o;
+      x.x += p.x; x.y += p.y; x.z += p.z; x.w += p.w;
+    }
+    *o = x;
+  } else {
+    bf16* o = out_bf16 + r * ldo + c;
+    o[0] = f2bf(acc.x * alpha); o[1] = f2bf(acc.y * alpha); o[2] = f2bf(acc.z * alpha); o[3] = f2bf(acc.w * alpha);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    TORCH_CHECK(e == cudaSuccess && q == cudaDriverEntryPointSuccess && p, "cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major matrix [rows, cols] with row stride ld (elements).
+static CUtensorMap make_map(const void* base, long rows, long cols, long ld, int box_cols, int box_rows) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = get_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with code ", (int)r);
+  return m;
+}
+
+static int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+template <int BN, bool A_MN, bool B_MN>
+static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, cudaStream_t st) {
+  using Cfg = GemmCfg<BN>;
+  static bool attr_set = false;
+  auto kern = gemm_tc_kernel<BN, A_MN, B_MN>;
+  if (!attr_set) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+    attr_set = true;
+  }
+  const int mt = (a.M + kBM - 1) / kBM, nt = (a.N + BN - 1) / BN;
+  const int units = mt * nt * a.splits;
+  const int grid = std::min(units, num_sms());
+  kern<<<grid, kThreads, Cfg::SMEM_BYTES, st>>>(ta, tb, a);
+  count_launch();
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Picks the tile width and split-K factor: prefer BN=256 (fewer shared-memory
+// bytes per FLOP); fall back to BN=128 and then split K until the persistent grid
+// covers the SMs.
+static void choose_tiling(int M, int N, int K, int& bn, int& splits) {
+  const int sms = num_sms();
+  const int mt = (M + kBM - 1) / kBM;
+  const int t256 = mt * ((N + 255) / 256), t128 = mt * ((N + 127) / 128);
+  if (t256 >= sms || N <= 128) {
+    bn = (N <= 128) ? 128 : 256;
+  } else {
+    bn = 128;
+  }
+  const int tiles = (bn == 256) ? t256 : t128;
+  splits = 1;
+  const int kb = (K + kBK - 1) / kBK;
+  while (tiles * splits * 2 <= sms + sms / 4 && kb / (splits * 2) >= 4) splits *= 2;
+}
+
+// a: stored [M,K] (a_trans=false) or [K,M] (a_trans=true); b: stored [K,N] (b_trans=false) or [N,K] (b_trans=true).
+void gemm(torch::Tensor a, bool a_trans, torch::Tensor b, bool b_trans, torch::Tensor out, int64_t epi,
+          c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> resid, c10::optional<torch::Tensor> aux,
+          double alpha, bool accumulate, int64_t force_bn, int64_t force_splits,
+          c10::optional<torch::Tensor> workspace) {
+  TORCH_CHECK(a.is_cuda() && b.is_cuda() && out.is_cuda(), "gemm: CUDA tensors expected");
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm: bf16 operands expected");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && out.dim() == 2, "gemm: 2-D tensors expected");
+  TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && out.stride(1) == 1, "gemm: rows must be contiguous");
+  const long M = a_trans ? a.size(1) : a.size(0);
+  const long K = a_trans ? a.size(0) : a.size(1);
+  const long Kb = b_trans ? b.size(1) : b.size(0);
+  const long N = b_trans ? b.size(0) : b.size(1);
+  TORCH_CHECK(K == Kb, "gemm: inner dimensions differ (", K, " vs ", Kb, ")");
+  TORCH_CHECK(out.size(0) == M && out.size(1) == N, "gemm: output shape mismatch");
+  TORCH_CHECK(M > 0 && N > 0 && K > 0, "gemm: empty problem");
+  TORCH_CHECK(a.stride(0) % 8 == 0 && b.stride(0) % 8 == 0, "gemm: leading dimensions must be multiples of 8");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(a.data_ptr()) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(b.data_ptr()) & 15) == 0,
+              "gemm: operands must be 16-byte aligned");
+  TORCH_CHECK(N % 8 == 0 && out.stride(0) % 8 == 0 && (reinterpret_cast<uintptr_t>(out.data_ptr()) & 15) == 0,
+              "gemm: output columns / leading dimension must be multiples of 8 and 16-byte aligned");
+  const bool f32_out = (epi == EPI_F32);
+  TORCH_CHECK(out.scalar_type() == (f32_out ? at::kFloat : at::kBFloat16), "gemm: wrong output dtype for epilogue");
+  c10::cuda::CUDAGuard guard(a.device());
+
+  GemmArgs args{};
+  args.M = (int)M;
+  args.N = (int)N;
+  args.K = (int)K;
+  args.epi = (int)epi;
+  args.out = out.data_ptr();
+  args.ldo = out.stride(0);
+  args.alpha = (float)alpha;
+  args.accumulate = accumulate ? 1 : 0;
+  if (bias && bias->defined()) {
+    TORCH_CHECK(bias->scalar_type() == at::kBFloat16 && bias->numel() == N && bias->is_contiguous(), "gemm: bias");
+    args.bias = reinterpret_cast<const bf16*>(bias->data_ptr());
+  }
+  if (resid && resid->defined()) {
+    TORCH_CHECK(resid->scalar_type() == at::kBFloat16 && resid->size(0) == M && resid->size(1) == N &&
+                    resid->stride(1) == 1 && resid->stride(0) % 8 == 0,
+                "gemm: resid");
+    args.resid = reinterpret_cast<const bf16*>(resid->data_ptr());
+    args.ldr = resid->stride(0);
+  }
+  if (aux && aux->defined()) {
+    TORCH_CHECK(aux->scalar_type() == at::kBFloat16 && aux->size(0) == M && aux->size(1) == N &&
+                    aux->stride(1) == 1 && aux->stride(0) % 8 == 0,
+                "gemm: aux");
+    args.aux = reinterpret_cast<bf16*>(aux->data_ptr());
+    args.ldx = aux->stride(0);
+  }
+  TORCH_CHECK(epi != EPI_GELU && epi != EPI_DGELU ? true : args.aux != nullptr, "gemm: gelu epilogues need aux");
+
+  int bn, splits;
+  choose_tiling((int)M, (int)N, (int)K, bn, splits);
+  if (force_bn > 0) bn = (int)force_bn;
+  if (force_splits > 0) splits = (int)force_splits;
+  TORCH_CHECK(bn == 128 || bn == 256, "gemm: BN must be 128 or 256");
+  // split-K is only wired for the fp32 / bf16 plain epilogues without bias or residual
+  if (splits > 1 && !((epi == EPI_F32) || (epi == EPI_BF16 && !args.bias && !args.resid))) splits = 1;
+
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  // A map: K-major [M rows, K cols] box {64, 128}; MN-major [K rows, M cols] box {64, 64}
+  CUtensorMap ta = a_trans ? make_map(a.data_ptr(), K, M, a.stride(0), 64, 64)
+                           : make_map(a.data_ptr(), M, K, a.stride(0), 64, kBM);
+  CUtensorMap tb = b_trans ? make_map(b.data_ptr(), N, K, b.stride(0), 64, bn)
+                           : make_map(b.data_ptr(), K, N, b.stride(0), 64, 64);
+
+  GemmArgs run = args;
+  torch::Tensor ws;
+  if (splits > 1) {
+    const long need = (long)splits * M * N;
+    if (workspace && workspace->defined() && workspace->numel() >= need) {
+      ws = *workspace;
+    } else {
+      ws = torch::empty({need}, a.options().dtype(at::kFloat));
+    }
+    run.epi = EPI_PARTIAL;
+    run.out = ws.data_ptr();
+    run.splits = splits;
+  } else {
+    run.splits = 1;
+  }
+
+#define DTB_GEMM_DISPATCH(BNV)                                           \
+  if (!a_trans && !b_trans) launch_gemm<BNV, false, true>(ta, tb, run, st);  \
+  else if (!a_trans && b_trans) launch_gemm<BNV, false, false>(ta, tb, run, st); \
+  else if (a_trans && !b_trans) launch_gemm<BNV, true, true>(ta, tb, run, st);   \
+  else launch_gemm<BNV, true, false>(ta, tb, run, st);
+  if (bn == 256) {
+    DTB_GEMM_DISPATCH(256)
+  } else {
+    DTB_GEMM_DISPATCH(128)
+  }
+#undef DTB_GEMM_DISPATCH
+
+  if (splits > 1) {
+    const long MN = M * N;
+    const int threads = 256;
+    const long blocks = (MN / 4 + threads - 1) / threads;
+    splitk_reduce_kernel<<<(unsigned)blocks, threads, 0, st>>>(
+        reinterpret_cast<const float*>(ws.data_ptr()), splits, MN, (int)N,
+        f32_out ? reinterpret_cast<float*>(out.data_ptr()) : nullptr,
+        f32_out ? nullptr : reinterpret_cast<bf16*>(out.data_ptr()), out.stride(0), (float)alpha,
+        accumulate ? 1 : 0);
+    count_launch();
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+}
+
+// Returns the (BN, splits) the heuristic would pick, for tests and tuning.
+std::vector<int64_t> gemm_tiling(int64_t M, int64_t N, int64_t K) {
+  int bn, s;
+  choose_tiling((int)M, (int)N, (int)K, bn, s);
+  return {bn, s};
+}
+
+DTB_DEFINE_STATUS_READER(status_gemm)
+
+}  // namespace dtb

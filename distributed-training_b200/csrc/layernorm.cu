@@ -1,0 +1,336 @@
+// LayerNorm forward/backward and the deterministic column-sum used for bias grads.
+//
+// Mirrors dtrain/autograd.py:207-223 (layer_norm): population variance of the
+// centred input, rstd = 1/sqrt(var + eps), y = xhat*w + b; backward
+//   dx = rstd * (g*w - mean(g*w) - xhat * mean(g*w*xhat))
+// plus row sums for dw and db.  Here x/y/dy/dx are bf16 [rows, C], statistics and
+// parameter gradients are fp32.  The backward also adds the residual-stream
+// gradient (dresid) so the residual add costs no extra pass.
+//
+// Determinism: dw/db are reduced in two fixed-order stages (per-block partials in
+// a workspace, then a column-wise sum over blocks in block order), never with
+// float atomics, so repeated runs give identical bits.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+
+namespace dtb {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ void ld8(const bf16* p, float* v) {
+  uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+__device__ __forceinline__ void st8(bf16* p, const float* v) {
+  uint4 u;
+  u.x = pack_bf16x2(v[0], v[1]);
+  u.y = pack_bf16x2(v[2], v[3]);
+  u.z = pack_bf16x2(v[4], v[5]);
+  u.w = pack_bf16x2(v[6], v[7]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
+// One warp per row; lane l owns 8-element chunks l, l+32, l+64, ... (NCH chunks).
+template <int NCH>
+__global__ void ln_fwd_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w, const bf16* __restrict__ b,
+                              bf16* __restrict__ y, float* __restrict__ mean_out, float* __restrict__ rstd_out,
+                              int rows, int C, float eps) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const bf16* xr = x + (long)warp * C;
+  float v[NCH][8];
+  float s = 0.f;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int col = (c * 32 + lane) * 8;
+    if (col < C) {
+      ld8(xr + col, v[c]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s += v[c][j];
+    }
+  }
+  const float mu = warp_sum(s) / C;
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int col = (c * 32 + lane) * 8;
+    if (col < C) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float d = v[c][j] - mu;
+        ss += d * d;
+      }
+    }
+  }
+  const float var = warp_sum(ss) / C;
+  const float rs = rsqrtf(var + eps);
+  bf16* yr = y + (long)warp * C;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int col = (c * 32 + lane) * 8;
+    if (col < C) {
+      float wv[8], bv[8], o[8];
+      ld8(w + col, wv);
+      ld8(b + col, bv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = (v[c][j] - mu) * rs * wv[j] + bv[j];
+      st8(yr + col, o);
+    }
+  }
+  if (lane == 0) {
+    mean_out[warp] = mu;
+    rstd_out[warp] = rs;
+  }
+}
+
+constexpr int kLnBwdWarps = 8;
+constexpr int kLnBwdRowsPerBlock = 64;
+
+// Block b handles rows [b*64, b*64+64); warp k handles rows b*64 + k, +8, ...
+// Per-block dw/db partials go to part_w/part_b [gridDim.x, C].
+template <int NCH>
+__global__ void __launch_bounds__(kLnBwdWarps * 32)
+    ln_bwd_kernel(const bf16* __restrict__ dy, const bf16* __restrict__ x, const bf16* __restrict__ w,
+                  const float* __restrict__ mean, const float* __restrict__ rstd, const bf16* __restrict__ dresid,
+                  bf16* __restrict__ dx, float* __restrict__ part_w, float* __restrict__ part_b, int rows, int C) {
+  extern __shared__ float sm[];  // [kLnBwdWarps][2][C]
+  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float aw[NCH][8], ab[NCH][8], wv[NCH][8];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int col = (c * 32 + lane) * 8;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) aw[c][j] = ab[c][j] = 0.f;
+    if (col < C) ld8(w + col, wv[c]);
+  }
+  const int r0 = blockIdx.x * kLnBwdRowsPerBlock;
+  for (int rr = wid; rr < kLnBwdRowsPerBlock; rr += kLnBwdWarps) {
+    const int r = r0 + rr;
+    if (r >= rows) break;
+    const float mu = mean[r], rs = rstd[r];
+    float g[NCH][8], xh[NCH][8];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int col = (c * 32 + lane) * 8;
+      if (col < C) {
+        float xv[8];
+        ld8(dy + (long)r * C + col, g[c]);
+        ld8(x + (long)r * C + col, xv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          xh[c][j] = (xv[j] - mu) * rs;
+          const float gw = g[c][j] * wv[c][j];
+          s1 += gw;
+          s2 += gw * xh[c][j];
+          aw[c][j] += g[c][j] * xh[c][j];
+          ab[c][j] += g[c][j];
+        }
+      }
+    }
+    const float m1 = warp_sum(s1) / C, m2 = warp_sum(s2) / C;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int col = (c * 32 + lane) * 8;
+      if (col < C) {
+        float o[8], rv[8];
+        if (dresid) ld8(dresid + (long)r * C + col, rv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          o[j] = rs * (g[c][j] * wv[c][j] - m1 - xh[c][j] * m2);
+          if (dresid) o[j] += rv[j];
+        }
+        st8(dx + (long)r * C + col, o);
+      }
+    }
+  }
+  // combine the warps of this block in warp order
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int col = (c * 32 + lane) * 8;
+    if (col < C) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        sm[(wid * 2 + 0) * C + col + j] = aw[c][j];
+        sm[(wid * 2 + 1) * C + col + j] = ab[c][j];
+      }
+    }
+  }
+  __syncthreads();
+  for (int col = threadIdx.x; col < C; col += blockDim.x) {
+    float sw = 0.f, sb = 0.f;
+    for (int k = 0; k < kLnBwdWarps; ++k) {
+      sw += sm[(k * 2 + 0) * C + col];
+      sb += sm[(k * 2 + 1) * C + col];
+    }
+    part_w[(long)blockIdx.x * C + col] = sw;
+    part_b[(long)blockIdx.x * C + col] = sb;
+  }
+}
+
+// out[col] = (accumulate ? out[col] : 0) + sum_{k=0..nparts-1} part[k, col]  (fixed order)
+__global__ void colsum_partials_kernel(const float* __restrict__ part, int nparts, int C, float* __restrict__ out,
+                                       int accumulate) {
+  const int col = blockIdx.x * blockDim.x + threadIdx.x;
+  if (col >= C) return;
+  float s = 0.f;
+  for (int k = 0; k < nparts; ++k) s += part[(long)k * C + col];
+  out[col] = accumulate ? out[col] + s : s;
+}
+
+// Bias gradient stage 1: partial column sums of a bf16 [rows, N] matrix over
+// blocks of kColRows rows.  Thread layout: 32 column groups of 8 x 8 row lanes.
+constexpr int kColRows = 128;
+__global__ void __launch_bounds__(256)
+    colsum_bf16_stage1(const bf16* __restrict__ g, long ld, int rows, int N, float* __restrict__ part) {
+  __shared__ float sm[8][256 + 8];
+  const int cg = threadIdx.x & 31, rl = threadIdx.x >> 5;
+  const int col = blockIdx.x * 256 + cg * 8;
+  const int r0 = blockIdx.y * kColRows;
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (col < N) {
+    for (int r = r0 + rl; r < min(r0 + kColRows, rows); r += 8) {
+      float v[8];
+      ld8(g + (long)r * ld + col, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] += v[j];
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) sm[rl][cg * 8 + j] = acc[j];
+  __syncthreads();
+  const int c = threadIdx.x;
+  if (blockIdx.x * 256 + c < N) {
+    float s = 0.f;
+    for (int k = 0; k < 8; ++k) s += sm[k][c];
+    part[(long)blockIdx.y * N + blockIdx.x * 256 + c] = s;
+  }
+}
+
+// ------------------------------------------------------------------ host
+static int ln_chunks(int C) {
+  TORCH_CHECK(C % 8 == 0 && C <= 2048, "layernorm: C must be a multiple of 8 and <= 2048, got ", C);
+  return (C + 255) / 256;
+}
+
+std::vector<torch::Tensor> layernorm_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor b, double eps) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous(), "layernorm_fwd: x");
+  TORCH_CHECK(w.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "layernorm_fwd: w/b bf16");
+  c10::cuda::CUDAGuard guard(x.device());
+  const int C = (int)x.size(-1);
+  const int rows = (int)(x.numel() / C);
+  auto y = torch::empty_like(x);
+  auto mean = torch::empty({rows}, x.options().dtype(at::kFloat));
+  auto rstd = torch::empty({rows}, x.options().dtype(at::kFloat));
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  const int threads = 256;
+  const int blocks = (rows * 32 + threads - 1) / threads;
+  const int nch = ln_chunks(C);
+  auto* xp = reinterpret_cast<const bf16*>(x.data_ptr());
+  auto* wp = reinterpret_cast<const bf16*>(w.data_ptr());
+  auto* bp = reinterpret_cast<const bf16*>(b.data_ptr());
+  auto* yp = reinterpret_cast<bf16*>(y.data_ptr());
+#define LNF(NC) ln_fwd_kernel<NC><<<blocks, threads, 0, st>>>(xp, wp, bp, yp, mean.data_ptr<float>(), rstd.data_ptr<float>(), rows, C, (float)eps)
+  switch (nch) {
+    case 1: LNF(1); break;
+    case 2: LNF(2); break;
+    case 3: LNF(3); break;
+    case 4: LNF(4); break;
+    case 5: case 6: LNF(6); break;
+    case 7: case 8: LNF(8); break;
+    default: TORCH_CHECK(false, "layernorm: C too large");
+  }
+#undef LNF
+  count_launch();
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {y, mean, rstd};
+}
+
+// Returns dx; writes dw, db (fp32 [C]) — accumulating when requested.
+torch::Tensor layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor mean,
+                            torch::Tensor rstd, c10::optional<torch::Tensor> dresid, torch::Tensor dw,
+                            torch::Tensor db, bool accumulate) {
+  TORCH_CHECK(dy.is_contiguous() && x.is_contiguous() && dy.scalar_type() == at::kBFloat16, "layernorm_bwd: dy/x");
+  TORCH_CHECK(dw.scalar_type() == at::kFloat && db.scalar_type() == at::kFloat, "layernorm_bwd: dw/db fp32");
+  c10::cuda::CUDAGuard guard(x.device());
+  const int C = (int)x.size(-1);
+  const int rows = (int)(x.numel() / C);
+  auto dx = torch::empty_like(x);
+  const int nblk = (rows + kLnBwdRowsPerBlock - 1) / kLnBwdRowsPerBlock;
+  auto part = torch::empty({2, nblk, C}, x.options().dtype(at::kFloat));
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  const bf16* dr = nullptr;
+  if (dresid && dresid->defined()) {
+    TORCH_CHECK(dresid->is_contiguous() && dresid->numel() == x.numel(), "layernorm_bwd: dresid");
+    dr = reinterpret_cast<const bf16*>(dresid->data_ptr());
+  }
+  const int nch = ln_chunks(C);
+  const size_t smem = (size_t)kLnBwdWarps * 2 * C * sizeof(float);
+  auto* dyp = reinterpret_cast<const bf16*>(dy.data_ptr());
+  auto* xp = reinterpret_cast<const bf16*>(x.data_ptr());
+  auto* wp = reinterpret_cast<const bf16*>(w.data_ptr());
+  auto* dxp = reinterpret_cast<bf16*>(dx.data_ptr());
+  float* pw = part.data_ptr<float>();
+  float* pb = pw + (long)nblk * C;
+#define LNB(NC)                                                                                          \
+  {                                                                                                      \
+    auto k = ln_bwd_kernel<NC>;                                                                          \
+    if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+    k<<<nblk, kLnBwdWarps * 32, smem, st>>>(dyp, xp, wp, mean.data_ptr<float>(), rstd.data_ptr<float>(), dr, dxp, pw, pb, rows, C); \
+  }
+  switch (nch) {
+    case 1: LNB(1); break;
+    case 2: LNB(2); break;
+    case 3: LNB(3); break;
+    case 4: LNB(4); break;
+    case 5: case 6: LNB(6); break;
+    case 7: case 8: LNB(8); break;
+    default: TORCH_CHECK(false, "layernorm_bwd: C too large");
+  }
+#undef LNB
+  count_launch();
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  colsum_partials_kernel<<<(C + 255) / 256, 256, 0, st>>>(pw, nblk, C, dw.data_ptr<float>(), accumulate ? 1 : 0);
+  colsum_partials_kernel<<<(C + 255) / 256, 256, 0, st>>>(pb, nblk, C, db.data_ptr<float>(), accumulate ? 1 : 0);
+  count_launch(2);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return dx;
+}
+
+// db[N] (+)= column sums of g [rows, N] (bf16), deterministic.
+void bias_grad(torch::Tensor g, torch::Tensor db, bool accumulate) {
+  TORCH_CHECK(g.dim() == 2 && g.stride(1) == 1 && g.scalar_type() == at::kBFloat16, "bias_grad: g");
+  TORCH_CHECK(db.scalar_type() == at::kFloat && db.is_contiguous(), "bias_grad: db");
+  c10::cuda::CUDAGuard guard(g.device());
+  const int rows = (int)g.size(0), N = (int)g.size(1);
+  TORCH_CHECK(N % 8 == 0 && g.stride(0) % 8 == 0, "bias_grad: N must be a multiple of 8");
+  const int rb = (rows + kColRows - 1) / kColRows;
+  auto part = torch::empty({rb, N}, g.options().dtype(at::kFloat));
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  dim3 grid((N + 255) / 256, rb);
+  colsum_bf16_stage1<<<grid, 256, 0, st>>>(reinterpret_cast<const bf16*>(g.data_ptr()), g.stride(0), rows, N,
+                                           part.data_ptr<float>());
+  colsum_partials_kernel<<<(N + 255) / 256, 256, 0, st>>>(part.data_ptr<float>(), rb, N, db.data_ptr<float>(),
+                                                          accumulate ? 1 : 0);
+  count_launch(2);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+DTB_DEFINE_STATUS_READER(status_layernorm)
+
+}  // namespace dtb

@@ -1,0 +1,105 @@
+"""Thin Python wrappers over the sm_100a kernels in ``csrc/``.
+
+Each function takes and returns torch tensors on a CUDA device and calls exactly
+one entry point of the extension; shapes and dtypes are checked in C++.  These
+are the building blocks of the fused autograd functions in ``models/gpt.py`` and
+of the functional API in ``ops/functional.py``.
+"""
+from __future__ import annotations
+
+import torch
+
+from ._ext import lib
+
+# GEMM epilogues (csrc/gemm.cu: GemmEpi)
+EPI_BF16 = 0    # out(bf16) = alpha*acc [+ bias] [+ resid]
+EPI_GELU = 1    # aux(bf16) = acc + bias ; out(bf16) = gelu(aux)
+EPI_DGELU = 2   # out(bf16) = acc * gelu'(aux)
+EPI_F32 = 3     # out(f32)  = alpha*acc [+ out]
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, *, a_trans: bool = False,
+         b_trans: bool = False, epi: int = EPI_BF16, bias: torch.Tensor | None = None,
+         resid: torch.Tensor | None = None, aux: torch.Tensor | None = None, alpha: float = 1.0,
+         accumulate: bool = False, force_bn: int = 0, force_splits: int = 0) -> torch.Tensor:
+    """C = op(A) @ op(B) with a fused epilogue on the tcgen05 GEMM.
+
+    ``a`` is stored [M, K] (or [K, M] with ``a_trans``); ``b`` is stored [K, N]
+    (or [N, K] with ``b_trans``).  bf16 operands, fp32 accumulation.
+    """
+    M = a.shape[1] if a_trans else a.shape[0]
+    N = b.shape[0] if b_trans else b.shape[1]
+    if out is None:
+        dt = torch.float32 if epi == EPI_F32 else torch.bfloat16
+        out = torch.empty(M, N, dtype=dt, device=a.device)
+    lib().gemm(a, a_trans, b, b_trans, out, epi, bias, resid, aux, alpha, accumulate, force_bn, force_splits, None)
+    return out
+
+
+def layernorm_fwd(x: torch.Tensor, w16: torch.Tensor, b16: torch.Tensor, eps: float = 1e-5):
+    """Returns (y bf16, mean fp32 [rows], rstd fp32 [rows])."""
+    return lib().layernorm_fwd(x, w16, b16, eps)
+
+
+def layernorm_bwd(dy, x, w16, mean, rstd, dresid, dw, db, accumulate=False):
+    """dx (bf16) = LN backward + dresid; writes dw, db (fp32)."""
+    return lib().layernorm_bwd(dy, x, w16, mean, rstd, dresid, dw, db, accumulate)
+
+
+def bias_grad(g: torch.Tensor, db: torch.Tensor, accumulate: bool = False) -> None:
+    lib().bias_grad(g, db, accumulate)
+
+
+def embed_fwd(idx: torch.Tensor, tok16: torch.Tensor, pos16: torch.Tensor, bad: torch.Tensor) -> torch.Tensor:
+    return lib().embed_fwd(idx, tok16, pos16, bad)
+
+
+def embed_bwd(idx: torch.Tensor, dx: torch.Tensor, dtok: torch.Tensor, dpos: torch.Tensor,
+              accumulate: bool = False) -> None:
+    B, T = idx.shape
+    sorted_ids, perm = torch.sort(idx.reshape(-1), stable=True)
+    lib().embed_bwd(sorted_ids, perm, dx, dtok, dpos, B, T, accumulate)
+
+
+def xent_fwd(logits: torch.Tensor, targets: torch.Tensor):
+    """Returns (mean loss fp32 scalar, lse fp32 [rows])."""
+    return lib().xent_fwd(logits, targets.reshape(-1))
+
+
+def xent_bwd(logits: torch.Tensor, targets: torch.Tensor, lse: torch.Tensor, gscale: torch.Tensor) -> None:
+    """In place: logits <- (softmax - onehot) * gscale / rows."""
+    lib().xent_bwd(logits, targets.reshape(-1), lse, gscale.reshape(1).float())
+
+
+def attn_fwd(qkv: torch.Tensor, B: int, T: int, H: int, D: int):
+    """Returns (out [B*T, H*D] bf16, lse2 [B*H, T] fp32)."""
+    return lib().attn_fwd(qkv, B, T, H, D)
+
+
+def attn_bwd(qkv, out, dout, lse, B, T, H, D) -> torch.Tensor:
+    return lib().attn_bwd(qkv, out, dout, lse, B, T, H, D)
+
+
+def adamw_step(p, g, m, v, p16, lr, b1, b2, eps, wd, t, sq=None, max_norm=0.0) -> None:
+    lib().adamw_step(p, g, m, v, p16, lr, b1, b2, eps, wd, t, sq, max_norm)
+
+
+def grad_sqnorm(g: torch.Tensor, out: torch.Tensor | None = None, scale: float = 1.0) -> torch.Tensor:
+    if out is None:
+        out = torch.empty(1, dtype=torch.float64, device=g.device)
+    lib().grad_sqnorm(g, out, scale)
+    return out
+
+
+def cast_f32_bf16(x: torch.Tensor, y: torch.Tensor) -> None:
+    lib().cast_f32_bf16(x, y)
+
+
+def launch_count() -> int:
+    """Kernels launched through this extension so far (host-side counter)."""
+    return int(lib().launch_count())
+
+
+def device_status() -> int:
+    """First non-zero error code any kernel recorded (bounded-wait timeouts etc.); clears it."""
+    return int(lib().device_status())

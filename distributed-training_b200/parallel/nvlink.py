@@ -1,0 +1,344 @@
+"""GPU process group: collectives as sm_100a kernels over NVLink / NVSwitch peer memory.
+
+Same API as the host ``ProcessGroup`` (dtrain/comm.py:241-432): ``allreduce``,
+``reduce_scatter``, ``all_gather``, ``broadcast``, ``barrier``,
+``allreduce_async`` -> work handle, ``close``, ``rank``, ``world``, ``seq``.
+
+Memory model.  ``alloc(numel, dtype)`` is a collective: every rank allocates a
+buffer of the same size (cudaMalloc), exports an IPC handle, publishes it through
+the bootstrap ``exchange`` function and opens its peers' handles.  Collectives on
+tensors that live inside such a buffer run in place, reading and writing peer
+memory directly from the kernel (``csrc/comm.cu``); other CUDA tensors are staged
+through a symmetric scratch buffer.  DDP and ZeRO allocate their flat gradient,
+master and working-copy buffers here, so their collectives never copy.
+
+Ordering and failure.  Collectives are stream-ordered on the caller's current
+stream (``allreduce_async`` uses a dedicated comm stream and returns a handle
+whose ``wait()`` makes the current stream wait on it, like NCCL).  Every rank
+must issue the same collectives in the same order; each kernel synchronises with
+its peers through per-CTA epoch flags, and every wait gives up after ``timeout``
+seconds, writing an error code to a host-mapped status word.  ``check()`` turns a
+non-zero status into ``CommError``.
+"""
+from __future__ import annotations
+
+import os
+
+import torch
+
+from ..ops._ext import lib
+from ..utils.store import CommError
+from .comm import partition
+
+DT = {torch.float32: 0, torch.bfloat16: 1}
+ORDER_RANK, ORDER_CYCLIC = 0, 1
+ALGO_ONESHOT, ALGO_TWOSHOT = 0, 1
+_SIG_BYTES = 128 * 8 * 4  # [max CTAs][max ranks] uint32 flags
+_ONESHOT_MAX_BYTES = 1 << 20
+
+
+class SymmetricBuffer:
+    """One peer-mapped allocation: a local tensor view plus every rank's base pointer."""
+
+    def __init__(self, group: "NVLinkGroup", nbytes: int):
+        C = lib()
+        self.nbytes = int(nbytes)
+        ptr, handle = C.symm_alloc(max(self.nbytes, 256))
+        self.ptr = int(ptr)
+        handles = group._exchange(f"symm/{group._nalloc}", bytes(handle.numpy().tobytes()))
+        group._nalloc += 1
+        self.ptrs = []
+        self._opened = []
+        for r, h in enumerate(handles):
+            if r == group.rank:
+                self.ptrs.append(self.ptr)
+            else:
+                p = int(C.symm_open(torch.frombuffer(bytearray(h), dtype=torch.uint8)))
+                self.ptrs.append(p)
+                self._opened.append(p)
+        self.device = group.device
+
+    def tensor(self, numel: int, dtype: torch.dtype, byte_offset: int = 0) -> torch.Tensor:
+        assert byte_offset + numel * torch.tensor([], dtype=dtype).element_size() <= self.nbytes
+        return lib().tensor_from_ptr(self.ptr + byte_offset, [int(numel)], dtype, self.device.index)
+
+    def contains(self, t: torch.Tensor) -> int | None:
+        """Byte offset of ``t`` inside this buffer, or None."""
+        p = t.data_ptr()
+        end = p + t.numel() * t.element_size()
+        if self.ptr <= p and end <= self.ptr + self.nbytes:
+            return p - self.ptr
+        return None
+
+    def free(self):
+        C = lib()
+        for p in self._opened:
+            C.symm_close(p)
+        self._opened = []
+        if self.ptr:
+            C.symm_free(self.ptr)
+            self.ptr = 0
+
+
+class GPUWork:
+    """Handle of an asynchronous GPU collective (event on the comm stream)."""
+
+    def __init__(self, event: torch.cuda.Event, group: "NVLinkGroup"):
+        self.event, self.group = event, group
+
+    def wait(self):
+        """Make the current stream wait for the collective (no host synchronisation)."""
+        torch.cuda.current_stream().wait_event(self.event)
+
+    def synchronize(self):
+        self.event.synchronize()
+        self.group.check()
+
+    def is_completed(self) -> bool:
+        return self.event.query()
+
+
+class NVLinkGroup:
+    backend = "nvlink"
+
+    def __init__(self, rank: int, world: int, device, exchange, timeout: float = 60.0, blocks: int = 0):
+        """``exchange(key, payload: bytes) -> list[bytes]`` is the bootstrap all-gather
+        (over the rendezvous store or torch.distributed); it is used only at set-up."""
+        if world > int(lib().comm_max_ranks()):
+            raise ValueError(f"NVLinkGroup supports up to {lib().comm_max_ranks()} ranks per node")
+        self.rank, self.world = int(rank), int(world)
+        self.device = torch.device(device)
+        self.timeout = float(timeout)
+        self.blocks = int(blocks)
+        self._exchange_fn = exchange
+        self._nalloc = 0
+        self.seq = 0            # collectives issued
+        self.epoch = 1          # next device flag epoch (identical on every rank)
+        self.buffers: list[SymmetricBuffer] = []
+        with torch.cuda.device(self.device):
+            lib().comm_status_clear()
+            self._sig = self._new_buffer(_SIG_BYTES)
+            self.comm_stream = torch.cuda.Stream(device=self.device)
+        self._staging: SymmetricBuffer | None = None
+        self._sq_parts = None
+        self.barrier()
+        self.synchronize()
+
+    # ------------------------------------------------------------ plumbing
+    def _exchange(self, key: str, payload: bytes) -> list[bytes]:
+        return self._exchange_fn(key, payload)
+
+    def _new_buffer(self, nbytes: int) -> SymmetricBuffer:
+        b = SymmetricBuffer(self, nbytes)
+        self.buffers.append(b)
+        return b
+
+    def alloc(self, numel: int, dtype: torch.dtype = torch.float32) -> torch.Tensor:
+        """Collective: a zero-filled peer-mapped tensor (same size on every rank)."""
+        esz = torch.tensor([], dtype=dtype).element_size()
+        with torch.cuda.device(self.device):
+            buf = self._new_buffer(int(numel) * esz)
+        return buf.tensor(numel, dtype)
+
+    def _locate(self, t: torch.Tensor):
+        for b in self.buffers:
+            off = b.contains(t)
+            if off is not None:
+                return b, off
+        return None, None
+
+    @property
+    def _sigs(self):
+        return self._sig.ptrs
+
+    def _advance(self, used: int):
+        self.epoch += int(used)
+        self.seq += 1
+
+    def _stage(self, nbytes: int) -> SymmetricBuffer:
+        if self._staging is None or self._staging.nbytes < nbytes:
+            # growth is collective: every rank stages the same sizes in the same order
+            self.synchronize()
+            self._staging = self._new_buffer(max(nbytes, 1 << 20))
+        return self._staging
+
+    def check(self):
+        """Raise CommError if any collective kernel timed out waiting for a peer."""
+        code = int(lib().comm_status())
+        if code:
+            raise CommError(f"NVLink collective failed on rank {self.rank} (device status {code}): "
+                            "a peer did not arrive within the timeout")
+
+    def synchronize(self):
+        torch.cuda.synchronize(self.device)
+        self.check()
+
+    # ---------------------------------------------------------- collectives
+    def _order(self, algo: str) -> int:
+        return ORDER_CYCLIC if algo == "ring" else ORDER_RANK
+
+    def allreduce(self, t: torch.Tensor, algo: str = "ring", scale: float = 1.0, method: str = "auto"):
+        """In-place sum (times ``scale``) over ranks.
+
+        ``algo`` selects the summation order: "ring" (dtrain ring order) or
+        "direct" (rank order).  ``method`` selects the data movement: "oneshot"
+        (every rank reduces everything: latency-optimal), "twoshot" (reduce-scatter
+        + all-gather: bandwidth-optimal) or "auto" (one-shot up to 1 MiB).
+        """
+        if self.world == 1:
+            if scale != 1.0:
+                t.mul_(scale)
+            return t
+        if not t.is_contiguous():
+            raise ValueError("allreduce needs a contiguous tensor")
+        if t.dtype not in DT:
+            raise TypeError("NVLink allreduce supports float32 and bfloat16")
+        n = t.numel()
+        nbytes = n * t.element_size()
+        if method == "auto":
+            method = "oneshot" if nbytes <= _ONESHOT_MAX_BYTES else "twoshot"
+        buf, off = self._locate(t)
+        staged = buf is None
+        # one-shot writes out of place: it needs scratch for the result (and for the
+        # input too when t is not peer-mapped); size the staging buffer once, up front
+        need = nbytes * ((2 if staged else 1) if method == "oneshot" else (1 if staged else 0))
+        stage = self._stage(need) if need else None
+        if staged:
+            buf, off = stage, 0
+            buf.tensor(n, t.dtype).copy_(t.reshape(-1))
+        C = lib()
+        if method == "oneshot":
+            if stage is buf and not staged:
+                raise RuntimeError("one-shot scratch aliases the input")
+            out = stage.tensor(n, t.dtype, nbytes if staged else 0)
+            used = C.allreduce(self._sigs, self.rank, self.epoch, buf.ptrs, off, n, DT[t.dtype], out.data_ptr(),
+                               DT[t.dtype], ALGO_ONESHOT, self._order(algo), scale, self.timeout, self.blocks)
+            t.reshape(-1).copy_(out)
+        else:
+            used = C.allreduce(self._sigs, self.rank, self.epoch, buf.ptrs, off, n, DT[t.dtype], 0, DT[t.dtype],
+                               ALGO_TWOSHOT, self._order(algo), scale, self.timeout, self.blocks)
+            if staged:
+                t.reshape(-1).copy_(buf.tensor(n, t.dtype))
+        self._advance(used)
+        return t
+
+    def reduce_scatter(self, flat: torch.Tensor, scale: float = 1.0, sq_parts: torch.Tensor | None = None):
+        """Sum over ranks (ring order); this rank's partition then holds the total.
+        Returns a view of it.  With ``sq_parts`` (fp64, symmetric) the kernel also
+        writes per-CTA sums of squares of the reduced partition."""
+        n = flat.numel()
+        b = partition(n, self.world)
+        if self.world > 1:
+            buf, off = self._locate(flat)
+            if buf is None:
+                raise ValueError("reduce_scatter needs a tensor allocated with NVLinkGroup.alloc")
+            sqp = sq_parts.data_ptr() if sq_parts is not None else 0
+            used = lib().reduce_scatter(self._sigs, self.rank, self.epoch, buf.ptrs, off, n, DT[flat.dtype], 0,
+                                        ORDER_CYCLIC, scale, sqp, self.timeout, self._rs_blocks())
+            self._advance(used)
+        elif scale != 1.0:
+            flat.mul_(scale)
+        return flat[b[self.rank]:b[self.rank + 1]]
+
+    def _rs_blocks(self) -> int:
+        return self.blocks or 32
+
+    def all_gather(self, flat: torch.Tensor):
+        if self.world > 1:
+            buf, off = self._locate(flat)
+            if buf is None:
+                raise ValueError("all_gather needs a tensor allocated with NVLinkGroup.alloc")
+            used = lib().all_gather(self._sigs, self.rank, self.epoch, buf.ptrs, off, flat.numel(), DT[flat.dtype],
+                                    self.timeout, self.blocks)
+            self._advance(used)
+        return flat
+
+    def broadcast(self, t: torch.Tensor, root: int = 0, cast_to: torch.Tensor | None = None):
+        """Copy root's ``t`` to every rank (optionally also casting fp32 -> bf16 into ``cast_to``)."""
+        if self.world == 1:
+            if cast_to is not None:
+                cast_to.copy_(t)
+            return t
+        buf, off = self._locate(t)
+        staged = buf is None
+        nbytes = t.numel() * t.element_size()
+        if staged:
+            buf, off = self._stage(nbytes), 0
+            if self.rank == root:
+                buf.tensor(nbytes, torch.uint8).copy_(t.reshape(-1).view(torch.uint8))
+        if cast_to is not None and t.dtype != torch.float32:
+            raise TypeError("broadcast cast_to needs a float32 source")
+        c16 = cast_to.data_ptr() if cast_to is not None else 0
+        src = buf.ptr + off  # every rank's copy of the payload after the first phase
+        used = lib().broadcast(self._sigs, self.rank, self.epoch, buf.ptrs, off, nbytes, root,
+                               src if cast_to is not None else 0, c16, t.numel() if cast_to is not None else 0,
+                               self.timeout, self.blocks)
+        self._advance(used)
+        if staged and self.rank != root:
+            t.reshape(-1).view(torch.uint8).copy_(buf.tensor(nbytes, torch.uint8))
+        return t
+
+    def barrier(self):
+        used = lib().device_barrier(self._sigs, self.rank, self.epoch, self.timeout)
+        self._advance(used)
+
+    def allreduce_async(self, t: torch.Tensor, algo: str = "ring", scale: float = 1.0,
+                        method: str = "auto") -> GPUWork:
+        """Launch on the comm stream after the work already queued on the current stream."""
+        cur = torch.cuda.current_stream(self.device)
+        self.comm_stream.wait_stream(cur)
+        with torch.cuda.stream(self.comm_stream):
+            self.allreduce(t, algo, scale, method)
+            ev = torch.cuda.Event()
+            ev.record(self.comm_stream)
+        t.record_stream(self.comm_stream)
+        return GPUWork(ev, self)
+
+    def close(self):
+        try:
+            torch.cuda.synchronize(self.device)
+        except Exception:  # noqa: BLE001 - closing after a failure must not raise
+            pass
+        for b in self.buffers:
+            b.free()
+        self.buffers = []
+
+
+def store_exchange(store, rank: int, world: int, prefix: str = ""):
+    """Bootstrap all-gather over the rendezvous store."""
+
+    def ex(key: str, payload: bytes) -> list[bytes]:
+        store.set(f"{prefix}nvl/{key}/{rank}", payload)
+        return [store.get(f"{prefix}nvl/{key}/{r}") for r in range(world)]
+
+    return ex
+
+
+def torch_exchange():
+    """Bootstrap all-gather over an initialised torch.distributed group."""
+    import torch.distributed as dist
+
+    def ex(key: str, payload: bytes) -> list[bytes]:
+        out = [None] * dist.get_world_size()
+        dist.all_gather_object(out, payload)
+        return out
+
+    return ex
+
+
+def from_env(device=None, timeout: float | None = None) -> NVLinkGroup:
+    """NVLinkGroup from RANK / WORLD_SIZE / STORE_ADDR (the launcher) or torchrun's env."""
+    t = timeout if timeout is not None else float(os.environ.get("DTRAIN_TIMEOUT", "60"))
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    dev = torch.device(device) if device is not None else torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if "STORE_ADDR" in os.environ:
+        from ..utils.store import Store
+        store = Store(os.environ["STORE_ADDR"], t)
+        return NVLinkGroup(rank, world, dev, store_exchange(store, rank, world, os.environ.get("DTRAIN_PREFIX", "")),
+                           timeout=t)
+    import torch.distributed as dist
+    if not dist.is_initialized():
+        raise RuntimeError("no STORE_ADDR and torch.distributed is not initialised")
+    return NVLinkGroup(rank, world, dev, torch_exchange(), timeout=t)
