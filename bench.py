@@ -1,0 +1,278 @@
+"""Flagship benchmark: GPT-2-small-shape DDP training throughput on N B200s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--bucket-mb 1]
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \
+        --master-port P bench.py --gpus N --steps K --warmup W
+
+Config (GPT-2-small DDP): 12 layers, d_model 768, 12 heads,
+context 1024, vocab 50304, 16 sequences per GPU of iid uniform random tokens,
+bf16 compute with fp32 grads and master weights, AdamW with global-norm clip
+1.0, 1 MiB gradient buckets, random init.  Weak scaling: per-GPU work is fixed.
+
+Timing: W untimed warm-up steps, then K steps bracketed by a barrier and
+torch.cuda.synchronize() on both sides, timed with CUDA events on the training
+stream; the reported time is the max over ranks.  ``value`` is the whole-job
+tokens/s with inputs already on the device; ``e2e`` is the same metric through
+the public per-step API (``Trainer.step``): each step copies its token ids from
+pinned host memory and reads the loss back.  Inputs (weights, activations,
+logits) are far larger than the 126 MB L2, so no flush is needed between steps.
+
+``--impl reference`` runs the reference's own torch path from ``baseline/_ref``
+(dtrain.torch_ref.TorchGPT + torch DistributedDataParallel over NCCL +
+torch.optim.AdamW + clip_grad_norm_, bf16 autocast) on the same config and
+prints the same JSON line with ``"impl": "reference"``.
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import datetime
+import io
+import json
+import os
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "GPT tokens/s at 1/2/4/8 B200 (DDP, ZeRO-1) vs ref NCCL; all-reduce busbw GB/s"
+MODEL = dict(vocab=50304, ctx=1024, dim=768, heads=12, layers=12)
+SEQ_PER_GPU = 16
+BASELINE_VALUE = None  # BASELINE.md publishes no number for this config (CPU-only reference numbers)
+
+
+def _env_rank():
+    if "RANK" in os.environ and "WORLD_SIZE" in os.environ:
+        return int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ.get("LOCAL_RANK", 0))
+    return 0, 1, 0
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks / throttle reasons while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [r for r in csv.reader(io.StringIO(out)) if len(r) >= 9]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows]
+        smax = float(rows[0][2])
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.strip().lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": smax, "reasons": reasons, "samples": len(rows),
+                "power_w_max": max(float(r[3]) for r in rows if r[3].strip() not in ("", "[N/A]"))}
+
+
+def _timed(fn, steps: int, world: int):
+    """CUDA-event time of ``steps`` calls of fn, barrier + synchronize on both sides; max over ranks (ms)."""
+    import torch.distributed as dist
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(steps):
+        fn(i)
+    end.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+# ------------------------------------------------------------------ our arm
+def run_ours(a, rank, world, local):
+    from dtrain_b200 import train as T
+    from dtrain_b200.models.gpt import GPTConfig
+    from dtrain_b200.ops import kernels as K
+    from dtrain_b200.parallel.nvlink import NVLinkGroup, torch_exchange
+    from dtrain_b200.utils.data import SyntheticData
+    import torch.distributed as dist
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+        pg = NVLinkGroup(rank, world, dev, torch_exchange(), timeout=120.0)
+    else:
+        pg = NVLinkGroup(0, 1, dev, lambda k, p: [p], timeout=120.0)
+    args = T.parse(["--mode", "ddp", "--dtype", "bfloat16", "--batch", str(SEQ_PER_GPU), "--ctx", str(MODEL["ctx"]),
+                    "--dim", str(MODEL["dim"]), "--heads", str(MODEL["heads"]), "--layers", str(MODEL["layers"]),
+                    "--lr", "6e-4", "--clip", "1.0", "--bucket-mb", str(a.bucket_mb), "--data", "synthetic",
+                    "--vocab", str(MODEL["vocab"]), "--algo", a.algo])
+    cfg = GPTConfig(dtype="bfloat16", **MODEL)
+    tr = T.Trainer(args, cfg, dev, pg)
+    data = SyntheticData(MODEL["vocab"])
+    nb = a.warmup + a.steps
+    host = [data.rank_batch(s, 0, SEQ_PER_GPU, MODEL["ctx"], 0, rank, world) for s in range(nb)]
+    dev_batches = [(torch.from_numpy(x).to(dev), torch.from_numpy(y).to(dev)) for x, y in host]
+
+    def device_step(i):  # inputs already resident: the kernel-side number
+        tr.step([[dev_batches[i % nb]]], return_loss=False)
+
+    for i in range(a.warmup):
+        device_step(i)
+    torch.cuda.synchronize()
+    pg.check()
+    sampler = ClockSampler(local) if local == 0 else None
+    if sampler:
+        sampler.start()
+    l0 = K.launch_count()
+    ms = _timed(lambda i: device_step(a.warmup + i), a.steps, world)
+    launches = K.launch_count() - l0
+    clocks = sampler.stop() if sampler else None
+    pg.check()
+
+    # end to end through the public per-step API: H2D of ids from pinned memory + loss D2H every step
+    losses = []
+
+    def e2e_step(i):
+        s = a.warmup + i
+        losses.append(tr.step([[host[s % nb]]]))
+
+    ms_e2e = _timed(e2e_step, a.steps, world)
+    pg.check()
+    tokens = SEQ_PER_GPU * MODEL["ctx"] * world
+    res = {
+        "metric": METRIC, "value": tokens * a.steps / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms / a.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (iid uniform token ids, random-init weights)",
+        "config": {"model": "GPT-2-small (12L, d768, 12H, ctx 1024, vocab 50304)", "global_batch": SEQ_PER_GPU * world,
+                   "seq_len": MODEL["ctx"], "parallelism": f"dp{world}", "bucket_mb": a.bucket_mb,
+                   "optimizer": "AdamW, clip 1.0", "allreduce_order": a.algo,
+                   "l2": "no flush: weights/activations/logits per step >> 126 MB L2"},
+        "e2e": {"value": tokens * a.steps / (ms_e2e / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": 2 * SEQ_PER_GPU * MODEL["ctx"] * 8, "d2h_bytes_per_step": 4,
+                "ms_per_step": ms_e2e / a.steps, "final_loss": losses[-1] if losses else None},
+        "gpu_launches": int(launches),
+        "gpu_launches_per_step": launches / max(1, a.steps),
+        "clocks": clocks,
+    }
+    pg.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return res
+
+
+# ------------------------------------------------------------ reference arm
+def run_reference(a, rank, world, local):
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_dir, "dtrain")):
+        return {"impl": "reference", "unavailable": "baseline/_ref is not installed (pip install --target baseline/_ref)"}
+    sys.path.insert(0, ref_dir)
+    import torch.distributed as dist
+    from torch.nn.parallel import DistributedDataParallel
+
+    from dtrain.nn import GPTConfig as RefConfig
+    from dtrain.torch_ref import TorchGPT
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+    cfg = RefConfig(dtype="float32", **MODEL)
+    # random init with the reference's own initialiser (dtrain.nn.GPT), then its torch mirror
+    from dtrain.nn import GPT as RefGPT
+    model = TorchGPT.from_dtrain(RefGPT(cfg, seed=0)).to(dev)
+    ddp = DistributedDataParallel(model, device_ids=[local], bucket_cap_mb=a.bucket_mb) if world > 1 else model
+    opt = torch.optim.AdamW(model.parameters(), lr=6e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+    rng = np.random.default_rng([0, rank])
+    nb = a.warmup + a.steps
+    host = [rng.integers(0, MODEL["vocab"], size=(SEQ_PER_GPU, MODEL["ctx"] + 1), dtype=np.int64) for _ in range(nb)]
+    pinned = [torch.from_numpy(h).pin_memory() for h in host]
+    dev_tokens = [p.to(dev) for p in pinned]
+
+    def step(tok, read_loss):
+        opt.zero_grad(set_to_none=True)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            _, loss = ddp(tok[:, :-1], tok[:, 1:])
+        loss.backward()
+        torch.nn.utils.clip_grad_norm_(model.parameters(), 1.0)
+        opt.step()
+        return float(loss.item()) if read_loss else None
+
+    for i in range(a.warmup):
+        step(dev_tokens[i], False)
+    sampler = ClockSampler(local) if local == 0 else None
+    if sampler:
+        sampler.start()
+    ms = _timed(lambda i: step(dev_tokens[a.warmup + i], False), a.steps, world)
+    clocks = sampler.stop() if sampler else None
+    ms_e2e = _timed(lambda i: step(pinned[a.warmup + i].to(dev, non_blocking=True), True), a.steps, world)
+    tokens = SEQ_PER_GPU * MODEL["ctx"] * world
+    res = {
+        "impl": "reference", "metric": METRIC, "value": tokens * a.steps / (ms / 1e3), "unit": "tokens/s",
+        "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms / a.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (torch.autocast)",
+        "data": "synthetic (iid uniform token ids, random-init weights)",
+        "config": {"model": "GPT-2-small (12L, d768, 12H, ctx 1024, vocab 50304)", "global_batch": SEQ_PER_GPU * world,
+                   "seq_len": MODEL["ctx"], "parallelism": f"dp{world}", "bucket_mb": a.bucket_mb,
+                   "stack": "dtrain.torch_ref.TorchGPT + torch DDP (NCCL) + torch.optim.AdamW + clip_grad_norm_",
+                   "l2": "no flush: weights/activations/logits per step >> 126 MB L2"},
+        "e2e": {"value": tokens * a.steps / (ms_e2e / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": SEQ_PER_GPU * (MODEL["ctx"] + 1) * 8, "d2h_bytes_per_step": 4,
+                "ms_per_step": ms_e2e / a.steps},
+        "gpu_launches": 0,
+        "clocks": clocks,
+    }
+    if world > 1:
+        dist.destroy_process_group()
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--bucket-mb", type=float, default=1.0)
+    ap.add_argument("--algo", choices=["ring", "direct"], default="ring")
+    a = ap.parse_args()
+    if a.warmup < 3:
+        a.warmup = 3
+    rank, world, local = _env_rank()
+    if world != a.gpus:
+        raise SystemExit(f"--gpus {a.gpus} but WORLD_SIZE={world}; launch N>1 with torch.distributed.run")
+    res = run_reference(a, rank, world, local) if a.impl == "reference" else run_ours(a, rank, world, local)
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

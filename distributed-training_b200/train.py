@@ -121,6 +121,8 @@ class Trainer:
 
     # -------------------------------------------------------------- inputs
     def to_device(self, arr, key) -> torch.Tensor:
+        if isinstance(arr, torch.Tensor) and arr.device == self.device:
+            return arr if arr.dtype == torch.int64 else arr.long()
         t = torch.as_tensor(np.asarray(arr, dtype=np.int64))
         if not self.gpu:
             return t
