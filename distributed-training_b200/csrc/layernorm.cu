@@ -14,6 +14,9 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <cstdio>
+#include <mutex>
+
 #include "common.cuh"
 
 namespace dtb {
@@ -332,5 +335,139 @@ void bias_grad(torch::Tensor g, torch::Tensor db, bool accumulate) {
 }
 
 DTB_DEFINE_STATUS_READER(status_layernorm)
+
+}  // namespace dtb
+
+// ============================================================================
+// dtb_layernorm_bwd_noalloc: allocation-free LayerNorm backward (C entry point)
+// ============================================================================
+// This entry point has no counterpart in the reference project.
+//
+// Who it is for: callers that must not allocate device memory while they run.
+// Examples are host runtimes that reserve the whole GPU in their own pool before
+// training starts (a cudaMalloc would fail, or fragment their pool), and
+// latency-sensitive loops that cannot afford cudaMalloc/cudaFree, which may
+// synchronise the whole device.  It is also usable from plain C, without torch.
+//
+// What it computes: exactly what layernorm_bwd() above computes - dx (bf16),
+// plus dw and db (fp32, written or accumulated) - with the same kernels and the
+// same deterministic two-stage reduction.  The difference is where the per-block
+// partial sums live: instead of a workspace from the caching allocator they go
+// to the file-scope device array below.  The caller still passes every input and
+// output; this function allocates nothing (no cudaMalloc, no cudaFree, no torch).
+//
+// Limits and rules:
+//   * Scratch holds kLnNoAllocScratchFloats floats (4 MiB) per device, resident
+//     on every GPU that loads this library until the process exits.  A call needs
+//     2 * ceil(rows / 64) * C floats; larger calls are rejected (return
+//     DTB_NOALLOC_TOO_LARGE, with a message on stderr) before anything launches.
+//     At C = 768 that is up to 43,690 rows (rows * C <= 32 Mi elements).
+//   * C must be a multiple of 8 and at most 2048; all pointers 16-byte aligned
+//     except mean/rstd/dw/db (4-byte).
+//   * Every call on a device shares the one scratch array, and the array keeps
+//     the previous call's contents.  Nothing in it needs to start at zero (each
+//     call overwrites every partial it later reads), but two calls that overlap on
+//     the GPU - on different streams, or from different host threads without
+//     ordering - race on it.  Serialise calls on one device.
+//   * Set-up: the first call on each device looks up the array's device address
+//     with cudaGetSymbolAddress (with that device current) and caches it; in host
+//     code the array's name is only a host-side stand-in, so it is never passed
+//     to a kernel directly.  Make that first call before any stream capture.
+//
+// Returns 0 on success or a negative DTB_NOALLOC_* code.
+constexpr long kLnNoAllocScratchFloats = 1L << 20;  // 4 MiB of fp32 partials per device
+
+// The scratch array itself (one copy per device that loads this library).
+static __device__ __align__(256) float g_ln_noalloc_scratch[kLnNoAllocScratchFloats];
+
+namespace {
+
+constexpr int kNoAllocMaxDevices = 64;
+
+enum : int {
+  DTB_NOALLOC_OK = 0,
+  DTB_NOALLOC_BAD_ARGUMENT = -1,
+  DTB_NOALLOC_TOO_LARGE = -2,
+  DTB_NOALLOC_SETUP_FAILED = -3,
+  DTB_NOALLOC_LAUNCH_FAILED = -4,
+};
+
+std::mutex g_noalloc_mu;
+float* g_noalloc_scratch_ptr[kNoAllocMaxDevices] = {nullptr};
+
+// Device address of the scratch array on the current device (looked up once per device).
+int noalloc_scratch(float** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return DTB_NOALLOC_SETUP_FAILED;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_ln_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      std::fprintf(stderr, "dtb_layernorm_bwd_noalloc: cudaGetSymbolAddress failed on device %d: %s\n", dev,
+                   cudaGetErrorString(e));
+      return DTB_NOALLOC_SETUP_FAILED;
+    }
+    g_noalloc_scratch_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_scratch_ptr[dev];
+  return DTB_NOALLOC_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+
+extern "C" __attribute__((visibility("default"))) int dtb_layernorm_bwd_noalloc(
+    const void* dy, const void* x, const void* w, const float* mean, const float* rstd, const void* dresid,
+    void* dx, float* dw, float* db, int rows, int C, int accumulate, cudaStream_t stream) {
+  using namespace dtb;
+  if (!dy || !x || !w || !mean || !rstd || !dx || !dw || !db || rows <= 0 || C <= 0 || C % 8 != 0 || C > 2048 ||
+      !aligned16(dy) || !aligned16(x) || !aligned16(w) || !aligned16(dx) || (dresid && !aligned16(dresid)))
+    return DTB_NOALLOC_BAD_ARGUMENT;
+  const long nblk = (rows + kLnBwdRowsPerBlock - 1) / kLnBwdRowsPerBlock;
+  const long need = 2 * nblk * (long)C;
+  if (need > kLnNoAllocScratchFloats) {
+    std::fprintf(stderr,
+                 "dtb_layernorm_bwd_noalloc: rows=%d, C=%d needs %ld scratch floats, more than the fixed %ld "
+                 "(rows * C must stay within about 32 Mi elements)\n",
+                 rows, C, need, kLnNoAllocScratchFloats);
+    return DTB_NOALLOC_TOO_LARGE;
+  }
+  float* scratch = nullptr;
+  if (noalloc_scratch(&scratch) != DTB_NOALLOC_OK) return DTB_NOALLOC_SETUP_FAILED;
+  float* pw = scratch;
+  float* pb = scratch + nblk * C;
+  const int nch = (C + 255) / 256;
+  const size_t smem = (size_t)kLnBwdWarps * 2 * C * sizeof(float);
+  auto* dyp = static_cast<const bf16*>(dy);
+  auto* xp = static_cast<const bf16*>(x);
+  auto* wp = static_cast<const bf16*>(w);
+  auto* drp = static_cast<const bf16*>(dresid);
+  auto* dxp = static_cast<bf16*>(dx);
+#define DTB_LNB_NOALLOC(NC)                                                                                       \
+  {                                                                                                               \
+    auto k = ln_bwd_kernel<NC>;                                                                                   \
+    if (smem > 48 * 1024 && cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=     \
+                                cudaSuccess)                                                                      \
+      return DTB_NOALLOC_LAUNCH_FAILED;                                                                           \
+    k<<<(unsigned)nblk, kLnBwdWarps * 32, smem, stream>>>(dyp, xp, wp, mean, rstd, drp, dxp, pw, pb, rows, C);    \
+  }
+  switch (nch) {
+    case 1: DTB_LNB_NOALLOC(1); break;
+    case 2: DTB_LNB_NOALLOC(2); break;
+    case 3: DTB_LNB_NOALLOC(3); break;
+    case 4: DTB_LNB_NOALLOC(4); break;
+    case 5: case 6: DTB_LNB_NOALLOC(6); break;
+    default: DTB_LNB_NOALLOC(8); break;
+  }
+#undef DTB_LNB_NOALLOC
+  colsum_partials_kernel<<<(C + 255) / 256, 256, 0, stream>>>(pw, (int)nblk, C, dw, accumulate ? 1 : 0);
+  colsum_partials_kernel<<<(C + 255) / 256, 256, 0, stream>>>(pb, (int)nblk, C, db, accumulate ? 1 : 0);
+  if (cudaGetLastError() != cudaSuccess) return DTB_NOALLOC_LAUNCH_FAILED;
+  return DTB_NOALLOC_OK;
+}
+
+namespace dtb {
 
 }  // namespace dtb
