@@ -1,0 +1,226 @@
+"""NVLink collectives (csrc/comm.cu) across real processes, one GPU per rank.
+
+Each test spawns W ranks (W = min(4, visible GPUs); skipped with fewer than 2),
+bootstraps an NVLinkGroup through the rendezvous store and checks results
+against fp64 sums, bit-identity across ranks, and bit-equality with the
+reference's summation orders ("ring": chunk c summed from rank c cyclically;
+"direct": rank order).  The failure test makes one rank skip a collective on
+the host; its peer's device-side wait must time out into CommError with the
+CUDA context still usable - no GPU fault or hang.
+"""
+import multiprocessing as mp
+import os
+import traceback
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+NGPU = torch.cuda.device_count() if torch.cuda.is_available() else 0
+WORLD = min(4, NGPU)
+needs2 = pytest.mark.skipif(NGPU < 2, reason="needs at least 2 GPUs")
+
+
+def _entry(rank, world, addr, fn, args, q):
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    try:
+        import torch
+        from dtrain_b200.parallel.nvlink import NVLinkGroup, store_exchange
+        from dtrain_b200.utils.store import Store
+        torch.cuda.set_device(rank)
+        store = Store(addr, 60)
+        pg = NVLinkGroup(rank, world, torch.device("cuda", rank), store_exchange(store, rank, world), timeout=20.0)
+        res = fn(pg, *args)
+        pg.close()
+        q.put((rank, res))
+    except BaseException as e:  # noqa: BLE001
+        q.put((rank, RuntimeError(f"rank {rank}: {e!r}\n{traceback.format_exc()}")))
+
+
+def _run(world, fn, *args, timeout=240):
+    from dtrain_b200.utils.store import StoreServer
+    srv = StoreServer()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_entry, args=(r, world, srv.address, fn, args, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    out = {}
+    try:
+        for _ in range(world):
+            r, res = q.get(timeout=timeout)
+            out[r] = res
+    finally:
+        for p in ps:
+            p.join(30)
+            if p.is_alive():
+                p.kill()
+        srv.close()
+    errs = [v for v in out.values() if isinstance(v, BaseException)]
+    if errs:
+        raise errs[0]
+    return [out[r] for r in range(world)]
+
+
+def _inputs(rank, n, seed, dtype):
+    return np.random.default_rng([seed, rank]).standard_normal(n).astype(np.float32 if dtype == "f32" else np.float32)
+
+
+def _expected(world, n, seed, algo, dtype):
+    from dtrain_b200.parallel.comm import partition
+    xs = [_inputs(r, n, seed, dtype) for r in range(world)]
+    if dtype == "bf16":
+        xs = [torch.from_numpy(x).bfloat16().float().numpy() for x in xs]
+    out = np.empty(n, np.float32)
+    b = partition(n, world)
+    for c in range(world):
+        lo, hi = b[c], b[c + 1]
+        first = c if algo == "ring" else 0
+        acc = xs[first][lo:hi].copy()
+        for k in range(1, world):
+            acc = (acc + xs[(first + k) % world][lo:hi]).astype(np.float32)
+        out[lo:hi] = acc
+    return out
+
+
+SIZES = [1, 7, 1000, 12345, (1 << 20) + 3]
+
+
+def _allreduce_all(pg, algo, method, dtype):
+    import torch
+    res = []
+    for i, n in enumerate(SIZES):
+        x = torch.from_numpy(_inputs(pg.rank, n, i, dtype)).cuda()
+        if dtype == "bf16":
+            x = x.bfloat16()
+        buf = pg.alloc(n, x.dtype)
+        buf.copy_(x)
+        pg.allreduce(buf, algo, method=method)
+        y = x.clone()
+        pg.allreduce(y, algo, method=method)  # staged path (tensor not peer-mapped)
+        pg.synchronize()
+        res.append((buf.float().cpu().numpy(), y.float().cpu().numpy()))
+    return res
+
+
+@needs2
+@pytest.mark.parametrize("method", ["oneshot", "twoshot"])
+@pytest.mark.parametrize("algo", ["ring", "direct"])
+def test_allreduce_orders_and_bit_identity(method, algo):
+    res = _run(WORLD, _allreduce_all, algo, method, "f32")
+    for i, n in enumerate(SIZES):
+        exp = _expected(WORLD, n, i, algo, "f32")
+        for r in range(WORLD):
+            inplace, staged = res[r][i]
+            assert np.array_equal(inplace, exp), (r, n)
+            assert np.array_equal(staged, exp), (r, n)
+
+
+@needs2
+def test_allreduce_bf16():
+    res = _run(WORLD, _allreduce_all, "direct", "twoshot", "bf16")
+    for i, n in enumerate(SIZES):
+        exp = _expected(WORLD, n, i, "direct", "bf16")
+        for r in range(WORLD):
+            np.testing.assert_allclose(res[r][i][0], exp, rtol=1e-2, atol=1e-2)
+            assert np.array_equal(res[r][i][0], res[0][i][0])
+
+
+def _rs_ag_bcast(pg, n):
+    import torch
+    from dtrain_b200.parallel.comm import partition
+    flat = pg.alloc(n, torch.float32)
+    flat.copy_(torch.arange(n, dtype=torch.float32, device=flat.device) * (pg.rank + 1))
+    mine = pg.reduce_scatter(flat).clone()
+    b = partition(n, pg.world)
+    full = pg.alloc(n, torch.float32)
+    full[b[pg.rank]:b[pg.rank + 1]] = mine
+    pg.all_gather(full)
+    x = torch.full((1001,), float(pg.rank), device=flat.device)
+    pg.broadcast(x, root=1)
+    pg.barrier()
+    pg.synchronize()
+    return mine.cpu().numpy(), full.cpu().numpy(), x.cpu().numpy()
+
+
+@needs2
+@pytest.mark.parametrize("n", [3, 1001, 1 << 20])
+def test_reduce_scatter_all_gather_broadcast(n):
+    from dtrain_b200.parallel.comm import partition
+    res = _run(WORLD, _rs_ag_bcast, n)
+    total = np.arange(n, dtype=np.float32) * sum(range(1, WORLD + 1))
+    b = partition(n, WORLD)
+    for r, (mine, full, x) in enumerate(res):
+        np.testing.assert_array_equal(mine, total[b[r]:b[r + 1]])
+        np.testing.assert_array_equal(full, total)
+        np.testing.assert_array_equal(x, np.ones(1001, np.float32))
+
+
+def _skip_one(pg):
+    import torch
+    from dtrain_b200.utils.store import CommError
+    x = pg.alloc(1 << 16, torch.float32)  # collective allocation, before the fault
+    if pg.rank == 1:
+        # never joins the collective (host-side fault); keeps its buffers mapped
+        # until rank 0 has seen the timeout, then leaves
+        pg._exchange("fault-test-done", b"")
+        return "skipped"
+    pg.timeout = 1.0
+    pg.allreduce(x, "ring", method="twoshot")
+    out = "no error"
+    try:
+        pg.synchronize()
+    except CommError as e:
+        # the context is still usable after the timed-out kernel returned
+        y = torch.ones(10, device=x.device) * 2
+        out = ("commerror", str(e)[:80], float(y.sum().item()))
+    pg._exchange("fault-test-done", b"")
+    return out
+
+
+@needs2
+def test_peer_that_never_arrives_gives_commerror_not_a_hang():
+    res = _run(2, _skip_one)
+    assert res[1] == "skipped"
+    assert res[0][0] == "commerror" and res[0][2] == 20.0
+
+
+def _ddp_step(pg, bucket_mb):
+    import torch
+    from dtrain_b200.models.gpt import GPT, GPTConfig
+    from dtrain_b200.parallel.ddp import DDP
+    cfg = GPTConfig(vocab=512, ctx=128, dim=128, heads=2, layers=2, dtype="bfloat16")
+    m = GPT(cfg, seed=0)
+    ddp = DDP(m, pg, bucket_mb=bucket_mb)
+    g = torch.Generator().manual_seed(0)
+    xs = torch.randint(0, 512, (2 * pg.world, 128), generator=g)
+    ys = torch.randint(0, 512, (2 * pg.world, 128), generator=g)
+    x, y = xs[2 * pg.rank:2 * pg.rank + 2].cuda(), ys[2 * pg.rank:2 * pg.rank + 2].cuda()
+    m.zero_grad()
+    _, loss = m(x, y)
+    loss.backward()
+    ddp.finish()
+    pg.synchronize()
+    return torch.cat([p.grad.reshape(-1) for p in m.parameters()]).cpu().numpy()
+
+
+@needs2
+@pytest.mark.parametrize("bucket_mb", [0.01, 25.0])
+def test_ddp_gradients_match_single_process_and_agree_across_ranks(bucket_mb):
+    from dtrain_b200.models.gpt import GPT, GPTConfig
+    res = _run(2, _ddp_step, bucket_mb)
+    assert np.array_equal(res[0], res[1]), "DDP gradients must be bit-identical across ranks"
+    cfg = GPTConfig(vocab=512, ctx=128, dim=128, heads=2, layers=2, dtype="bfloat16")
+    m = GPT(cfg, seed=0)
+    m.flatten("cuda:0")
+    g = torch.Generator().manual_seed(0)
+    xs = torch.randint(0, 512, (4, 128), generator=g).cuda()
+    ys = torch.randint(0, 512, (4, 128), generator=g).cuda()
+    for sl in (slice(0, 2), slice(2, 4)):
+        _, loss = m(xs[sl], ys[sl])
+        (loss * 0.5).backward()
+    ref = torch.cat([p.grad.reshape(-1) for p in m.parameters()]).cpu().numpy()
+    err = np.linalg.norm(res[0] - ref) / np.linalg.norm(ref)
+    assert err < 1e-2, err
