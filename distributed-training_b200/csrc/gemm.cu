@@ -10,14 +10,18 @@
 //   dX      : A = dY (K-major),  B = W stored (in,out)  -> K-major (W^T)
 //   dW      : A = X  stored (tokens,in) -> MN-major,  B = dY (tokens,out) -> MN-major
 //
-// Structure (one CTA per SM, persistent over output tiles):
+// Structure (one CTA per SM, persistent over output tiles, 10 warps):
 //   warp 0      TMA producer: 128x64 A tile and BNx64 B tile per stage into
 //               128B-swizzled shared memory, one mbarrier per stage.
-//   warp 1      owns TMEM (allocates 2*BN columns = two accumulators) and one
-//               lane issues tcgen05.mma (M=128, N=BN, K=16) for every stage,
-//               then tcgen05.commit to free the stage / publish the accumulator.
-//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time from their TMEM lane
-//               quarter, apply the fused epilogue, store to global memory.
+//   warp 1      owns TMEM (2*BN columns = two accumulators); one lane issues
+//               tcgen05.mma (M=128, N=BN, K=16) for every stage, then
+//               tcgen05.commit to free the stage / publish the accumulator.
+//   warps 2..9  epilogue, two warps per TMEM lane quarter, each owning half of
+//               the tile's columns: tcgen05.ld 64 columns per wait, fused math
+//               (bias, residual, GELU / GELU', scale), bf16/fp32 packing into a
+//               per-warp shared-memory slab, then a TMA bulk-tensor store (or
+//               TMA reduce-add for fp32 accumulation) that writes whole lines and
+//               clips partial tiles in hardware.
 // The two TMEM accumulators let the epilogue of tile i overlap the main loop of
 // tile i+1.  Every barrier wait is bounded (common.cuh).
 #include <torch/extension.h>
@@ -42,12 +46,10 @@ struct GemmArgs {
   int M, N, K;
   int epi;
   int splits;        // split-K factor (>= 1)
-  void* out;
-  long ldo;
   const bf16* bias;  // [N] or nullptr
   const bf16* resid;
   long ldr;
-  bf16* aux;
+  const bf16* aux_in;  // DGELU: pre-activation to differentiate
   long ldx;
   float alpha;
   int accumulate;
@@ -55,16 +57,19 @@ struct GemmArgs {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + kEpiWarps * 32;
+constexpr int kEpiSlab = 4096;  // bytes of store staging per epilogue warp (32 rows x 32 fp32)
 
 template <int BN>
 struct GemmCfg {
   static constexpr int A_BYTES = kBM * kBK * 2;
   static constexpr int B_BYTES = BN * kBK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  static constexpr int STAGES = (BN == 256) ? 4 : 5;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int EPI_BYTES = kEpiWarps * kEpiSlab;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
 
 __device__ __forceinline__ void tile_coords(int t, int mt, int nt, int& mi, int& ni) {
@@ -79,15 +84,6 @@ __device__ __forceinline__ void tile_coords(int t, int mt, int nt, int& mi, int&
   ni = r / gm;
 }
 
-__device__ __forceinline__ void store_bf16x8(bf16* dst, const float* v) {
-  uint4 u;
-  u.x = pack_bf16x2(v[0], v[1]);
-  u.y = pack_bf16x2(v[2], v[3]);
-  u.z = pack_bf16x2(v[4], v[5]);
-  u.w = pack_bf16x2(v[6], v[7]);
-  *reinterpret_cast<uint4*>(dst) = u;
-}
-
 __device__ __forceinline__ void load_bf16x8(const bf16* src, float* v) {
   uint4 u = *reinterpret_cast<const uint4*>(src);
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
@@ -99,114 +95,126 @@ __device__ __forceinline__ void load_bf16x8(const bf16* src, float* v) {
   }
 }
 
-// Apply the epilogue to 8 consecutive columns [col, col+8) of one row.
-__device__ __forceinline__ void epi8(const GemmArgs& a, int row, int col, float* v, int split) {
-  const bool full = (col + 8 <= a.N);
+// Load 32 bf16 values [col, col+32) of a row into fp32 (zeros past n_valid).
+__device__ __forceinline__ void load_row32(const bf16* rowp, int col, int N, float* v) {
+  if (col + 32 <= N) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) load_bf16x8(rowp + col + j, v + j);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = (col + j < N) ? bf2f(rowp[col + j]) : 0.f;
+  }
+}
+
+// Write 32 fp32 values as bf16 into this lane's 64-byte row of a slab.
+__device__ __forceinline__ void slab_put_bf16(uint8_t* slab, int lane, const float* v) {
+  uint4* dst = reinterpret_cast<uint4*>(slab + lane * 64);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint4 u;
+    u.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
+    u.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+    u.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+    u.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+    dst[j] = u;
+  }
+}
+
+__device__ __forceinline__ void slab_put_f32(uint8_t* slab, int lane, const float* v) {
+  float4* dst = reinterpret_cast<float4*>(slab + lane * 128);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+}
+
+// Epilogue for one 32x32 chunk held in registers (this lane = one row).  Writes the
+// staging slab and lets lane 0 issue the TMA store(s).
+__device__ __forceinline__ void epi_chunk(const GemmArgs& a, const CUtensorMap* tmOut, const CUtensorMap* tmAux,
+                                          uint8_t* slab, int lane, int row0, int col, int split, float* v) {
+  const int row = row0 + lane;
+  const bool row_ok = row < a.M;
   switch (a.epi) {
     case EPI_BF16: {
-      float b[8], r[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] *= a.alpha;
-      if (full) {
-        if (a.bias) {
-          load_bf16x8(a.bias + col, b);
+      for (int j = 0; j < 32; ++j) v[j] *= a.alpha;
+      if (a.bias) {
+        float b[32];
+        load_row32(a.bias, col, a.N, b);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) v[j] += b[j];
-        }
-        if (a.resid) {
-          load_bf16x8(a.resid + (long)row * a.ldr + col, r);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) v[j] += r[j];
-        }
-        store_bf16x8(reinterpret_cast<bf16*>(a.out) + (long)row * a.ldo + col, v);
-      } else {
-        for (int j = 0; j < 8 && col + j < a.N; ++j) {
-          float x = v[j];
-          if (a.bias) x += bf2f(a.bias[col + j]);
-          if (a.resid) x += bf2f(a.resid[(long)row * a.ldr + col + j]);
-          reinterpret_cast<bf16*>(a.out)[(long)row * a.ldo + col + j] = f2bf(x);
-        }
+        for (int j = 0; j < 32; ++j) v[j] += b[j];
       }
+      if (a.resid && row_ok) {
+        float r[32];
+        load_row32(a.resid + (long)row * a.ldr, col, a.N, r);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] += r[j];
+      }
+      slab_put_bf16(slab, lane, v);
       break;
     }
     case EPI_GELU: {
-      float b[8];
-      if (full) {
-        if (a.bias) {
-          load_bf16x8(a.bias + col, b);
+      if (a.bias) {
+        float b[32];
+        load_row32(a.bias, col, a.N, b);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) v[j] += b[j];
-        }
-        // round the pre-activation to bf16 first: backward sees exactly this value
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = bf2f(f2bf(v[j]));
-        store_bf16x8(a.aux + (long)row * a.ldx + col, v);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = gelu_tanh(v[j]);
-        store_bf16x8(reinterpret_cast<bf16*>(a.out) + (long)row * a.ldo + col, v);
-      } else {
-        for (int j = 0; j < 8 && col + j < a.N; ++j) {
-          float x = v[j] + (a.bias ? bf2f(a.bias[col + j]) : 0.f);
-          bf16 xb = f2bf(x);
-          a.aux[(long)row * a.ldx + col + j] = xb;
-          reinterpret_cast<bf16*>(a.out)[(long)row * a.ldo + col + j] = f2bf(gelu_tanh(bf2f(xb)));
-        }
+        for (int j = 0; j < 32; ++j) v[j] += b[j];
       }
+      // the saved pre-activation is the bf16-rounded value; GELU is taken of exactly that
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = bf2f(f2bf(v[j]));
+      slab_put_bf16(slab, lane, v);  // aux chunk at slab[0, 2048)
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = gelu_fast(v[j]);
+      slab_put_bf16(slab + 2048, lane, v);  // out chunk at slab[2048, 4096)
       break;
     }
     case EPI_DGELU: {
-      float h[8];
-      if (full) {
-        load_bf16x8(a.aux + (long)row * a.ldx + col, h);
+      if (row_ok) {
+        float h[32];
+        load_row32(a.aux_in + (long)row * a.ldx, col, a.N, h);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] *= gelu_tanh_grad(h[j]);
-        store_bf16x8(reinterpret_cast<bf16*>(a.out) + (long)row * a.ldo + col, v);
-      } else {
-        for (int j = 0; j < 8 && col + j < a.N; ++j) {
-          float g = gelu_tanh_grad(bf2f(a.aux[(long)row * a.ldx + col + j]));
-          reinterpret_cast<bf16*>(a.out)[(long)row * a.ldo + col + j] = f2bf(v[j] * g);
-        }
+        for (int j = 0; j < 32; ++j) v[j] *= gelu_grad_fast(h[j]);
       }
+      slab_put_bf16(slab, lane, v);
       break;
     }
     case EPI_F32: {
-      float* o = reinterpret_cast<float*>(a.out) + (long)row * a.ldo + col;
-      if (full) {
-        float4* o4 = reinterpret_cast<float4*>(o);
-        float4 x0 = make_float4(v[0] * a.alpha, v[1] * a.alpha, v[2] * a.alpha, v[3] * a.alpha);
-        float4 x1 = make_float4(v[4] * a.alpha, v[5] * a.alpha, v[6] * a.alpha, v[7] * a.alpha);
-        if (a.accumulate) {
-          float4 p0 = o4[0], p1 = o4[1];
-          x0.x += p0.x; x0.y += p0.y; x0.z += p0.z; x0.w += p0.w;
-          x1.x += p1.x; x1.y += p1.y; x1.z += p1.z; x1.w += p1.w;
-        }
-        o4[0] = x0;
-        o4[1] = x1;
-      } else {
-        for (int j = 0; j < 8 && col + j < a.N; ++j) o[j] = (a.accumulate ? o[j] : 0.f) + v[j] * a.alpha;
-      }
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] *= a.alpha;
+      slab_put_f32(slab, lane, v);
       break;
     }
     case EPI_PARTIAL: {
-      float* o = reinterpret_cast<float*>(a.out) + (long)split * a.M * a.N + (long)row * a.N + col;
-      if (full && (a.N % 4 == 0)) {
-        reinterpret_cast<float4*>(o)[0] = make_float4(v[0], v[1], v[2], v[3]);
-        reinterpret_cast<float4*>(o)[1] = make_float4(v[4], v[5], v[6], v[7]);
-      } else {
-        for (int j = 0; j < 8 && col + j < a.N; ++j) o[j] = v[j];
-      }
+      slab_put_f32(slab, lane, v);
       break;
     }
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    if (a.epi == EPI_GELU) {
+      tma_store_2d(tmAux, slab, col, row0);
+      tma_store_2d(tmOut, slab + 2048, col, row0);
+    } else if (a.epi == EPI_PARTIAL) {
+      tma_store_3d(tmOut, slab, col, row0, split);
+    } else if (a.epi == EPI_F32 && a.accumulate) {
+      tma_reduce_add_2d(tmOut, slab, col, row0);
+    } else {
+      tma_store_2d(tmOut, slab, col, row0);
+    }
+    bulk_commit();
   }
 }
 
 template <int BN, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs args) {
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmAux,
+                   GemmArgs args) {
   using Cfg = GemmCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + Cfg::STAGES * Cfg::STAGE_BYTES);
+  uint8_t* epi_smem = smem + Cfg::STAGES * Cfg::STAGE_BYTES;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(epi_smem + Cfg::EPI_BYTES);
   uint64_t* empty_bar = full_bar + Cfg::STAGES;
   uint64_t* tfull_bar = empty_bar + Cfg::STAGES;  // [2]
   uint64_t* tempty_bar = tfull_bar + 2;           // [2]
@@ -223,7 +231,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull_bar[b], 1);
-      mbar_init(&tempty_bar[b], 4);
+      mbar_init(&tempty_bar[b], kEpiWarps);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -317,7 +325,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // -------------------------------------------------------------- epilogue
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int ew = warp - 2;       // 0..7
+    const int q = warp & 3;        // TMEM lane quarter this warp may access
+    const int half = ew >> 2;      // which half of the tile's columns
+    uint8_t* slab = epi_smem + ew * kEpiSlab;
     int ab = 0;
     uint32_t aphase = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x) {
@@ -327,18 +338,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m0 = mi * kBM, n0 = ni * BN;
       if (!mbar_wait(&tfull_bar[ab], aphase, abort_flag)) break;
       tc_fence_after();
-      const int row = m0 + q * 32 + lane;
+      const int row0 = m0 + q * 32;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN);
+      const int c_begin = half * (BN / 2), c_end = c_begin + BN / 2;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
+      for (int c = c_begin; c < c_end; c += 64) {
         if (n0 + c >= N) break;  // warp-uniform
+        uint32_t r0[32], r1[32];
+        tmem_ld32_issue(tbase + c, r0);
+        tmem_ld32_issue(tbase + c + 32, r1);
+        tmem_wait_ld();
         float v[32];
-        tmem_ld32(tbase + c, v);
-        if (row < M) {
+        // chunk c .. c+31
 #pragma unroll
-          for (int j = 0; j < 32; j += 8) {
-            if (n0 + c + j < N) epi8(args, row, n0 + c + j, v + j, sp);
-          }
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r0[j]);
+        if (lane == 0) bulk_wait_read0();  // the slab's previous store has read its source
+        __syncwarp();
+        epi_chunk(args, &tmOut, &tmAux, slab, lane, row0, n0 + c, sp, v);
+        // chunk c+32 .. c+63
+        if (n0 + c + 32 < N) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r1[j]);
+          if (lane == 0) bulk_wait_read0();
+          __syncwarp();
+          epi_chunk(args, &tmOut, &tmAux, slab, lane, row0, n0 + c + 32, sp, v);
         }
       }
       tc_fence_before();
@@ -346,6 +369,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&tempty_bar[ab]);
       if (++ab == 2) { ab = 0; aphase ^= 1; }
     }
+    if (lane == 0) bulk_wait0();
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -399,7 +424,7 @@ static EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-// 2-D bf16 tensor map over a row-major matrix [rows, cols] with row stride ld (elements).
+// 2-D bf16 operand map over a row-major matrix [rows, cols] with row stride ld (elements), 128B swizzle.
 static CUtensorMap make_map(const void* base, long rows, long cols, long ld, int box_cols, int box_rows) {
   CUtensorMap m;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
@@ -410,6 +435,32 @@ static CUtensorMap make_map(const void* base, long rows, long cols, long ld, int
                                estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with code ", (int)r);
+  return m;
+}
+
+// Store map: [rows, cols] (optionally [depth, rows, cols]) row-major, 32x32 boxes, no swizzle.
+static CUtensorMap make_store_map(void* base, bool f32, long rows, long cols, long ld, long depth = 0) {
+  CUtensorMap m;
+  const int esz = f32 ? 4 : 2;
+  const CUtensorMapDataType dt = f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r;
+  if (depth > 0) {
+    cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)depth};
+    cuuint64_t strides[2] = {(cuuint64_t)ld * esz, (cuuint64_t)ld * rows * esz};
+    cuuint32_t box[3] = {32, 32, 1};
+    r = get_encode_fn()(&m, dt, 3, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * esz};
+    cuuint32_t box[2] = {32, 32};
+    r = get_encode_fn()(&m, dt, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (store) failed with code ", (int)r);
   return m;
 }
 
@@ -424,7 +475,8 @@ static int num_sms() {
 }
 
 template <int BN, bool A_MN, bool B_MN>
-static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, cudaStream_t st) {
+static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const CUtensorMap& tx,
+                        const GemmArgs& a, cudaStream_t st) {
   using Cfg = GemmCfg<BN>;
   static bool attr_set = false;
   auto kern = gemm_tc_kernel<BN, A_MN, B_MN>;
@@ -435,27 +487,35 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const Gemm
   const int mt = (a.M + kBM - 1) / kBM, nt = (a.N + BN - 1) / BN;
   const int units = mt * nt * a.splits;
   const int grid = std::min(units, num_sms());
-  kern<<<grid, kThreads, Cfg::SMEM_BYTES, st>>>(ta, tb, a);
+  kern<<<grid, kThreads, Cfg::SMEM_BYTES, st>>>(ta, tb, to, tx, a);
   count_launch();
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-// Picks the tile width and split-K factor: prefer BN=256 (fewer shared-memory
-// bytes per FLOP); fall back to BN=128 and then split K until the persistent grid
-// covers the SMs.
-static void choose_tiling(int M, int N, int K, int& bn, int& splits) {
+// Picks the tile width and split-K factor.  128x256 tiles sustain ~1.4 PFLOP/s
+// on the main loop while 128x128 tiles measured ~0.8, so BN=256 is used whenever
+// N > 128.  The split-K factor s minimises a makespan model of the persistent
+// grid: ceil(tiles*s / SMs) waves of ceil(kb/s) k-blocks each, plus the fp32
+// partial traffic of the deterministic reduction ((s+1) M N 4 bytes) when s > 1.
+static void choose_tiling(int M, int N, int K, int& bn, int& splits, bool allow_split = true) {
   const int sms = num_sms();
   const int mt = (M + kBM - 1) / kBM;
-  const int t256 = mt * ((N + 255) / 256), t128 = mt * ((N + 127) / 128);
-  if (t256 >= sms || N <= 128) {
-    bn = (N <= 128) ? 128 : 256;
-  } else {
-    bn = 128;
-  }
-  const int tiles = (bn == 256) ? t256 : t128;
-  splits = 1;
+  bn = (N <= 128) ? 128 : 256;
+  const int tiles = mt * ((N + bn - 1) / bn);
   const int kb = (K + kBK - 1) / kBK;
-  while (tiles * splits * 2 <= sms + sms / 4 && kb / (splits * 2) >= 4) splits *= 2;
+  const double kb_seconds = 2.0 * kBM * bn * kBK / (1.4e15 / sms);  // one k-block on one SM
+  splits = 1;
+  double best = 1e30;
+  for (int s = 1; s <= 16; ++s) {
+    if (s > 1 && (!allow_split || kb / s < 8)) break;
+    const long waves = ((long)tiles * s + sms - 1) / sms;
+    const double t = waves * (double)((kb + s - 1) / s) * kb_seconds +
+                     (s > 1 ? (double)M * N * 4.0 * (s + 1) / 6.0e12 + 4e-6 : 0.0);
+    if (t < best * 0.97) {
+      best = t;
+      splits = s;
+    }
+  }
 }
 
 // a: stored [M,K] (a_trans=false) or [K,M] (a_trans=true); b: stored [K,N] (b_trans=false) or [N,K] (b_trans=true).
@@ -482,6 +542,7 @@ void gemm(torch::Tensor a, bool a_trans, torch::Tensor b, bool b_trans, torch::T
               "gemm: output columns / leading dimension must be multiples of 8 and 16-byte aligned");
   const bool f32_out = (epi == EPI_F32);
   TORCH_CHECK(out.scalar_type() == (f32_out ? at::kFloat : at::kBFloat16), "gemm: wrong output dtype for epilogue");
+  TORCH_CHECK(epi >= EPI_BF16 && epi <= EPI_F32, "gemm: unknown epilogue");
   c10::cuda::CUDAGuard guard(a.device());
 
   GemmArgs args{};
@@ -489,8 +550,6 @@ void gemm(torch::Tensor a, bool a_trans, torch::Tensor b, bool b_trans, torch::T
   args.N = (int)N;
   args.K = (int)K;
   args.epi = (int)epi;
-  args.out = out.data_ptr();
-  args.ldo = out.stride(0);
   args.alpha = (float)alpha;
   args.accumulate = accumulate ? 1 : 0;
   if (bias && bias->defined()) {
@@ -504,22 +563,26 @@ void gemm(torch::Tensor a, bool a_trans, torch::Tensor b, bool b_trans, torch::T
     args.resid = reinterpret_cast<const bf16*>(resid->data_ptr());
     args.ldr = resid->stride(0);
   }
+  torch::Tensor auxt;
   if (aux && aux->defined()) {
     TORCH_CHECK(aux->scalar_type() == at::kBFloat16 && aux->size(0) == M && aux->size(1) == N &&
-                    aux->stride(1) == 1 && aux->stride(0) % 8 == 0,
+                    aux->stride(1) == 1 && aux->stride(0) % 8 == 0 &&
+                    (reinterpret_cast<uintptr_t>(aux->data_ptr()) & 15) == 0,
                 "gemm: aux");
-    args.aux = reinterpret_cast<bf16*>(aux->data_ptr());
+    auxt = *aux;
+    args.aux_in = reinterpret_cast<const bf16*>(aux->data_ptr());
     args.ldx = aux->stride(0);
   }
-  TORCH_CHECK(epi != EPI_GELU && epi != EPI_DGELU ? true : args.aux != nullptr, "gemm: gelu epilogues need aux");
+  TORCH_CHECK((epi != EPI_GELU && epi != EPI_DGELU) || auxt.defined(), "gemm: gelu epilogues need aux");
 
+  // split-K is only wired for the fp32 / bf16 plain epilogues without bias or residual
+  const bool can_split = (epi == EPI_F32) || (epi == EPI_BF16 && !args.bias && !args.resid);
   int bn, splits;
-  choose_tiling((int)M, (int)N, (int)K, bn, splits);
+  choose_tiling((int)M, (int)N, (int)K, bn, splits, can_split);
   if (force_bn > 0) bn = (int)force_bn;
   if (force_splits > 0) splits = (int)force_splits;
   TORCH_CHECK(bn == 128 || bn == 256, "gemm: BN must be 128 or 256");
-  // split-K is only wired for the fp32 / bf16 plain epilogues without bias or residual
-  if (splits > 1 && !((epi == EPI_F32) || (epi == EPI_BF16 && !args.bias && !args.resid))) splits = 1;
+  if (splits > 1 && !can_split) splits = 1;
 
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   // A map: K-major [M rows, K cols] box {64, 128}; MN-major [K rows, M cols] box {64, 64}
@@ -530,6 +593,7 @@ void gemm(torch::Tensor a, bool a_trans, torch::Tensor b, bool b_trans, torch::T
 
   GemmArgs run = args;
   torch::Tensor ws;
+  CUtensorMap to, tx;
   if (splits > 1) {
     const long need = (long)splits * M * N;
     if (workspace && workspace->defined() && workspace->numel() >= need) {
@@ -538,17 +602,19 @@ void gemm(torch::Tensor a, bool a_trans, torch::Tensor b, bool b_trans, torch::T
       ws = torch::empty({need}, a.options().dtype(at::kFloat));
     }
     run.epi = EPI_PARTIAL;
-    run.out = ws.data_ptr();
     run.splits = splits;
+    to = make_store_map(ws.data_ptr(), true, M, N, N, splits);
   } else {
     run.splits = 1;
+    to = make_store_map(out.data_ptr(), f32_out, M, N, out.stride(0));
   }
+  tx = (epi == EPI_GELU) ? make_store_map(auxt.data_ptr(), false, M, N, auxt.stride(0)) : to;
 
-#define DTB_GEMM_DISPATCH(BNV)                                           \
-  if (!a_trans && !b_trans) launch_gemm<BNV, false, true>(ta, tb, run, st);  \
-  else if (!a_trans && b_trans) launch_gemm<BNV, false, false>(ta, tb, run, st); \
-  else if (a_trans && !b_trans) launch_gemm<BNV, true, true>(ta, tb, run, st);   \
-  else launch_gemm<BNV, true, false>(ta, tb, run, st);
+#define DTB_GEMM_DISPATCH(BNV)                                                      \
+  if (!a_trans && !b_trans) launch_gemm<BNV, false, true>(ta, tb, to, tx, run, st);   \
+  else if (!a_trans && b_trans) launch_gemm<BNV, false, false>(ta, tb, to, tx, run, st); \
+  else if (a_trans && !b_trans) launch_gemm<BNV, true, true>(ta, tb, to, tx, run, st);   \
+  else launch_gemm<BNV, true, false>(ta, tb, to, tx, run, st);
   if (bn == 256) {
     DTB_GEMM_DISPATCH(256)
   } else {

@@ -107,55 +107,57 @@ constexpr int kLnBwdRowsPerBlock = 64;
 // Block b handles rows [b*64, b*64+64); warp k handles rows b*64 + k, +8, ...
 // Per-block dw/db partials go to part_w/part_b [gridDim.x, C].
 template <int NCH>
-__global__ void __launch_bounds__(kLnBwdWarps * 32)
+__global__ void __launch_bounds__(kLnBwdWarps * 32, 2)
     ln_bwd_kernel(const bf16* __restrict__ dy, const bf16* __restrict__ x, const bf16* __restrict__ w,
                   const float* __restrict__ mean, const float* __restrict__ rstd, const bf16* __restrict__ dresid,
                   bf16* __restrict__ dx, float* __restrict__ part_w, float* __restrict__ part_b, int rows, int C) {
   extern __shared__ float sm[];  // [kLnBwdWarps][2][C]
   const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float aw[NCH][8], ab[NCH][8], wv[NCH][8];
+  float aw[NCH][8], ab[NCH][8];
 #pragma unroll
-  for (int c = 0; c < NCH; ++c) {
-    const int col = (c * 32 + lane) * 8;
+  for (int c = 0; c < NCH; ++c)
 #pragma unroll
     for (int j = 0; j < 8; ++j) aw[c][j] = ab[c][j] = 0.f;
-    if (col < C) ld8(w + col, wv[c]);
-  }
   const int r0 = blockIdx.x * kLnBwdRowsPerBlock;
   for (int rr = wid; rr < kLnBwdRowsPerBlock; rr += kLnBwdWarps) {
     const int r = r0 + rr;
     if (r >= rows) break;
     const float mu = mean[r], rs = rstd[r];
-    float g[NCH][8], xh[NCH][8];
     float s1 = 0.f, s2 = 0.f;
+    // pass 1: row statistics of g*w and g*w*xhat, plus the dw/db accumulators
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
       const int col = (c * 32 + lane) * 8;
       if (col < C) {
-        float xv[8];
-        ld8(dy + (long)r * C + col, g[c]);
+        float g[8], xv[8], wv[8];
+        ld8(dy + (long)r * C + col, g);
         ld8(x + (long)r * C + col, xv);
+        ld8(w + col, wv);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          xh[c][j] = (xv[j] - mu) * rs;
-          const float gw = g[c][j] * wv[c][j];
+          const float xh = (xv[j] - mu) * rs;
+          const float gw = g[j] * wv[j];
           s1 += gw;
-          s2 += gw * xh[c][j];
-          aw[c][j] += g[c][j] * xh[c][j];
-          ab[c][j] += g[c][j];
+          s2 += gw * xh;
+          aw[c][j] += g[j] * xh;
+          ab[c][j] += g[j];
         }
       }
     }
     const float m1 = warp_sum(s1) / C, m2 = warp_sum(s2) / C;
+    // pass 2: dx (operands re-read; they are still in L1)
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
       const int col = (c * 32 + lane) * 8;
       if (col < C) {
-        float o[8], rv[8];
+        float g[8], xv[8], wv[8], o[8], rv[8];
+        ld8(dy + (long)r * C + col, g);
+        ld8(x + (long)r * C + col, xv);
+        ld8(w + col, wv);
         if (dresid) ld8(dresid + (long)r * C + col, rv);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          o[j] = rs * (g[c][j] * wv[c][j] - m1 - xh[c][j] * m2);
+          o[j] = rs * (g[j] * wv[j] - m1 - (xv[j] - mu) * rs * m2);
           if (dresid) o[j] += rv[j];
         }
         st8(dx + (long)r * C + col, o);
@@ -186,14 +188,33 @@ __global__ void __launch_bounds__(kLnBwdWarps * 32)
   }
 }
 
-// out[col] = (accumulate ? out[col] : 0) + sum_{k=0..nparts-1} part[k, col]  (fixed order)
-__global__ void colsum_partials_kernel(const float* __restrict__ part, int nparts, int C, float* __restrict__ out,
-                                       int accumulate) {
-  const int col = blockIdx.x * blockDim.x + threadIdx.x;
-  if (col >= C) return;
+// out[col] = (accumulate ? out[col] : 0) + sum_{k=0..nparts-1} part[k, col].
+// Block = 32 columns x 8 partial-lanes: lane k sums partials k, k+8, ... (coalesced
+// 128-byte rows), then lane sums are combined in lane order - a fixed order, so
+// the result is deterministic.
+constexpr int kColsumThreads = 256;
+__global__ void __launch_bounds__(kColsumThreads)
+    colsum_partials_kernel(const float* __restrict__ part, int nparts, int C, float* __restrict__ out,
+                           int accumulate) {
+  __shared__ float sm[8][33];
+  const int cl = threadIdx.x & 31, kl = threadIdx.x >> 5;
+  const int col = blockIdx.x * 32 + cl;
   float s = 0.f;
-  for (int k = 0; k < nparts; ++k) s += part[(long)k * C + col];
-  out[col] = accumulate ? out[col] + s : s;
+  if (col < C)
+    for (int k = kl; k < nparts; k += 8) s += part[(long)k * C + col];
+  sm[kl][cl] = s;
+  __syncthreads();
+  if (kl == 0 && col < C) {
+    float t = sm[0][cl];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) t += sm[i][cl];
+    out[col] = accumulate ? out[col] + t : t;
+  }
+}
+
+static inline void launch_colsum(const float* part, int nparts, int C, float* out, int accumulate,
+                                 cudaStream_t st) {
+  colsum_partials_kernel<<<(C + 31) / 32, kColsumThreads, 0, st>>>(part, nparts, C, out, accumulate);
 }
 
 // Bias gradient stage 1: partial column sums of a bf16 [rows, N] matrix over
@@ -308,8 +329,8 @@ torch::Tensor layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, 
 #undef LNB
   count_launch();
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  colsum_partials_kernel<<<(C + 255) / 256, 256, 0, st>>>(pw, nblk, C, dw.data_ptr<float>(), accumulate ? 1 : 0);
-  colsum_partials_kernel<<<(C + 255) / 256, 256, 0, st>>>(pb, nblk, C, db.data_ptr<float>(), accumulate ? 1 : 0);
+  launch_colsum(pw, nblk, C, dw.data_ptr<float>(), accumulate ? 1 : 0, st);
+  launch_colsum(pb, nblk, C, db.data_ptr<float>(), accumulate ? 1 : 0, st);
   count_launch(2);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return dx;
@@ -328,8 +349,7 @@ void bias_grad(torch::Tensor g, torch::Tensor db, bool accumulate) {
   dim3 grid((N + 255) / 256, rb);
   colsum_bf16_stage1<<<grid, 256, 0, st>>>(reinterpret_cast<const bf16*>(g.data_ptr()), g.stride(0), rows, N,
                                            part.data_ptr<float>());
-  colsum_partials_kernel<<<(N + 255) / 256, 256, 0, st>>>(part.data_ptr<float>(), rb, N, db.data_ptr<float>(),
-                                                          accumulate ? 1 : 0);
+  launch_colsum(part.data_ptr<float>(), rb, N, db.data_ptr<float>(), accumulate ? 1 : 0, st);
   count_launch(2);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -462,8 +482,8 @@ extern "C" __attribute__((visibility("default"))) int dtb_layernorm_bwd_noalloc(
     default: DTB_LNB_NOALLOC(8); break;
   }
 #undef DTB_LNB_NOALLOC
-  colsum_partials_kernel<<<(C + 255) / 256, 256, 0, stream>>>(pw, (int)nblk, C, dw, accumulate ? 1 : 0);
-  colsum_partials_kernel<<<(C + 255) / 256, 256, 0, stream>>>(pb, (int)nblk, C, db, accumulate ? 1 : 0);
+  launch_colsum(pw, (int)nblk, C, dw, accumulate ? 1 : 0, stream);
+  launch_colsum(pb, (int)nblk, C, db, accumulate ? 1 : 0, stream);
   if (cudaGetLastError() != cudaSuccess) return DTB_NOALLOC_LAUNCH_FAILED;
   return DTB_NOALLOC_OK;
 }
