@@ -494,12 +494,19 @@ static void check_qkv(const torch::Tensor& qkv, int64_t B, int64_t T, int64_t H,
   TORCH_CHECK(D == 64 || D == 128, "attention: head dim must be 64 or 128");
 }
 
-// Returns (out [B*T, H*D] bf16, lse2 [B*H, T] fp32).
-std::vector<torch::Tensor> attn_fwd(torch::Tensor qkv, int64_t B, int64_t T, int64_t H, int64_t D) {
+void attn_fwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor lse, int64_t B, int64_t T, int64_t H);
+
+// Returns (out [B*T, H*D] bf16, lse2 [B*H, T] fp32).  Head dim 64 runs the tcgen05
+// kernel (attention_tc.cu) unless `legacy` asks for the mma.sync kernel below.
+std::vector<torch::Tensor> attn_fwd(torch::Tensor qkv, int64_t B, int64_t T, int64_t H, int64_t D, bool legacy) {
   check_qkv(qkv, B, T, H, D);
   c10::cuda::CUDAGuard guard(qkv.device());
   auto out = torch::empty({B * T, H * D}, qkv.options());
   auto lse = torch::empty({B * H, T}, qkv.options().dtype(at::kFloat));
+  if (D == 64 && !legacy) {
+    attn_fwd_tc(qkv, out, lse, B, T, H);
+    return {out, lse};
+  }
   const float sl2 = (float)(1.0 / std::sqrt((double)D) * 1.4426950408889634);
   dim3 grid((unsigned)((T + attn::BQ - 1) / attn::BQ), (unsigned)(B * H));
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
@@ -520,9 +527,28 @@ std::vector<torch::Tensor> attn_fwd(torch::Tensor qkv, int64_t B, int64_t T, int
 }
 
 // Returns dqkv [B*T, 3*H*D] bf16.
+void attn_bwd_tc(torch::Tensor qkv, torch::Tensor dout, torch::Tensor lse, torch::Tensor delta, torch::Tensor dqkv,
+                 int64_t B, int64_t T, int64_t H);
+
+// Head dim 64 runs the tcgen05 backward kernels (attention_tc.cu) unless `legacy`.
 torch::Tensor attn_bwd(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torch::Tensor lse, int64_t B,
-                       int64_t T, int64_t H, int64_t D) {
+                       int64_t T, int64_t H, int64_t D, bool legacy) {
   check_qkv(qkv, B, T, H, D);
+  if (D == 64 && !legacy) {
+    TORCH_CHECK(dout.is_contiguous() && dout.scalar_type() == at::kBFloat16 && dout.numel() == B * T * H * D,
+                "attention: dout");
+    c10::cuda::CUDAGuard guard(qkv.device());
+    auto dqkv = torch::empty_like(qkv);
+    auto delta = torch::empty({B * H, T}, qkv.options().dtype(at::kFloat));
+    const long warps = B * T * H;
+    attn::delta_kernel<64><<<(unsigned)((warps * 32 + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+        reinterpret_cast<const bf16*>(out.data_ptr()), reinterpret_cast<const bf16*>(dout.data_ptr()),
+        delta.data_ptr<float>(), (int)B, (int)T, (int)H);
+    count_launch();
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    attn_bwd_tc(qkv, dout, lse, delta, dqkv, B, T, H);
+    return dqkv;
+  }
   TORCH_CHECK(dout.is_contiguous() && dout.scalar_type() == at::kBFloat16 && dout.numel() == B * T * H * D,
               "attention: dout");
   c10::cuda::CUDAGuard guard(qkv.device());

@@ -34,9 +34,9 @@ void grad_sqnorm(torch::Tensor g, torch::Tensor out, double scale);
 void cast_f32_bf16(torch::Tensor x, torch::Tensor y);
 void scale_f32(torch::Tensor x, double s);
 // attention.cu
-std::vector<torch::Tensor> attn_fwd(torch::Tensor qkv, int64_t B, int64_t T, int64_t H, int64_t D);
+std::vector<torch::Tensor> attn_fwd(torch::Tensor qkv, int64_t B, int64_t T, int64_t H, int64_t D, bool legacy);
 torch::Tensor attn_bwd(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torch::Tensor lse, int64_t B,
-                       int64_t T, int64_t H, int64_t D);
+                       int64_t T, int64_t H, int64_t D, bool legacy);
 // comm.cu
 std::tuple<int64_t, torch::Tensor> symm_alloc(int64_t nbytes);
 int64_t symm_open(torch::Tensor handle);
@@ -72,11 +72,12 @@ int status_embed_xent();
 int status_optim();
 int status_attention();
 int status_comm();
+int status_attention_tc();
 
 // First non-zero device status word over all kernel files (and clears them).
 int64_t device_status() {
   int codes[] = {status_gemm(), status_layernorm(), status_embed_xent(), status_optim(), status_attention(),
-                 status_comm()};
+                 status_comm(), status_attention_tc()};
   for (int c : codes)
     if (c) return c;
   return 0;
@@ -105,8 +106,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("grad_sqnorm", &grad_sqnorm);
   m.def("cast_f32_bf16", &cast_f32_bf16);
   m.def("scale_f32", &scale_f32);
-  m.def("attn_fwd", &attn_fwd);
-  m.def("attn_bwd", &attn_bwd);
+  m.def("attn_fwd", &attn_fwd, py::arg("qkv"), py::arg("B"), py::arg("T"), py::arg("H"), py::arg("D"),
+        py::arg("legacy") = false);
+  m.def("attn_bwd", &attn_bwd, py::arg("qkv"), py::arg("out"), py::arg("dout"), py::arg("lse"), py::arg("B"),
+        py::arg("T"), py::arg("H"), py::arg("D"), py::arg("legacy") = false);
   m.def("symm_alloc", &symm_alloc);
   m.def("symm_open", &symm_open);
   m.def("symm_close", &symm_close);

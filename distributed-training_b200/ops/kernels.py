@@ -71,13 +71,15 @@ def xent_bwd(logits: torch.Tensor, targets: torch.Tensor, lse: torch.Tensor, gsc
     lib().xent_bwd(logits, targets.reshape(-1), lse, gscale.reshape(1).float())
 
 
-def attn_fwd(qkv: torch.Tensor, B: int, T: int, H: int, D: int):
-    """Returns (out [B*T, H*D] bf16, lse2 [B*H, T] fp32)."""
-    return lib().attn_fwd(qkv, B, T, H, D)
+def attn_fwd(qkv: torch.Tensor, B: int, T: int, H: int, D: int, legacy: bool = False):
+    """Returns (out [B*T, H*D] bf16, lse2 [B*H, T] fp32).  Head dim 64 uses the
+    tcgen05 kernel; ``legacy`` selects the warp-level mma.sync kernel."""
+    return lib().attn_fwd(qkv, B, T, H, D, legacy)
 
 
-def attn_bwd(qkv, out, dout, lse, B, T, H, D) -> torch.Tensor:
-    return lib().attn_bwd(qkv, out, dout, lse, B, T, H, D)
+def attn_bwd(qkv, out, dout, lse, B, T, H, D, legacy: bool = False) -> torch.Tensor:
+    """dqkv [B*T, 3*H*D]; head dim 64 uses the tcgen05 kernels unless ``legacy``."""
+    return lib().attn_bwd(qkv, out, dout, lse, B, T, H, D, legacy)
 
 
 def adamw_step(p, g, m, v, p16, lr, b1, b2, eps, wd, t, sq=None, max_norm=0.0) -> None:

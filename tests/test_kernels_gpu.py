@@ -131,21 +131,23 @@ def _attn_ref(qkv, B, T, H, D):
     return (p @ v).transpose(1, 2).reshape(B * T, H * D)
 
 
-@pytest.mark.parametrize("B,T,H,D", [(2, 64, 2, 64), (1, 100, 3, 64), (2, 256, 4, 64), (1, 192, 2, 128)])
-def test_attention(B, T, H, D):
+@pytest.mark.parametrize("legacy", [False, True])
+@pytest.mark.parametrize("B,T,H,D", [(2, 64, 2, 64), (1, 100, 3, 64), (2, 256, 4, 64), (1, 384, 2, 64),
+                                     (1, 1024, 2, 64), (1, 192, 2, 128)])
+def test_attention(B, T, H, D, legacy):
     qkv = torch.randn(B * T, 3 * H * D, device="cuda").bfloat16()
-    out, lse = K.attn_fwd(qkv, B, T, H, D)
+    out, lse = K.attn_fwd(qkv, B, T, H, D, legacy=legacy)
     qf = qkv.float().requires_grad_()
     ref = _attn_ref(qf, B, T, H, D)
     assert _rel(out, ref) < 2e-2
     dout = torch.randn(B * T, H * D, device="cuda").bfloat16()
     ref.backward(dout.float())
-    dqkv = K.attn_bwd(qkv, out, dout, lse, B, T, H, D)
+    dqkv = K.attn_bwd(qkv, out, dout, lse, B, T, H, D, legacy=legacy)
     g = qf.grad.view(B * T, 3, H * D)
     d = dqkv.view(B * T, 3, H * D)
     for i, name in enumerate("qkv"):
         assert _rel(d[:, i], g[:, i]) < 3e-2, name
-    dqkv2 = K.attn_bwd(qkv, out, dout, lse, B, T, H, D)
+    dqkv2 = K.attn_bwd(qkv, out, dout, lse, B, T, H, D, legacy=legacy)
     assert torch.equal(dqkv, dqkv2), "attention backward must be deterministic"
 
 
