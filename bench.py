@@ -25,6 +25,7 @@ prints the same JSON line with ``"impl": "reference"``.
 from __future__ import annotations
 
 import argparse
+import contextlib
 import csv
 import datetime
 import io
@@ -44,6 +45,15 @@ import torch  # noqa: E402
 METRIC = "GPT tokens/s at 1/2/4/8 B200 (DDP, ZeRO-1) vs ref NCCL; all-reduce busbw GB/s"
 MODEL = dict(vocab=50304, ctx=1024, dim=768, heads=12, layers=12)
 SEQ_PER_GPU = 16
+# BASELINE.json configs runnable with --config (the flagship is the default)
+CONFIGS = {
+    "gpt2-small-ddp": dict(model=MODEL, seq=SEQ_PER_GPU, mode="ddp", accum=1,
+                           name="GPT-2-small (12L, d768, 12H, ctx 1024, vocab 50304)"),
+    "gpt2-medium-zero": dict(model=dict(vocab=50304, ctx=1024, dim=1024, heads=16, layers=24), seq=8, mode="zero",
+                             accum=4, name="GPT-2-medium (24L, d1024, 16H, ctx 1024, vocab 50304), no_sync accum 4"),
+    "gpt-1.3b-zero": dict(model=dict(vocab=50304, ctx=2048, dim=2048, heads=16, layers=24), seq=4, mode="zero",
+                          accum=1, name="1.3B (24L, d2048, 16H, ctx 2048, vocab 50304)"),
+}
 BASELINE_VALUE = None  # BASELINE.md publishes no number for this config (CPU-only reference numbers)
 
 
@@ -130,19 +140,21 @@ def run_ours(a, rank, world, local):
         pg = NVLinkGroup(rank, world, dev, torch_exchange(), timeout=120.0)
     else:
         pg = NVLinkGroup(0, 1, dev, lambda k, p: [p], timeout=120.0)
-    args = T.parse(["--mode", "ddp", "--dtype", "bfloat16", "--batch", str(SEQ_PER_GPU), "--ctx", str(MODEL["ctx"]),
-                    "--dim", str(MODEL["dim"]), "--heads", str(MODEL["heads"]), "--layers", str(MODEL["layers"]),
+    C = CONFIGS[a.config]
+    M, seq, accum = C["model"], C["seq"], C["accum"]
+    args = T.parse(["--mode", C["mode"], "--dtype", "bfloat16", "--batch", str(seq), "--ctx", str(M["ctx"]),
+                    "--dim", str(M["dim"]), "--heads", str(M["heads"]), "--layers", str(M["layers"]),
                     "--lr", "6e-4", "--clip", "1.0", "--bucket-mb", str(a.bucket_mb), "--data", "synthetic",
-                    "--vocab", str(MODEL["vocab"]), "--algo", a.algo])
-    cfg = GPTConfig(dtype="bfloat16", **MODEL)
+                    "--vocab", str(M["vocab"]), "--algo", a.algo, "--accum", str(accum)])
+    cfg = GPTConfig(dtype="bfloat16", **M)
     tr = T.Trainer(args, cfg, dev, pg)
-    data = SyntheticData(MODEL["vocab"])
+    data = SyntheticData(M["vocab"])
     nb = a.warmup + a.steps
-    host = [data.rank_batch(s, 0, SEQ_PER_GPU, MODEL["ctx"], 0, rank, world) for s in range(nb)]
-    dev_batches = [(torch.from_numpy(x).to(dev), torch.from_numpy(y).to(dev)) for x, y in host]
+    host = [[data.rank_batch(s, mi, seq, M["ctx"], 0, rank, world) for mi in range(accum)] for s in range(nb)]
+    dev_batches = [[(torch.from_numpy(x).to(dev), torch.from_numpy(y).to(dev)) for x, y in hs] for hs in host]
 
     def device_step(i):  # inputs already resident: the kernel-side number
-        tr.step([[dev_batches[i % nb]]], return_loss=False)
+        tr.step([[mb] for mb in dev_batches[i % nb]], return_loss=False)
 
     for i in range(a.warmup):
         device_step(i)
@@ -162,22 +174,23 @@ def run_ours(a, rank, world, local):
 
     def e2e_step(i):
         s = a.warmup + i
-        losses.append(tr.step([[host[s % nb]]]))
+        losses.append(tr.step([[mb] for mb in host[s % nb]]))
 
     ms_e2e = _timed(e2e_step, a.steps, world)
     pg.check()
-    tokens = SEQ_PER_GPU * MODEL["ctx"] * world
+    tokens = seq * accum * M["ctx"] * world
     res = {
         "metric": METRIC, "value": tokens * a.steps / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
         "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms / a.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (iid uniform token ids, random-init weights)",
-        "config": {"model": "GPT-2-small (12L, d768, 12H, ctx 1024, vocab 50304)", "global_batch": SEQ_PER_GPU * world,
-                   "seq_len": MODEL["ctx"], "parallelism": f"dp{world}", "bucket_mb": a.bucket_mb,
+        "config": {"model": C["name"], "global_batch": seq * accum * world,
+                   "seq_len": M["ctx"], "parallelism": f"{'dp' if C['mode'] == 'ddp' else 'zero1-dp'}{world}",
+                   "grad_accum": accum, "bucket_mb": a.bucket_mb if C["mode"] == "ddp" else None,
                    "optimizer": "AdamW, clip 1.0", "allreduce_order": a.algo,
                    "l2": "no flush: weights/activations/logits per step >> 126 MB L2"},
         "e2e": {"value": tokens * a.steps / (ms_e2e / 1e3), "unit": "tokens/s",
-                "h2d_bytes_per_step": 2 * SEQ_PER_GPU * MODEL["ctx"] * 8, "d2h_bytes_per_step": 4,
+                "h2d_bytes_per_step": 2 * seq * accum * M["ctx"] * 8, "d2h_bytes_per_step": 4,
                 "ms_per_step": ms_e2e / a.steps, "final_loss": losses[-1] if losses else None},
         "gpu_launches": int(launches),
         "gpu_launches_per_step": launches / max(1, a.steps),
@@ -205,26 +218,40 @@ def run_reference(a, rank, world, local):
     torch.cuda.set_device(dev)
     if world > 1:
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
-    cfg = RefConfig(dtype="float32", **MODEL)
+    C = CONFIGS[a.config]
+    M, seq, accum = C["model"], C["seq"], C["accum"]
+    cfg = RefConfig(dtype="float32", **M)
     # random init with the reference's own initialiser (dtrain.nn.GPT), then its torch mirror
     from dtrain.nn import GPT as RefGPT
     model = TorchGPT.from_dtrain(RefGPT(cfg, seed=0)).to(dev)
     ddp = DistributedDataParallel(model, device_ids=[local], bucket_cap_mb=a.bucket_mb) if world > 1 else model
-    opt = torch.optim.AdamW(model.parameters(), lr=6e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+    adam = dict(lr=6e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+    if C["mode"] == "zero" and world > 1:
+        from torch.distributed.optim import ZeroRedundancyOptimizer
+        opt = ZeroRedundancyOptimizer(model.parameters(), optimizer_class=torch.optim.AdamW, **adam)
+    else:
+        opt = torch.optim.AdamW(model.parameters(), **adam)
     rng = np.random.default_rng([0, rank])
     nb = a.warmup + a.steps
-    host = [rng.integers(0, MODEL["vocab"], size=(SEQ_PER_GPU, MODEL["ctx"] + 1), dtype=np.int64) for _ in range(nb)]
-    pinned = [torch.from_numpy(h).pin_memory() for h in host]
-    dev_tokens = [p.to(dev) for p in pinned]
+    host = [[rng.integers(0, M["vocab"], size=(seq, M["ctx"] + 1), dtype=np.int64) for _ in range(accum)]
+            for _ in range(nb)]
+    pinned = [[torch.from_numpy(h).pin_memory() for h in hs] for hs in host]
+    dev_tokens = [[p.to(dev) for p in ps] for ps in pinned]
 
-    def step(tok, read_loss):
+    def step(toks, read_loss):
         opt.zero_grad(set_to_none=True)
-        with torch.autocast("cuda", dtype=torch.bfloat16):
-            _, loss = ddp(tok[:, :-1], tok[:, 1:])
-        loss.backward()
+        total = 0.0
+        for mi, tok in enumerate(toks):
+            last = mi == len(toks) - 1
+            ctx = ddp.no_sync() if (world > 1 and not last) else contextlib.nullcontext()
+            with ctx:
+                with torch.autocast("cuda", dtype=torch.bfloat16):
+                    _, loss = ddp(tok[:, :-1], tok[:, 1:])
+                (loss / len(toks)).backward()
+            total = total + loss.detach() / len(toks)
         torch.nn.utils.clip_grad_norm_(model.parameters(), 1.0)
         opt.step()
-        return float(loss.item()) if read_loss else None
+        return float(total.item()) if read_loss else None
 
     for i in range(a.warmup):
         step(dev_tokens[i], False)
@@ -233,19 +260,22 @@ def run_reference(a, rank, world, local):
         sampler.start()
     ms = _timed(lambda i: step(dev_tokens[a.warmup + i], False), a.steps, world)
     clocks = sampler.stop() if sampler else None
-    ms_e2e = _timed(lambda i: step(pinned[a.warmup + i].to(dev, non_blocking=True), True), a.steps, world)
-    tokens = SEQ_PER_GPU * MODEL["ctx"] * world
+    ms_e2e = _timed(lambda i: step([p.to(dev, non_blocking=True) for p in pinned[a.warmup + i]], True),
+                    a.steps, world)
+    tokens = seq * accum * M["ctx"] * world
     res = {
         "impl": "reference", "metric": METRIC, "value": tokens * a.steps / (ms / 1e3), "unit": "tokens/s",
         "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms / a.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (torch.autocast)",
         "data": "synthetic (iid uniform token ids, random-init weights)",
-        "config": {"model": "GPT-2-small (12L, d768, 12H, ctx 1024, vocab 50304)", "global_batch": SEQ_PER_GPU * world,
-                   "seq_len": MODEL["ctx"], "parallelism": f"dp{world}", "bucket_mb": a.bucket_mb,
-                   "stack": "dtrain.torch_ref.TorchGPT + torch DDP (NCCL) + torch.optim.AdamW + clip_grad_norm_",
+        "config": {"model": C["name"], "global_batch": seq * accum * world, "grad_accum": accum,
+                   "seq_len": M["ctx"], "parallelism": f"{'dp' if C['mode'] == 'ddp' else 'zero1-dp'}{world}",
+                   "bucket_mb": a.bucket_mb,
+                   "stack": "dtrain.torch_ref.TorchGPT + torch DDP (NCCL) + torch.optim.AdamW"
+                            + (" in ZeroRedundancyOptimizer" if C["mode"] == "zero" else "") + " + clip_grad_norm_",
                    "l2": "no flush: weights/activations/logits per step >> 126 MB L2"},
         "e2e": {"value": tokens * a.steps / (ms_e2e / 1e3), "unit": "tokens/s",
-                "h2d_bytes_per_step": SEQ_PER_GPU * (MODEL["ctx"] + 1) * 8, "d2h_bytes_per_step": 4,
+                "h2d_bytes_per_step": seq * accum * (M["ctx"] + 1) * 8, "d2h_bytes_per_step": 4,
                 "ms_per_step": ms_e2e / a.steps},
         "gpu_launches": 0,
         "clocks": clocks,
@@ -263,6 +293,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--bucket-mb", type=float, default=1.0)
     ap.add_argument("--algo", choices=["ring", "direct"], default="ring")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="gpt2-small-ddp")
     a = ap.parse_args()
     if a.warmup < 3:
         a.warmup = 3

@@ -135,23 +135,43 @@ __device__ __forceinline__ float reduce_elem(const Peers& in, long i, int W, int
   return acc;
 }
 
-// Vectorised fp32 path: 4 elements per thread per step.
+// Vectorised fp32 reduction of 4 elements starting at i.  With a compile-time
+// world size (WT > 0) every peer's load is issued before the first add, so a
+// thread keeps WT 16-byte loads in flight over NVLink (the loop is latency
+// bound otherwise); the adds still run in the fixed order first, first+1, ...
+template <int WT>
 __device__ __forceinline__ float4 reduce_vec4(const Peers& in, long i, int W, int first) {
-  int r = first;
-  float4 acc = __ldcg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(in.p[r]) + i));
-  for (int k = 1; k < W; ++k) {
-    r = (r + 1 == W) ? 0 : r + 1;
-    const float4 v = __ldcg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(in.p[r]) + i));
-    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+  if constexpr (WT > 0) {
+    float4 v[WT];
+#pragma unroll
+    for (int k = 0; k < WT; ++k) {
+      int r = first + k;
+      r -= (r >= WT) ? WT : 0;
+      v[k] = __ldcg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(in.p[r]) + i));
+    }
+    float4 acc = v[0];
+#pragma unroll
+    for (int k = 1; k < WT; ++k) {
+      acc.x += v[k].x; acc.y += v[k].y; acc.z += v[k].z; acc.w += v[k].w;
+    }
+    return acc;
+  } else {
+    int r = first;
+    float4 acc = __ldcg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(in.p[r]) + i));
+    for (int k = 1; k < W; ++k) {
+      r = (r + 1 == W) ? 0 : r + 1;
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(in.p[r]) + i));
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+    return acc;
   }
-  return acc;
 }
 
 // Reduce elements [a, b) into `out` (index space of the buffer), scaled.
 // If sq != nullptr, also accumulate sum of squares of the written values (fp64).
 // All ranks' buffers share one byte offset from 256-byte aligned bases, so they
 // have the same 16-byte phase; the vector loop runs when `out` shares it too.
-template <typename TI, typename TO>
+template <typename TI, typename TO, int WT = 0>
 __device__ __forceinline__ void reduce_range(const Peers& in, TO* out, long a, long b, int W, int first, float scale,
                                              double* sq) {
   double s = 0.0;
@@ -169,11 +189,26 @@ __device__ __forceinline__ void reduce_range(const Peers& in, TO* out, long a, l
       out[i] = v;
       s += (double)v * v;
     }
-    for (long i = head + threadIdx.x * 4; i < ve; i += (long)blockDim.x * 4) {
-      float4 v = reduce_vec4(in, i, W, first);
+    // two float4 per thread per iteration: 2*WT loads in flight
+    const long step = (long)blockDim.x * 4;
+    long i = head + threadIdx.x * 4;
+    for (; i + step < ve; i += 2 * step) {
+      float4 v0 = reduce_vec4<WT>(in, i, W, first);
+      float4 v1 = reduce_vec4<WT>(in, i + step, W, first);
+      v0.x *= scale; v0.y *= scale; v0.z *= scale; v0.w *= scale;
+      v1.x *= scale; v1.y *= scale; v1.z *= scale; v1.w *= scale;
+      *reinterpret_cast<float4*>(out + i) = v0;
+      *reinterpret_cast<float4*>(out + i + step) = v1;
+      if (sq) {
+        s += (double)v0.x * v0.x + (double)v0.y * v0.y + (double)v0.z * v0.z + (double)v0.w * v0.w;
+        s += (double)v1.x * v1.x + (double)v1.y * v1.y + (double)v1.z * v1.z + (double)v1.w * v1.w;
+      }
+    }
+    for (; i < ve; i += step) {
+      float4 v = reduce_vec4<WT>(in, i, W, first);
       v.x *= scale; v.y *= scale; v.z *= scale; v.w *= scale;
       *reinterpret_cast<float4*>(out + i) = v;
-      s += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
+      if (sq) s += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
     }
     for (long i = max(ve, head) + threadIdx.x; i < b; i += blockDim.x) {
       const float v = reduce_elem<TI>(in, i, W, first) * scale;
@@ -205,7 +240,18 @@ __device__ __forceinline__ void copy_range(const T* src, T* dst, long a, long b)
     for (long i = threadIdx.x; i < head; i += blockDim.x) d[i] = s[i];
     const uint4* sv = reinterpret_cast<const uint4*>(s + head);
     uint4* dv = reinterpret_cast<uint4*>(d + head);
-    for (long i = threadIdx.x; i < nv; i += blockDim.x) dv[i] = __ldcg(sv + i);
+    // four independent 16-byte loads per thread in flight
+    const long st = blockDim.x;
+    long i = threadIdx.x;
+    for (; i + 3 * st < nv; i += 4 * st) {
+      const uint4 x0 = __ldcg(sv + i), x1 = __ldcg(sv + i + st), x2 = __ldcg(sv + i + 2 * st),
+                  x3 = __ldcg(sv + i + 3 * st);
+      dv[i] = x0;
+      dv[i + st] = x1;
+      dv[i + 2 * st] = x2;
+      dv[i + 3 * st] = x3;
+    }
+    for (; i < nv; i += st) dv[i] = __ldcg(sv + i);
     for (long i = head + nv * 16 + threadIdx.x; i < nbytes; i += blockDim.x) d[i] = s[i];
   } else {
     for (long i = threadIdx.x; i < nbytes; i += blockDim.x) d[i] = s[i];
@@ -215,7 +261,7 @@ __device__ __forceinline__ void copy_range(const T* src, T* dst, long a, long b)
 // ---------------------------------------------------------------- kernels
 // One-shot all-reduce: every rank reduces the whole buffer from all peers (order
 // ORDER_RANK or ORDER_CYCLIC over the same chunking as the two-shot) into `out`.
-template <typename TI, typename TO>
+template <typename TI, typename TO, int WT>
 __global__ void __launch_bounds__(kCommThreads)
     allreduce_oneshot_kernel(CommCtx c, Peers in, TO* out, long n, int order, float scale) {
   if (!cta_barrier(c, c.epoch)) return;
@@ -223,7 +269,7 @@ __global__ void __launch_bounds__(kCommThreads)
     long lo, hi, a, b;
     chunk_bounds(n, c.world, ch, lo, hi);
     cta_slice(lo, hi, a, b);
-    reduce_range<TI, TO>(in, out, a, b, c.world, order == ORDER_CYCLIC ? ch : 0, scale, nullptr);
+    reduce_range<TI, TO, WT>(in, out, a, b, c.world, order == ORDER_CYCLIC ? ch : 0, scale, nullptr);
   }
   cta_barrier(c, c.epoch + 1);
 }
@@ -233,7 +279,7 @@ __global__ void __launch_bounds__(kCommThreads)
 // local input buffer).  in.p[rank] must be this rank's input; in-place is safe
 // because the owner only writes its own chunk, which peers do not read until the
 // middle barrier.
-template <typename T>
+template <typename T, int WT>
 __global__ void __launch_bounds__(kCommThreads)
     allreduce_twoshot_kernel(CommCtx c, Peers in, T* out, long n, int order, float scale) {
   if (!cta_barrier(c, c.epoch)) return;
@@ -241,7 +287,7 @@ __global__ void __launch_bounds__(kCommThreads)
   chunk_bounds(n, c.world, c.rank, lo, hi);
   cta_slice(lo, hi, a, b);
   T* mine = reinterpret_cast<T*>(in.p[c.rank]);
-  reduce_range<T, T>(in, mine, a, b, c.world, order == ORDER_CYCLIC ? c.rank : 0, scale, nullptr);
+  reduce_range<T, T, WT>(in, mine, a, b, c.world, order == ORDER_CYCLIC ? c.rank : 0, scale, nullptr);
   if (!cta_barrier(c, c.epoch + 1)) return;
   for (int k = 0; k < c.world; ++k) {
     const int p = (c.rank + k) % c.world;
@@ -260,7 +306,7 @@ __global__ void __launch_bounds__(kCommThreads)
 // dtrain's ring reduce-scatter with rotation, comm.py:310-316,342-362), scaled,
 // written to `out` (this rank's buffer index space).  With sq_part, each CTA also
 // writes the fp64 sum of squares of its slice to sq_part[blockIdx.x].
-template <typename TI, typename TO>
+template <typename TI, typename TO, int WT>
 __global__ void __launch_bounds__(kCommThreads)
     reduce_scatter_kernel(CommCtx c, Peers in, TO* out, long n, int order, float scale, double* sq_part) {
   __shared__ double red[kCommThreads / 32];
@@ -269,7 +315,8 @@ __global__ void __launch_bounds__(kCommThreads)
   chunk_bounds(n, c.world, c.rank, lo, hi);
   cta_slice(lo, hi, a, b);
   double s = 0.0;
-  reduce_range<TI, TO>(in, out, a, b, c.world, order == ORDER_CYCLIC ? c.rank : 0, scale, sq_part ? &s : nullptr);
+  reduce_range<TI, TO, WT>(in, out, a, b, c.world, order == ORDER_CYCLIC ? c.rank : 0, scale,
+                           sq_part ? &s : nullptr);
   if (sq_part) {
     // fixed-order block reduction
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
@@ -451,7 +498,7 @@ static Peers make_peers(const std::vector<int64_t>& ptrs, int64_t byte_offset) {
 
 static int comm_blocks(long bytes, int64_t want) {
   if (want > 0) return (int)std::min<int64_t>(want, kMaxCommBlocks);
-  const long per = 256 * 1024;  // ~256 KB per CTA before adding more CTAs
+  const long per = 64 * 1024;  // ~64 KB per CTA before adding more CTAs
   return (int)std::max<long>(1, std::min<long>(kMaxCommBlocks / 2, (bytes + per - 1) / per));
 }
 
@@ -467,12 +514,20 @@ int64_t allreduce(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::v
   const int nb = comm_blocks(n * esz, blocks);
   if (algo == 0) {  // one-shot, out-of-place
     TORCH_CHECK(out_ptr != 0, "allreduce one-shot needs an output buffer");
-    if (in_dtype == DT_F32 && out_dtype == DT_F32)
-      allreduce_oneshot_kernel<float, float><<<nb, kCommThreads, 0, st>>>(c, in, reinterpret_cast<float*>(out_ptr), n, (int)order, (float)scale);
-    else if (in_dtype == DT_BF16 && out_dtype == DT_F32)
-      allreduce_oneshot_kernel<bf16, float><<<nb, kCommThreads, 0, st>>>(c, in, reinterpret_cast<float*>(out_ptr), n, (int)order, (float)scale);
+    const int od = (int)order;
+    const float sc = (float)scale;
+    if (in_dtype == DT_F32 && out_dtype == DT_F32) {
+      auto* o = reinterpret_cast<float*>(out_ptr);
+      switch (c.world) {
+        case 2: allreduce_oneshot_kernel<float, float, 2><<<nb, kCommThreads, 0, st>>>(c, in, o, n, od, sc); break;
+        case 4: allreduce_oneshot_kernel<float, float, 4><<<nb, kCommThreads, 0, st>>>(c, in, o, n, od, sc); break;
+        case 8: allreduce_oneshot_kernel<float, float, 8><<<nb, kCommThreads, 0, st>>>(c, in, o, n, od, sc); break;
+        default: allreduce_oneshot_kernel<float, float, 0><<<nb, kCommThreads, 0, st>>>(c, in, o, n, od, sc);
+      }
+    } else if (in_dtype == DT_BF16 && out_dtype == DT_F32)
+      allreduce_oneshot_kernel<bf16, float, 0><<<nb, kCommThreads, 0, st>>>(c, in, reinterpret_cast<float*>(out_ptr), n, od, sc);
     else if (in_dtype == DT_BF16 && out_dtype == DT_BF16)
-      allreduce_oneshot_kernel<bf16, bf16><<<nb, kCommThreads, 0, st>>>(c, in, reinterpret_cast<bf16*>(out_ptr), n, (int)order, (float)scale);
+      allreduce_oneshot_kernel<bf16, bf16, 0><<<nb, kCommThreads, 0, st>>>(c, in, reinterpret_cast<bf16*>(out_ptr), n, od, sc);
     else
       TORCH_CHECK(false, "allreduce: unsupported dtype pair");
     count_launch();
@@ -481,10 +536,17 @@ int64_t allreduce(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::v
   }
   TORCH_CHECK(in_dtype == out_dtype, "allreduce two-shot: in/out dtypes must match");
   void* out = out_ptr ? reinterpret_cast<void*>(out_ptr) : in.p[rank];
-  if (in_dtype == DT_F32)
-    allreduce_twoshot_kernel<float><<<nb, kCommThreads, 0, st>>>(c, in, reinterpret_cast<float*>(out), n, (int)order, (float)scale);
-  else
-    allreduce_twoshot_kernel<bf16><<<nb, kCommThreads, 0, st>>>(c, in, reinterpret_cast<bf16*>(out), n, (int)order, (float)scale);
+  if (in_dtype == DT_F32) {
+    auto* o = reinterpret_cast<float*>(out);
+    switch (c.world) {
+      case 2: allreduce_twoshot_kernel<float, 2><<<nb, kCommThreads, 0, st>>>(c, in, o, n, (int)order, (float)scale); break;
+      case 4: allreduce_twoshot_kernel<float, 4><<<nb, kCommThreads, 0, st>>>(c, in, o, n, (int)order, (float)scale); break;
+      case 8: allreduce_twoshot_kernel<float, 8><<<nb, kCommThreads, 0, st>>>(c, in, o, n, (int)order, (float)scale); break;
+      default: allreduce_twoshot_kernel<float, 0><<<nb, kCommThreads, 0, st>>>(c, in, o, n, (int)order, (float)scale);
+    }
+  } else {
+    allreduce_twoshot_kernel<bf16, 0><<<nb, kCommThreads, 0, st>>>(c, in, reinterpret_cast<bf16*>(out), n, (int)order, (float)scale);
+  }
   count_launch();
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return 3;
@@ -499,10 +561,19 @@ int64_t reduce_scatter(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, s
   const int nb = comm_blocks(n * (dtype == DT_F32 ? 4 : 2), blocks);
   void* out = out_ptr ? reinterpret_cast<void*>(out_ptr) : in.p[rank];
   double* sq = reinterpret_cast<double*>(sq_part_ptr);
-  if (dtype == DT_F32)
-    reduce_scatter_kernel<float, float><<<nb, kCommThreads, 0, st>>>(c, in, reinterpret_cast<float*>(out), n, (int)order, (float)scale, sq);
-  else
-    reduce_scatter_kernel<bf16, bf16><<<nb, kCommThreads, 0, st>>>(c, in, reinterpret_cast<bf16*>(out), n, (int)order, (float)scale, sq);
+  if (dtype == DT_F32) {
+    auto* o = reinterpret_cast<float*>(out);
+    const int od = (int)order;
+    const float sc = (float)scale;
+    switch (c.world) {
+      case 2: reduce_scatter_kernel<float, float, 2><<<nb, kCommThreads, 0, st>>>(c, in, o, n, od, sc, sq); break;
+      case 4: reduce_scatter_kernel<float, float, 4><<<nb, kCommThreads, 0, st>>>(c, in, o, n, od, sc, sq); break;
+      case 8: reduce_scatter_kernel<float, float, 8><<<nb, kCommThreads, 0, st>>>(c, in, o, n, od, sc, sq); break;
+      default: reduce_scatter_kernel<float, float, 0><<<nb, kCommThreads, 0, st>>>(c, in, o, n, od, sc, sq);
+    }
+  } else {
+    reduce_scatter_kernel<bf16, bf16, 0><<<nb, kCommThreads, 0, st>>>(c, in, reinterpret_cast<bf16*>(out), n, (int)order, (float)scale, sq);
+  }
   count_launch();
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return 2;
