@@ -2,6 +2,8 @@
 #include <torch/extension.h>
 #include <atomic>
 
+#include "comm_engine.h"
+
 namespace dtb {
 
 static std::atomic<long long> g_launches{0};
@@ -124,5 +126,19 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("device_barrier", &device_barrier);
   m.def("zero_adamw_allgather", &zero_adamw_allgather);
   m.def("comm_max_blocks", &comm_max_blocks);
+  py::class_<CommEngine>(m, "CommEngine")
+      .def(py::init<int64_t, int64_t, std::vector<int64_t>, double, int64_t>())
+      .def("register_buffer", &CommEngine::register_buffer)
+      .def("forget_buffers", &CommEngine::forget_buffers)
+      .def("contains", &CommEngine::contains)
+      .def("peer_ptrs", &CommEngine::peer_ptrs)
+      .def("allreduce_inplace", &CommEngine::allreduce_inplace)
+      .def("reduce_scatter", &CommEngine::reduce_scatter)
+      .def("all_gather", &CommEngine::all_gather)
+      .def("barrier", &CommEngine::barrier)
+      .def("advance", &CommEngine::advance)
+      .def_property_readonly("epoch", &CommEngine::epoch)
+      .def_property("timeout", &CommEngine::timeout, &CommEngine::set_timeout)
+      .def_property_readonly("blocks", &CommEngine::blocks);
   m.def("comm_max_ranks", &comm_max_ranks);
 }

@@ -25,6 +25,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include "comm_engine.h"
 #include "common.cuh"
 
 namespace dtb {
@@ -32,6 +33,16 @@ namespace dtb {
 constexpr int kMaxRanks = 8;
 constexpr int kMaxCommBlocks = 128;
 constexpr int kCommThreads = 512;
+
+int64_t allreduce(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> bufs,
+                  int64_t byte_offset, int64_t n, int64_t in_dtype, int64_t out_ptr, int64_t out_dtype, int64_t algo,
+                  int64_t order, double scale, double timeout_s, int64_t blocks);
+int64_t reduce_scatter(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> bufs,
+                       int64_t byte_offset, int64_t n, int64_t dtype, int64_t out_ptr, int64_t order, double scale,
+                       int64_t sq_part_ptr, double timeout_s, int64_t blocks);
+int64_t all_gather(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> bufs,
+                   int64_t byte_offset, int64_t n, int64_t dtype, double timeout_s, int64_t blocks);
+int64_t device_barrier(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, double timeout_s);
 
 enum : int { ORDER_RANK = 0, ORDER_CYCLIC = 1 };
 enum : int { DT_F32 = 0, DT_BF16 = 1 };
@@ -638,6 +649,83 @@ int64_t zero_adamw_allgather(std::vector<int64_t> sigs, int64_t rank, int64_t ep
   count_launch();
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return 3;
+}
+
+// Native per-group state so a collective on a peer-mapped tensor costs one call
+// from Python: the registered buffers (every rank's base pointer), the signal
+// pads, the flag epoch counter and the timeout live here.
+CommEngine::CommEngine(int64_t rank, int64_t world, std::vector<int64_t> sigs, double timeout_s, int64_t blocks)
+    : rank_(rank), world_(world), sigs_(std::move(sigs)), timeout_(timeout_s), blocks_(blocks) {}
+
+int64_t CommEngine::register_buffer(std::vector<int64_t> ptrs, int64_t nbytes) {
+  TORCH_CHECK((int64_t)ptrs.size() == world_, "register_buffer: one pointer per rank expected");
+  bufs_.push_back(std::move(ptrs));
+  sizes_.push_back(nbytes);
+  return (int64_t)bufs_.size() - 1;
+}
+
+void CommEngine::forget_buffers() {
+  bufs_.clear();
+  sizes_.clear();
+}
+
+bool CommEngine::locate(const torch::Tensor& t, int64_t& id, int64_t& off) const {
+  const int64_t p = reinterpret_cast<int64_t>(t.data_ptr());
+  const int64_t nb = t.numel() * (int64_t)t.element_size();
+  for (size_t i = 0; i < bufs_.size(); ++i) {
+    const int64_t base = bufs_[i][rank_];
+    if (p >= base && p + nb <= base + sizes_[i]) {
+      id = (int64_t)i;
+      off = p - base;
+      return true;
+    }
+  }
+  return false;
+}
+
+bool CommEngine::contains(torch::Tensor t) const {
+  int64_t id, off;
+  return locate(t, id, off);
+}
+
+static int64_t dt_code(const torch::Tensor& t) {
+  if (t.scalar_type() == at::kFloat) return DT_F32;
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16, "NVLink collectives support float32 and bfloat16");
+  return DT_BF16;
+}
+
+void CommEngine::allreduce_inplace(torch::Tensor t, int64_t order, double scale) {
+  int64_t id, off;
+  TORCH_CHECK(t.is_contiguous() && locate(t, id, off), "allreduce_inplace: tensor is not in a registered buffer");
+  epoch_ += dtb::allreduce(sigs_, rank_, epoch_, bufs_[id], off, t.numel(), dt_code(t), 0, dt_code(t), 1, order,
+                           scale, timeout_, blocks_);
+}
+
+torch::Tensor CommEngine::reduce_scatter(torch::Tensor flat, int64_t order, double scale, int64_t sq_part_ptr,
+                                         int64_t blocks) {
+  int64_t id, off;
+  TORCH_CHECK(flat.is_contiguous() && locate(flat, id, off), "reduce_scatter: tensor is not in a registered buffer");
+  epoch_ += dtb::reduce_scatter(sigs_, rank_, epoch_, bufs_[id], off, flat.numel(), dt_code(flat), 0, order, scale,
+                                sq_part_ptr, timeout_, blocks > 0 ? blocks : blocks_);
+  const int64_t n = flat.numel(), base = n / world_, extra = n % world_;
+  const int64_t lo = rank_ * base + std::min(rank_, extra);
+  return flat.narrow(0, lo, base + (rank_ < extra ? 1 : 0));
+}
+
+void CommEngine::all_gather(torch::Tensor flat) {
+  int64_t id, off;
+  TORCH_CHECK(flat.is_contiguous() && locate(flat, id, off), "all_gather: tensor is not in a registered buffer");
+  epoch_ += dtb::all_gather(sigs_, rank_, epoch_, bufs_[id], off, flat.numel(), dt_code(flat), timeout_, blocks_);
+}
+
+void CommEngine::barrier() { epoch_ += dtb::device_barrier(sigs_, rank_, epoch_, timeout_); }
+
+std::vector<int64_t> CommEngine::peer_ptrs(torch::Tensor t) const {
+  int64_t id, off;
+  TORCH_CHECK(locate(t, id, off), "peer_ptrs: tensor is not in a registered buffer");
+  std::vector<int64_t> out(bufs_[id]);
+  for (auto& p : out) p += off;
+  return out;
 }
 
 int64_t comm_max_blocks() { return kMaxCommBlocks; }

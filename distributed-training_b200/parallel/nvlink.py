@@ -34,7 +34,9 @@ DT = {torch.float32: 0, torch.bfloat16: 1}
 ORDER_RANK, ORDER_CYCLIC = 0, 1
 ALGO_ONESHOT, ALGO_TWOSHOT = 0, 1
 _SIG_BYTES = 128 * 8 * 4  # [max CTAs][max ranks] uint32 flags
-_ONESHOT_MAX_BYTES = 1 << 20
+# "auto" picks one-shot only below this size: its out-of-place result costs a copy
+# back, and measured on 8 B200s the two-shot kernel was as fast down to 4 KB.
+_ONESHOT_MAX_BYTES = 0
 
 
 class SymmetricBuffer:
@@ -108,16 +110,17 @@ class NVLinkGroup:
             raise ValueError(f"NVLinkGroup supports up to {lib().comm_max_ranks()} ranks per node")
         self.rank, self.world = int(rank), int(world)
         self.device = torch.device(device)
-        self.timeout = float(timeout)
         self.blocks = int(blocks)
         self._exchange_fn = exchange
         self._nalloc = 0
         self.seq = 0            # collectives issued
-        self.epoch = 1          # next device flag epoch (identical on every rank)
         self.buffers: list[SymmetricBuffer] = []
+        self._eng = None
         with torch.cuda.device(self.device):
             lib().comm_status_clear()
             self._sig = self._new_buffer(_SIG_BYTES)
+            # native state: signal pads, registered buffers, flag epoch, timeout
+            self._eng = lib().CommEngine(self.rank, self.world, self._sig.ptrs, float(timeout), self.blocks)
             self.comm_stream = torch.cuda.Stream(device=self.device)
         self._staging: SymmetricBuffer | None = None
         self._sq_parts = None
@@ -125,12 +128,27 @@ class NVLinkGroup:
         self.synchronize()
 
     # ------------------------------------------------------------ plumbing
+    @property
+    def epoch(self) -> int:
+        """Next device flag epoch (advances identically on every rank)."""
+        return int(self._eng.epoch)
+
+    @property
+    def timeout(self) -> float:
+        return float(self._eng.timeout)
+
+    @timeout.setter
+    def timeout(self, t: float):
+        self._eng.timeout = float(t)
+
     def _exchange(self, key: str, payload: bytes) -> list[bytes]:
         return self._exchange_fn(key, payload)
 
     def _new_buffer(self, nbytes: int) -> SymmetricBuffer:
         b = SymmetricBuffer(self, nbytes)
         self.buffers.append(b)
+        if self._eng is not None:
+            self._eng.register_buffer(b.ptrs, b.nbytes)
         return b
 
     def alloc(self, numel: int, dtype: torch.dtype = torch.float32) -> torch.Tensor:
@@ -152,7 +170,7 @@ class NVLinkGroup:
         return self._sig.ptrs
 
     def _advance(self, used: int):
-        self.epoch += int(used)
+        self._eng.advance(int(used))
         self.seq += 1
 
     def _stage(self, nbytes: int) -> SymmetricBuffer:
@@ -197,6 +215,11 @@ class NVLinkGroup:
         nbytes = n * t.element_size()
         if method == "auto":
             method = "oneshot" if nbytes <= _ONESHOT_MAX_BYTES else "twoshot"
+        if method == "twoshot" and self._eng.contains(t):
+            # fast path: one native call, in place on the peer-mapped tensor
+            self._eng.allreduce_inplace(t, self._order(algo), scale)
+            self.seq += 1
+            return t
         buf, off = self._locate(t)
         staged = buf is None
         # one-shot writes out of place: it needs scratch for the result (and for the
@@ -229,13 +252,11 @@ class NVLinkGroup:
         n = flat.numel()
         b = partition(n, self.world)
         if self.world > 1:
-            buf, off = self._locate(flat)
-            if buf is None:
+            if not self._eng.contains(flat):
                 raise ValueError("reduce_scatter needs a tensor allocated with NVLinkGroup.alloc")
             sqp = sq_parts.data_ptr() if sq_parts is not None else 0
-            used = lib().reduce_scatter(self._sigs, self.rank, self.epoch, buf.ptrs, off, n, DT[flat.dtype], 0,
-                                        ORDER_CYCLIC, scale, sqp, self.timeout, self._rs_blocks())
-            self._advance(used)
+            self.seq += 1
+            return self._eng.reduce_scatter(flat, ORDER_CYCLIC, scale, sqp, self._rs_blocks())
         elif scale != 1.0:
             flat.mul_(scale)
         return flat[b[self.rank]:b[self.rank + 1]]
@@ -245,12 +266,10 @@ class NVLinkGroup:
 
     def all_gather(self, flat: torch.Tensor):
         if self.world > 1:
-            buf, off = self._locate(flat)
-            if buf is None:
+            if not self._eng.contains(flat):
                 raise ValueError("all_gather needs a tensor allocated with NVLinkGroup.alloc")
-            used = lib().all_gather(self._sigs, self.rank, self.epoch, buf.ptrs, off, flat.numel(), DT[flat.dtype],
-                                    self.timeout, self.blocks)
-            self._advance(used)
+            self._eng.all_gather(flat)
+            self.seq += 1
         return flat
 
     def broadcast(self, t: torch.Tensor, root: int = 0, cast_to: torch.Tensor | None = None):
@@ -279,8 +298,8 @@ class NVLinkGroup:
         return t
 
     def barrier(self):
-        used = lib().device_barrier(self._sigs, self.rank, self.epoch, self.timeout)
-        self._advance(used)
+        self._eng.barrier()
+        self.seq += 1
 
     def allreduce_async(self, t: torch.Tensor, algo: str = "ring", scale: float = 1.0,
                         method: str = "auto") -> GPUWork:
@@ -302,6 +321,8 @@ class NVLinkGroup:
         for b in self.buffers:
             b.free()
         self.buffers = []
+        if self._eng is not None:
+            self._eng.forget_buffers()
 
 
 def store_exchange(store, rank: int, world: int, prefix: str = ""):

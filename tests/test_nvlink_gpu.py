@@ -187,6 +187,59 @@ def test_peer_that_never_arrives_gives_commerror_not_a_hang():
     assert res[0][0] == "commerror" and res[0][2] == 20.0
 
 
+def _zero_vs_ddp(pg):
+    import torch
+    from dtrain_b200.models.gpt import GPT, GPTConfig
+    from dtrain_b200.ops import kernels as K
+    from dtrain_b200.ops.optim import AdamW
+    from dtrain_b200.parallel.ddp import DDP
+    from dtrain_b200.parallel.zero import ZeroAdamW
+    cfg = GPTConfig(vocab=512, ctx=128, dim=128, heads=2, layers=2, dtype="bfloat16")
+    g = torch.Generator().manual_seed(1)
+    batches = [(torch.randint(0, 512, (2 * pg.world, 128), generator=g),
+                torch.randint(0, 512, (2 * pg.world, 128), generator=g)) for _ in range(3)]
+    mine = [(x[2 * pg.rank:2 * pg.rank + 2].cuda(), y[2 * pg.rank:2 * pg.rank + 2].cuda()) for x, y in batches]
+    # DDP + flat AdamW with on-device clipping
+    md = GPT(cfg, seed=0)
+    ddp = DDP(md, pg, bucket_mb=0.05)
+    fp = md.flat
+    opt = AdamW([fp.master], lr=3e-3, work=[fp.work])
+    sq = torch.zeros(1, dtype=torch.float64, device=fp.master.device)
+    for x, y in mine:
+        md.zero_grad()
+        _, loss = md(x, y)
+        loss.backward()
+        ddp.finish()
+        K.grad_sqnorm(fp.grad, sq)
+        opt.step([fp.grad], sq_norm=sq, max_norm=1.0)
+    # ZeRO-1
+    mz = GPT(cfg, seed=0)
+    zero = ZeroAdamW(mz, pg, max_grad_norm=1.0, lr=3e-3)
+    for x, y in mine:
+        mz.zero_grad()
+        _, loss = mz(x, y)
+        loss.backward()
+        zero.step()
+    zero.gather_params()
+    pg.synchronize()
+    work_equal = bool(torch.equal(zero.fp.work, zero.fp.master.bfloat16()))
+    return ((fp.master - zero.flat).abs().max().item(), fp.master.abs().max().item(),
+            zero.state_bytes(), work_equal, zero.last_grad_norm)
+
+
+@needs2
+def test_zero1_matches_ddp_adamw_on_gpu():
+    res = _run(2, _zero_vs_ddp)
+    for diff, scale, state_bytes, work_equal, gnorm in res:
+        assert diff <= 1e-5 * max(1.0, scale), diff
+        assert work_equal, "bf16 working copy must equal the gathered fp32 masters"
+        assert gnorm > 0
+    from dtrain_b200.models.gpt import GPT, GPTConfig
+    n = sum(p.numel() for p in GPT(GPTConfig(vocab=512, ctx=128, dim=128, heads=2, layers=2,
+                                             dtype="bfloat16")).parameters())
+    assert sum(r[2] for r in res) == 8 * n  # fp32 m and v, sharded exactly once across ranks
+
+
 def _ddp_step(pg, bucket_mb):
     import torch
     from dtrain_b200.models.gpt import GPT, GPTConfig
