@@ -74,6 +74,8 @@ struct Bars {
   int abort_flag;
 };
 
+// 320 threads, one CTA per SM.  10 warps put 3 warps on some schedulers, so the
+// per-scheduler register file caps a thread at 168 registers.
 __global__ void __launch_bounds__(kThreads, 1)
     fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, bf16* __restrict__ out, float* __restrict__ lse2, int T,
                   int H, float sl2) {
@@ -89,7 +91,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int bh = blockIdx.y, b = bh / H, h = bh % H;
   const int C = H * D;
   const bool has_b = (2 * pair + 1) < nq;
-  const int last_kv[2] = {2 * pair, 2 * pair + 1};
+  // tile t (0 = A, 1 = B) is query tile 2*pair + t; its last (diagonal) key tile has the same index
   const int n_kv = has_b ? 2 * pair + 2 : 2 * pair + 1;
 
   if (threadIdx.x == 0) {
@@ -168,7 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t vbase = smem_u32(smem + OFF_V + s * TILE);
         for (int t = 0; t < 2; ++t) {
           if (t == 1 && !has_b) continue;
-          if (j > last_kv[t]) continue;
+          if (j > (2 * pair + t)) continue;
           if (!mbar_wait(&bars->p_full[t], j & 1, abort_flag)) { ok = false; break; }
           tc_fence_after();
           const uint32_t pbase = smem_u32(smem + OFF_P + t * PBYTES);
@@ -177,7 +179,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_mma_f16(tmem + TM_O + t * D, make_sw128_desc(pbase + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
                        make_sw128_desc(vbase + kk * 2048, 8192, 1024), id_pv, (j > 0 || kk > 0) ? 1u : 0u);
           tc_commit(&bars->o_done[t]);
-          if (j + 1 <= last_kv[t]) {
+          if (j + 1 <= (2 * pair + t)) {
             if (!next_k_ready) {
               const int s1 = (j + 1) % STAGES;
               if (!mbar_wait(&bars->k_full[s1], ((j + 1) / STAGES) & 1, abort_flag)) { ok = false; break; }
@@ -204,7 +206,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     if (active) {
-      for (int j = 0; j <= last_kv[t] && ok; ++j) {
+      for (int j = 0; j <= (2 * pair + t) && ok; ++j) {
         if (!mbar_wait(&bars->s_full[t], j & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
         uint32_t sr[128];
@@ -218,7 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(&bars->s_free[t]);
         // causal / length mask on the edge tiles, then the row max of the raw scores
         const int k0 = j * BKV;
-        const bool edge = (j == last_kv[t]) || (k0 + BKV > T);
+        const bool edge = (j == (2 * pair + t)) || (k0 + BKV > T);
         if (edge) {
           const int lim = min(qrow + 1, T) - k0;  // keys [k0, k0+lim) are visible
 #pragma unroll
@@ -277,14 +279,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // rescale this row of O when the running max moved (warp-uniform decision)
         if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-          uint32_t o[64];
-          tmem_ld32_issue(tmem + lane_off + TM_O + t * D, o);
-          tmem_ld32_issue(tmem + lane_off + TM_O + t * D + 32, o + 32);
-          tmem_wait_ld();
 #pragma unroll
-          for (int c = 0; c < 64; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-          tmem_st32(tmem + lane_off + TM_O + t * D, o);
-          tmem_st32(tmem + lane_off + TM_O + t * D + 32, o + 32);
+          for (int half = 0; half < 2; ++half) {
+            uint32_t o[32];
+            tmem_ld32_issue(tmem + lane_off + TM_O + t * D + half * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+            tmem_st32(tmem + lane_off + TM_O + t * D + half * 32, o);
+          }
           tmem_wait_st();
         }
         fence_proxy_async_smem();
@@ -293,7 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(&bars->p_full[t]);
       }
       // final: O / l
-      if (ok && mbar_wait(&bars->o_done[t], last_kv[t] & 1, abort_flag)) {
+      if (ok && mbar_wait(&bars->o_done[t], (2 * pair + t) & 1, abort_flag)) {
         tc_fence_after();
         uint32_t o[64];
         tmem_ld32_issue(tmem + lane_off + TM_O + t * D, o);
