@@ -656,6 +656,7 @@ void attn_fwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor lse, int64_
   TORCH_CHECK(qkv.is_contiguous() && qkv.scalar_type() == at::kBFloat16 && qkv.numel() == B * T * 3 * H * D,
               "attn_fwd_tc: qkv must be contiguous bf16 [B*T, 3*H*64]");
   c10::cuda::CUDAGuard guard(qkv.device());
+  bind_device_context(qkv.get_device());
   CUtensorMap m;
   const long rows = B * T, cols = 3 * H * D;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
@@ -700,6 +701,7 @@ void attn_bwd_tc(torch::Tensor qkv, torch::Tensor dout, torch::Tensor lse, torch
   using namespace attn_tc;
   TORCH_CHECK(dout.is_contiguous() && dout.numel() == B * T * H * D, "attn_bwd_tc: dout must be [B*T, H*64]");
   c10::cuda::CUDAGuard guard(qkv.device());
+  bind_device_context(qkv.get_device());
   CUtensorMap mq = attn_map(qkv, B * T, 3 * H * D);
   CUtensorMap md = attn_map(dout, B * T, H * D);
   static bool attr = false;

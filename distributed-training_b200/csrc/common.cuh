@@ -296,4 +296,18 @@ __device__ __forceinline__ float gelu_tanh_grad(float x) {
 // benchmark can report how many of its own kernels ran inside a timed region.
 void count_launch(int n = 1);
 
+// Makes `dev`'s primary context current on the calling host thread.  Driver-API
+// calls such as cuTensorMapEncodeTiled fail with CUDA_ERROR_INVALID_CONTEXT on a
+// thread that has none, and a fresh thread (PyTorch's autograd worker runs every
+// backward) gets one only from a runtime call that binds it: c10's device guard
+// skips cudaSetDevice when the index already matches.  cudaSetDevice binds the
+// primary context; it is called once per thread and device.
+inline void bind_device_context(int dev) {
+  thread_local unsigned long long bound = 0;
+  const unsigned long long bit = (dev >= 0 && dev < 64) ? (1ull << dev) : 0ull;
+  if (bit && (bound & bit)) return;
+  cudaSetDevice(dev);
+  bound |= bit;
+}
+
 }  // namespace dtb

@@ -544,6 +544,7 @@ void gemm(torch::Tensor a, bool a_trans, torch::Tensor b, bool b_trans, torch::T
   TORCH_CHECK(out.scalar_type() == (f32_out ? at::kFloat : at::kBFloat16), "gemm: wrong output dtype for epilogue");
   TORCH_CHECK(epi >= EPI_BF16 && epi <= EPI_F32, "gemm: unknown epilogue");
   c10::cuda::CUDAGuard guard(a.device());
+  bind_device_context(a.get_device());
 
   GemmArgs args{};
   args.M = (int)M;

@@ -35,6 +35,30 @@ _lock = threading.Lock()
 _lib = None
 
 
+def _shared_libstdcxx() -> list[str]:
+    """Linker input that binds the extension to the libstdc++ this process runs on.
+
+    A toolchain whose ``libstdc++.so`` link is missing silently links the static
+    ``libstdc++.a`` into the extension.  That private copy then mixes with the
+    process's shared libstdc++ (which already owns the iostream/locale objects), and
+    the first error message that formats a number (``TORCH_CHECK(..., n)``) crashes
+    with SIGSEGV instead of raising.  Naming the loaded ``libstdc++.so.6`` on the
+    link line resolves every C++ runtime symbol against it; the static archive the
+    driver appends afterwards then contributes nothing.
+    """
+    try:
+        with open("/proc/self/maps") as f:
+            for line in f:
+                path = line.split()[-1] if line.strip() else ""
+                if os.path.basename(path).startswith("libstdc++.so") and os.path.exists(path):
+                    return [path]
+    except OSError:
+        pass
+    import ctypes.util
+    name = ctypes.util.find_library("stdc++")
+    return [f"-l:{name}"] if name else []
+
+
 def build(verbose: bool = False):
     """Compile every CUDA source for sm_100a and return the loaded module."""
     from torch.utils import cpp_extension
@@ -46,6 +70,7 @@ def build(verbose: bool = False):
         build_directory=str(BUILD_DIR),
         extra_cflags=["-O3", "-std=c++17"],
         extra_cuda_cflags=CUDA_FLAGS,
+        extra_ldflags=_shared_libstdcxx(),
         verbose=verbose,
         with_cuda=True,
     )

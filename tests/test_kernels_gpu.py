@@ -151,6 +151,32 @@ def test_attention(B, T, H, D, legacy):
     assert torch.equal(dqkv, dqkv2), "attention backward must be deterministic"
 
 
+def test_kernels_from_a_fresh_host_thread():
+    """Autograd runs every backward on its own worker thread, which starts with no
+    CUDA context bound; TMA descriptor encoding (GEMM, tcgen05 attention) must work
+    there and give the same bits as on the main thread."""
+    import threading
+    x = torch.randn(300, 64, device="cuda").bfloat16()
+    w = torch.randn(256, 64, device="cuda").bfloat16()
+    qkv = torch.randn(128, 3 * 2 * 64, device="cuda").bfloat16()
+    main = (K.gemm(x, w, b_trans=True), K.attn_fwd(qkv, 1, 128, 2, 64)[0])
+    got = {}
+
+    def body():
+        try:
+            got["r"] = (K.gemm(x, w, b_trans=True), K.attn_fwd(qkv, 1, 128, 2, 64)[0])
+            torch.cuda.synchronize()
+        except BaseException as e:  # noqa: BLE001
+            got["e"] = e
+
+    t = threading.Thread(target=body)
+    t.start()
+    t.join()
+    assert "e" not in got, got.get("e")
+    for a, b in zip(main, got["r"]):
+        assert torch.equal(a, b)
+
+
 def test_embedding():
     B, T, V, C = 4, 64, 1000, 256
     idx = torch.randint(0, V, (B, T), device="cuda")
