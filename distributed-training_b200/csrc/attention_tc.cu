@@ -7,7 +7,7 @@
 //
 // One CTA = one (batch*head, pair of 128-query tiles A and B); the two tiles share
 // every K/V tile that both need.  10 warps:
-//   warp 0      TMA: Q_A, Q_B once; K_j, V_j through a 2-stage ring (128 keys x 64).
+//   warp 0      TMA: Q_A, Q_B once; K_j, V_j through 3-stage rings (128 keys x 64).
 //   warp 1      owns 512 TMEM columns (S_A, S_B: 128 each; O_A, O_B: 64 each); one
 //               lane issues  S_t = Q_t K_j^T  (M=128, N=128, K=64) and
 //               O_t += P_t V_j (M=128, N=64, K=128), committing to mbarriers.
@@ -17,8 +17,10 @@
 //               P = exp2(s*scale*log2e - m) as bf16 into 128B-swizzled shared memory
 //               (the K-major A operand of the PV MMA) and rescales its O row in
 //               TMEM when the running max moved.
-// While one tile's softmax runs, the MMA warp computes the other tile's scores, so
-// tensor-core and SIMT/SFU work overlap.  All waits are bounded (common.cuh).
+// A tile's next scores S_t(j+1) are computed while its softmax of step j runs (the
+// scores are copied to registers first), and its PV runs while the softmax of
+// step j+1 computes exponentials, so the softmax warps run back to back and the
+// tensor core hides behind them.  All waits are bounded (common.cuh).
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -36,7 +38,7 @@ constexpr int D = 64;
 constexpr int kThreads = 320;
 constexpr int TILE = BQ * D * 2;         // 16 KB: one Q, K or V tile
 constexpr int PBYTES = BQ * BKV * 2;     // 32 KB: one P tile (two 64-key swizzle atoms)
-constexpr int STAGES = 2;
+constexpr int STAGES = 3;
 constexpr int OFF_Q = 0;
 constexpr int OFF_K = OFF_Q + 2 * TILE;
 constexpr int OFF_V = OFF_K + STAGES * TILE;
@@ -66,9 +68,89 @@ __device__ __forceinline__ float ex2_fast(float x) {
   return y;
 }
 
+
+// ---------------------------------------------------------------- softmax math
+// Packed-FP32 (f32x2) and 3-input max instructions of sm_100: one instruction
+// does two FMAs / adds, or folds two values into a running max.
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+// (a0, a1) = (a0, a1) * (b0, b1) + (c0, c1)
+__device__ __forceinline__ void ffma2(float& a0, float& a1, float b0, float b1, float c0, float c1) {
+  asm("{\n\t.reg .b64 xa, xb, xc;\n\t"
+      "mov.b64 xa, {%0, %1};\n\tmov.b64 xb, {%2, %3};\n\tmov.b64 xc, {%4, %5};\n\t"
+      "fma.rn.f32x2 xa, xa, xb, xc;\n\tmov.b64 {%0, %1}, xa;\n\t}"
+      : "+f"(a0), "+f"(a1) : "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+// (a0, a1) += (b0, b1)
+__device__ __forceinline__ void fadd2(float& a0, float& a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 xa, xb;\n\t"
+      "mov.b64 xa, {%0, %1};\n\tmov.b64 xb, {%2, %3};\n\t"
+      "add.rn.f32x2 xa, xa, xb;\n\tmov.b64 {%0, %1}, xa;\n\t}"
+      : "+f"(a0), "+f"(a1) : "f"(b0), "f"(b1));
+}
+// (a0, a1) -= (b0, b1)
+__device__ __forceinline__ void fsub2(float& a0, float& a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 xa, xb;\n\t"
+      "mov.b64 xa, {%0, %1};\n\tmov.b64 xb, {%2, %3};\n\t"
+      "sub.rn.f32x2 xa, xa, xb;\n\tmov.b64 {%0, %1}, xa;\n\t}"
+      : "+f"(a0), "+f"(a1) : "f"(b0), "f"(b1));
+}
+
+// 2^x for x <= 9 on the FMA pipe, two values at a time, so part of the softmax
+// exponentials leave the special-function unit (the forward's bottleneck).
+// Range reduction x = n + f with n = rint(x) from the 1.5*2^23 shifter and
+// f in [-0.5, 0.5]; 2^f from a degree-3 polynomial whose coefficients were fitted
+// here by the Remez exchange algorithm on the relative error (max 7.5e-5, well
+// under bf16's 2^-9); 2^n is added to the exponent field.  x is clamped at -126
+// so the exponent never wraps: masked (-inf) scores give 2^-126 ~ 1e-38.
+__device__ __forceinline__ void exp2_poly2(float& x0, float& x1) {
+  constexpr float kShift = 12582912.f;  // 1.5 * 2^23
+  constexpr float c0 = 0.99992805719f, c1 = 0.69326096773f, c2 = 0.24261112511f, c3 = 0.05517166853f;
+  x0 = fmaxf(x0, -126.f);
+  x1 = fmaxf(x1, -126.f);
+  float j0 = x0, j1 = x1;
+  fadd2(j0, j1, kShift, kShift);    // low mantissa bits of j hold rint(x)
+  float n0 = j0, n1 = j1;
+  fsub2(n0, n1, kShift, kShift);    // rint(x)
+  float f0 = x0, f1 = x1;
+  fsub2(f0, f1, n0, n1);            // f = x - rint(x)
+  float p0 = c3, p1 = c3;
+  ffma2(p0, p1, f0, f1, c2, c2);
+  ffma2(p0, p1, f0, f1, c1, c1);
+  ffma2(p0, p1, f0, f1, c0, c0);
+  // bits(j) << 23 == rint(x) << 23 (the shifter's own bits leave the word)
+  x0 = __int_as_float(__float_as_int(p0) + __float_as_int(j0) * 8388608);
+  x1 = __int_as_float(__float_as_int(p1) + __float_as_int(j1) * 8388608);
+}
+
+// bf16x2 pack of two non-negative finite floats with integer rounding (half up)
+// on the integer pipe instead of the conversion unit.
+__device__ __forceinline__ uint32_t pack_bf16x2_pos(float lo, float hi) {
+  const uint32_t a = __float_as_uint(lo) + 0x8000u, b = __float_as_uint(hi) + 0x8000u;
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, 0x7632;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+#ifndef DTB_ATTN_POLY_EVERY
+#define DTB_ATTN_POLY_EVERY 0
+#endif
+#ifndef DTB_ATTN_PACK_INT
+#define DTB_ATTN_PACK_INT 0
+#endif
+// One pair of columns in every kPolyEvery uses exp2_poly2 (0: none) and kPackInt
+// selects the integer bf16 packing.  Measured on B200 (B=16, T=1024, H=12): with
+// exponentials, packing and stores fused in one pass the plain ex2 + cvt version
+// is fastest (94 us; 1/4 polynomial 98 us, 1/2 polynomial 105 us), so both are off.
+constexpr int kPolyEvery = DTB_ATTN_POLY_EVERY;
+constexpr bool kPackInt = DTB_ATTN_PACK_INT != 0;
+
 struct Bars {
   uint64_t q_full;
-  uint64_t k_full[STAGES], v_full[STAGES], kv_empty[STAGES];
+  uint64_t k_full[STAGES], v_full[STAGES], k_empty[STAGES], v_empty[STAGES];
   uint64_t s_full[2], s_free[2], p_full[2], o_done[2];
   uint32_t tmem_slot;
   int abort_flag;
@@ -99,7 +181,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&bars->k_full[s], 1);
       mbar_init(&bars->v_full[s], 1);
-      mbar_init(&bars->kv_empty[s], 1);
+      mbar_init(&bars->k_empty[s], 1);
+      mbar_init(&bars->v_empty[s], 1);
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&bars->s_full[t], 1);
@@ -127,9 +210,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < n_kv; ++j) {
         const int s = j % STAGES;
         const uint32_t ph = (j / STAGES) & 1;
-        if (!mbar_wait(&bars->kv_empty[s], ph ^ 1, abort_flag)) break;
+        // K and V stages are released separately: K_j once its scores are computed,
+        // V_j once its PV products are, so the next keys stream in early
+        if (!mbar_wait(&bars->k_empty[s], ph ^ 1, abort_flag)) break;
         mbar_arrive_expect_tx(&bars->k_full[s], TILE);
         tma_load_2d(&tmQKV, smem + OFF_K + s * TILE, &bars->k_full[s], C + h * D, row_base + j * BKV);
+        if (!mbar_wait(&bars->v_empty[s], ph ^ 1, abort_flag)) break;
         mbar_arrive_expect_tx(&bars->v_full[s], TILE);
         tma_load_2d(&tmQKV, smem + OFF_V + s * TILE, &bars->v_full[s], 2 * C + h * D, row_base + j * BKV);
       }
@@ -137,9 +223,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------------------------------------------------------- MMA
-      // Order: QK_A(0) QK_B(0) | PV_A(0) QK_A(1) | PV_B(0) QK_B(1) | PV_A(1) QK_A(2) | ...
-      // Each tile's next scores are issued right after its PV, so the tensor core
-      // works on one tile while the other tile's softmax runs.
+      // Per key tile j:  QK_A(j+1) QK_B(j+1) | PV_A(j) PV_B(j).
+      // A tile's next scores are issued as soon as its softmax has copied the
+      // current scores out of TMEM (s_free), so they are ready when that softmax
+      // finishes and the softmax warps never wait on the tensor core for scores.
       constexpr uint32_t id_qk = make_idesc_bf16(BQ, BKV, false, false);
       constexpr uint32_t id_pv = make_idesc_bf16(BQ, D, false, true);
       bool ok = mbar_wait(&bars->q_full, 0, abort_flag);
@@ -161,12 +248,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         ok = issue_qk(0, 0);
         if (ok && has_b) ok = issue_qk(1, 0);
+        if (ok) tc_commit(&bars->k_empty[0]);
       }
       for (int j = 0; j < n_kv && ok; ++j) {
         const int s = j % STAGES;
         const uint32_t ph = (j / STAGES) & 1;
+        // next scores of every tile that still has key tile j+1
+        if (j + 1 < n_kv) {
+          const int s1 = (j + 1) % STAGES;
+          if (!mbar_wait(&bars->k_full[s1], ((j + 1) / STAGES) & 1, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          for (int t = 0; t < 2 && ok; ++t) {
+            if (t == 1 && !has_b) continue;
+            if (j + 1 > (2 * pair + t)) continue;
+            ok = issue_qk(t, j + 1);
+          }
+          if (!ok) break;
+          tc_commit(&bars->k_empty[s1]);
+        }
         if (!mbar_wait(&bars->v_full[s], ph, abort_flag)) { ok = false; break; }
-        bool next_k_ready = false;
         const uint32_t vbase = smem_u32(smem + OFF_V + s * TILE);
         for (int t = 0; t < 2; ++t) {
           if (t == 1 && !has_b) continue;
@@ -179,18 +279,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_mma_f16(tmem + TM_O + t * D, make_sw128_desc(pbase + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
                        make_sw128_desc(vbase + kk * 2048, 8192, 1024), id_pv, (j > 0 || kk > 0) ? 1u : 0u);
           tc_commit(&bars->o_done[t]);
-          if (j + 1 <= (2 * pair + t)) {
-            if (!next_k_ready) {
-              const int s1 = (j + 1) % STAGES;
-              if (!mbar_wait(&bars->k_full[s1], ((j + 1) / STAGES) & 1, abort_flag)) { ok = false; break; }
-              tc_fence_after();
-              next_k_ready = true;
-            }
-            if (!issue_qk(t, j + 1)) { ok = false; break; }
-          }
         }
         if (!ok) break;
-        tc_commit(&bars->kv_empty[s]);
+        tc_commit(&bars->v_empty[s]);
       }
     }
   } else {
@@ -229,13 +320,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < BKV; c += 4) {
-          mx0 = fmaxf(mx0, __uint_as_float(sr[c]));
-          mx1 = fmaxf(mx1, __uint_as_float(sr[c + 1]));
-          mx2 = fmaxf(mx2, __uint_as_float(sr[c + 2]));
-          mx3 = fmaxf(mx3, __uint_as_float(sr[c + 3]));
+        for (int c = 0; c < BKV; c += 8) {
+          mx0 = max3f(mx0, __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
+          mx1 = max3f(mx1, __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
+          mx2 = max3f(mx2, __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
+          mx3 = max3f(mx3, __uint_as_float(sr[c + 6]), __uint_as_float(sr[c + 7]));
         }
-        const float mcand = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2;
+        const float mcand = fmaxf(max3f(mx0, mx1, mx2), mx3) * sl2;
         // Lazy rescaling: the reference max only moves when the new scores exceed it
         // by more than 2^8; P values stay <= 256, exact in the fp32 sum and fine in bf16.
         float alpha = 1.f;
@@ -245,38 +336,44 @@ __global__ void __launch_bounds__(kThreads, 1)
           alpha = ex2_fast(m - mcand);
           m = mcand;
         }
-        const float base = (m == -INFINITY) ? 0.f : m;
-        float rs0 = 0.f, rs1 = 0.f, rs2 = 0.f, rs3 = 0.f;
-#pragma unroll
-        for (int c = 0; c < BKV; c += 4) {
-          const float p0 = ex2_fast(fmaf(__uint_as_float(sr[c]), sl2, -base));
-          const float p1 = ex2_fast(fmaf(__uint_as_float(sr[c + 1]), sl2, -base));
-          const float p2 = ex2_fast(fmaf(__uint_as_float(sr[c + 2]), sl2, -base));
-          const float p3 = ex2_fast(fmaf(__uint_as_float(sr[c + 3]), sl2, -base));
-          sr[c] = __float_as_uint(p0);
-          sr[c + 1] = __float_as_uint(p1);
-          sr[c + 2] = __float_as_uint(p2);
-          sr[c + 3] = __float_as_uint(p3);
-          rs0 += p0;
-          rs1 += p1;
-          rs2 += p2;
-          rs3 += p3;
-        }
-        l = l * alpha + ((rs0 + rs1) + (rs2 + rs3));
-        // the previous PV must be done before P is overwritten and O rescaled
+        const float nb = (m == -INFINITY) ? 0.f : -m;
+        // the previous PV must be done before P is overwritten and O rescaled; it was
+        // issued when this tile's previous P was published, so this rarely waits
         if (j > 0 && !mbar_wait(&bars->o_done[t], (j - 1) & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        // P row -> shared memory (K-major, 128B swizzle, two 64-key atoms)
+        // exponentials, row sum and the bf16 P row (K-major, 128B swizzle, two 64-key
+        // atoms) in one pass of 8-column chunks, so the special-function unit (ex2),
+        // the integer pipe (packing) and the shared-memory stores run concurrently
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
 #pragma unroll
         for (int ch = 0; ch < BKV / 8; ++ch) {
+          float x[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) x[e] = __uint_as_float(sr[ch * 8 + e]);
+#pragma unroll
+          for (int e = 0; e < 8; e += 2) ffma2(x[e], x[e + 1], sl2, sl2, nb, nb);
+#pragma unroll
+          for (int e = 0; e < 8; e += 2) {
+            if (kPolyEvery > 0 && (((ch * 8 + e) >> 1) % (kPolyEvery > 0 ? kPolyEvery : 1)) == kPolyEvery - 1) {
+              exp2_poly2(x[e], x[e + 1]);
+            } else {
+              x[e] = ex2_fast(x[e]);
+              x[e + 1] = ex2_fast(x[e + 1]);
+            }
+          }
+          fadd2(s0, s1, x[0], x[1]);
+          fadd2(s2, s3, x[2], x[3]);
+          fadd2(s0, s1, x[4], x[5]);
+          fadd2(s2, s3, x[6], x[7]);
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            w[e] = kPackInt ? pack_bf16x2_pos(x[2 * e], x[2 * e + 1]) : pack_bf16x2(x[2 * e], x[2 * e + 1]);
           const int atom = ch >> 3, k16 = ch & 7;
-          uint4 u;
-          u.x = pack_bf16x2(__uint_as_float(sr[ch * 8 + 0]), __uint_as_float(sr[ch * 8 + 1]));
-          u.y = pack_bf16x2(__uint_as_float(sr[ch * 8 + 2]), __uint_as_float(sr[ch * 8 + 3]));
-          u.z = pack_bf16x2(__uint_as_float(sr[ch * 8 + 4]), __uint_as_float(sr[ch * 8 + 5]));
-          u.w = pack_bf16x2(__uint_as_float(sr[ch * 8 + 6]), __uint_as_float(sr[ch * 8 + 7]));
-          *reinterpret_cast<uint4*>(P + atom * 16384 + r * 128 + ((k16 ^ (r & 7)) << 4)) = u;
+          *reinterpret_cast<uint4*>(P + atom * 16384 + r * 128 + ((k16 ^ (r & 7)) << 4)) =
+              make_uint4(w[0], w[1], w[2], w[3]);
         }
+        l = l * alpha + ((s0 + s1) + (s2 + s3));
         // rescale this row of O when the running max moved (warp-uniform decision)
         if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
@@ -328,77 +425,43 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // =============================================================================
-// Backward.  Two deterministic kernels (no atomics), 6 warps each:
-//   warp 0 TMA, warp 1 MMA (+ 256 TMEM columns), warps 2..5 element-wise math with
-//   one 128-wide tile row per thread.  TMEM holds X (128 columns, reused for the
-//   scores and then for dP) and the fp32 gradient accumulators.  Shared memory
-//   (~97 KB) lets two CTAs share an SM, so one CTA's tensor work overlaps the
-//   other's element-wise phase.
+// Backward.  Two deterministic kernels (no atomics) with the forward's layout:
+// 10 warps, one CTA per SM, two 128-row sub-tiles A and B per CTA whose tensor
+// work and element-wise work interleave (while one sub-tile's warps compute
+// exponentials, the tensor core runs the other's products).
+//   warp 0      TMA: the four fixed tiles, then the streamed tiles through
+//               2-stage rings (one ring per streamed operand).
+//   warp 1      owns 512 TMEM columns: X_t (128, scores and then dP) and the fp32
+//               gradient accumulators; one lane issues every tcgen05.mma.
+//   warps 2..5  element-wise math of sub-tile A, warps 6..9 of sub-tile B: one
+//               query row per thread (the TMEM lane), so lse and delta are scalars.
 //
-// dK/dV kernel: CTA = (batch*head, 128-key tile j); loops over query tiles i >= j:
-//   X = K Q_i^T (S^T) -> P^T = exp2(S^T*scale*log2e - lse2[q])          (regs, bf16)
-//   X = V dO_i^T (dP^T);  dV += P^T dO_i                                   (MMA)
-//   dS^T = P^T * (dP^T - delta[q]);  dK += dS^T Q_i                         (MMA)
-// dQ kernel: CTA = (batch*head, 128-query tile i); loops over key tiles j <= i:
-//   X = Q K_j^T -> P;  X = dO V_j^T -> dS = P*(dP - delta);  dQ += dS K_j
+// dK/dV kernel: CTA = (batch*head, pair of 128-key tiles kA=2p, kB=2p+1); loops
+// over query tiles i >= kA (sub-tile B starts at i = kB):
+//   X_t = Q_i K_t^T -> P = exp2(S*scale*log2e - lse2[q])  (regs; bf16 P -> smem)
+//   X_t = dO_i V_t^T (dP);  dV_t += P^T dO_i   (A = P read MN-major)
+//   dS = P * (dP - delta[q])  (bf16 -> smem);  dK_t += dS^T Q_i
+// dQ kernel: CTA = (batch*head, pair of 128-query tiles), loops over key tiles j:
+//   X_t = Q_t K_j^T -> P;  X_t = dO_t V_j^T -> dS = P*(dP - delta);  dQ_t += dS K_j
+// Reference math: dtrain/autograd.py:226-252 (attention backward).
 // =============================================================================
-constexpr int BW_THREADS = 192;
-constexpr int BW_OFF_A = 0;                 // tile 0 (K for dkdv, Q for dq)
-constexpr int BW_OFF_B = TILE;              // tile 1 (V for dkdv, dO for dq)
-constexpr int BW_OFF_C = 2 * TILE;          // streamed tile (Q_i for dkdv, K_j for dq)
-constexpr int BW_OFF_D = 3 * TILE;          // streamed tile (dO_i for dkdv, V_j for dq)
-constexpr int BW_OFF_P = 4 * TILE;          // bf16 A operand: P^T then dS^T (dkdv), dS (dq)
-constexpr int BW_OFF_LD = BW_OFF_P + PBYTES;  // [2][2][128] fp32 lse2 / delta (dkdv)
-constexpr int BW_OFF_BAR = BW_OFF_LD + 2 * 2 * 128 * 4;
-constexpr int BW_SMEM = BW_OFF_BAR + 256 + 1024;
-constexpr uint32_t BW_X = 0, BW_G0 = 128, BW_G1 = 192;  // TMEM columns
+constexpr int BW_THREADS = 320;
+constexpr int BW_OFF_F = 0;                     // fixed tiles [t][2]: dkdv K_t, V_t; dq Q_t, dO_t
+constexpr int BW_OFF_S0 = 4 * TILE;             // streamed ring 0 [2]: dkdv Q_i; dq K_j
+constexpr int BW_OFF_S1 = 6 * TILE;             // streamed ring 1 [2]: dkdv dO_i; dq V_j
+constexpr int BW_OFF_P = 8 * TILE;              // [t] bf16 P then dS (128 query rows x 128 keys)
+constexpr int BW_OFF_BAR = BW_OFF_P + 2 * PBYTES;
+constexpr int BW_SMEM = BW_OFF_BAR + 512 + 1024;
+constexpr uint32_t BW_X = 0, BW_G = 256;        // X_t at t*128; G0_t at 256 + t*128, G1_t at 256 + t*128 + 64
 
 struct BwBars {
-  uint64_t fixed_full;                 // the two per-CTA tiles
-  uint64_t c_full, c_empty, d_full, d_empty;
-  uint64_t s_full, dp_full, ew_p, ew_ds, done;
+  uint64_t fixed_full;
+  uint64_t s0_full[2], s0_empty[2], s1_full[2], s1_empty[2];
+  uint64_t s_full[2], x_free[2], p_ready[2], dp_full[2], pv_done[2], ds_ready[2], ds_done[2];
+  uint64_t done;
   uint32_t tmem_slot;
   int abort_flag;
 };
-
-__device__ __forceinline__ void bw_init(BwBars* b) {
-  mbar_init(&b->fixed_full, 1);
-  mbar_init(&b->c_full, 1);
-  mbar_init(&b->c_empty, 1);
-  mbar_init(&b->d_full, 1);
-  mbar_init(&b->d_empty, 1);
-  mbar_init(&b->s_full, 1);
-  mbar_init(&b->dp_full, 1);
-  mbar_init(&b->ew_p, 4);
-  mbar_init(&b->ew_ds, 4);
-  mbar_init(&b->done, 1);
-  b->abort_flag = 0;
-  fence_barrier_init();
-}
-
-// Write 32 bf16-packed pairs (64 values) of this thread's row into the K-major
-// 128B-swizzled A-operand tile at columns [c0, c0+64) (c0 multiple of 64).
-__device__ __forceinline__ void put_row64(uint8_t* A, int r, int c0, const uint32_t* pk) {
-  const int atom = c0 >> 6;
-#pragma unroll
-  for (int k16 = 0; k16 < 8; ++k16) {
-    uint4 u = make_uint4(pk[k16 * 4 + 0], pk[k16 * 4 + 1], pk[k16 * 4 + 2], pk[k16 * 4 + 3]);
-    *reinterpret_cast<uint4*>(A + atom * 16384 + r * 128 + ((k16 ^ (r & 7)) << 4)) = u;
-  }
-}
-
-__device__ __forceinline__ float bf_lo(uint32_t p) { return __uint_as_float(p << 16); }
-__device__ __forceinline__ float bf_hi(uint32_t p) { return __uint_as_float(p & 0xffff0000u); }
-
-// Write 16 bf16-packed pairs (32 values) at columns [c0, c0+32) (c0 multiple of 32).
-__device__ __forceinline__ void put_row32(uint8_t* A, int r, int c0, const uint32_t* pk) {
-  const int atom = c0 >> 6, k0 = (c0 & 63) >> 3;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    uint4 u = make_uint4(pk[i * 4 + 0], pk[i * 4 + 1], pk[i * 4 + 2], pk[i * 4 + 3]);
-    *reinterpret_cast<uint4*>(A + atom * 16384 + r * 128 + (((k0 + i) ^ (r & 7)) << 4)) = u;
-  }
-}
 
 // Load 64 fp32 TMEM columns of this thread's row (every lane must call: the load
 // is warp-collective) and, when `store` is set, write them scaled as bf16.
@@ -419,8 +482,24 @@ __device__ __forceinline__ void store_row64(uint32_t taddr, bf16* dst, float sca
   }
 }
 
+__device__ __forceinline__ float bf_lo(uint32_t p) { return __uint_as_float(p << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t p) { return __uint_as_float(p & 0xffff0000u); }
+
+// Write this thread's 128-key bf16 row (64 packed words) into a [128 rows][128 keys]
+// tile laid out as two 128B-swizzled 64-key atoms: the K-major A operand of dQ
+// (M = queries) and, read with the MN-major descriptor, the A operand P^T / dS^T
+// of dV / dK (M = keys).
+__device__ __forceinline__ void put_row128(uint8_t* A, int r, const uint32_t* pk) {
+#pragma unroll
+  for (int ch = 0; ch < 16; ++ch) {
+    const int atom = ch >> 3, k16 = ch & 7;
+    *reinterpret_cast<uint4*>(A + atom * 16384 + r * 128 + ((k16 ^ (r & 7)) << 4)) =
+        make_uint4(pk[ch * 4 + 0], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
+  }
+}
+
 template <bool DKDV>
-__global__ void __launch_bounds__(BW_THREADS, 2)
+__global__ void __launch_bounds__(BW_THREADS, 1)
     bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_constant__ CUtensorMap tmDO,
                   const float* __restrict__ lse2, const float* __restrict__ delta, bf16* __restrict__ dqkv, int T,
                   int H, float sl2, float scale) {
@@ -430,21 +509,42 @@ __global__ void __launch_bounds__(BW_THREADS, 2)
   volatile int* abort_flag = &bars->abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nt = (T + 127) / 128;
-  // dkdv: heavy (low) key tiles first; dq: heavy (high) query tiles first
-  const int tile = DKDV ? (int)blockIdx.x : nt - 1 - (int)blockIdx.x;
+  const int npairs = (nt + 1) / 2;
+  // dkdv: low key pairs have the most query tiles; dq: high query pairs the most key tiles
+  const int pair = DKDV ? (int)blockIdx.x : npairs - 1 - (int)blockIdx.x;
   const int bh = blockIdx.y, b = bh / H, h = bh % H;
   const int C = H * D;
   const int row_base = b * T;
-  const int it0 = DKDV ? tile : 0;            // streamed tile range
-  const int it1 = DKDV ? nt - 1 : tile;
-  const int n_it = it1 - it0 + 1;
+  const bool has_b = 2 * pair + 1 < nt;
+  // streamed tile range [s_lo, s_hi]; sub-tile t is active for s in [lo_t, hi_t]
+  const int s_lo = DKDV ? 2 * pair : 0;
+  const int s_hi = DKDV ? nt - 1 : (has_b ? 2 * pair + 1 : 2 * pair);
+  auto lo_of = [&](int t) { return DKDV ? 2 * pair + t : 0; };
+  auto hi_of = [&](int t) { return DKDV ? nt - 1 : 2 * pair + t; };
+  auto active = [&](int t, int s) { return (t == 0 || has_b) && s >= lo_of(t) && s <= hi_of(t); };
 
   if (threadIdx.x == 0) {
-    bw_init(bars);
+    mbar_init(&bars->fixed_full, 1);
+    for (int k = 0; k < 2; ++k) {
+      mbar_init(&bars->s0_full[k], 1);
+      mbar_init(&bars->s0_empty[k], 1);
+      mbar_init(&bars->s1_full[k], 1);
+      mbar_init(&bars->s1_empty[k], 1);
+      mbar_init(&bars->s_full[k], 1);
+      mbar_init(&bars->x_free[k], 4);
+      mbar_init(&bars->p_ready[k], 4);
+      mbar_init(&bars->dp_full[k], 1);
+      mbar_init(&bars->pv_done[k], 1);
+      mbar_init(&bars->ds_ready[k], 4);
+      mbar_init(&bars->ds_done[k], 1);
+    }
+    mbar_init(&bars->done, 1);
+    bars->abort_flag = 0;
+    fence_barrier_init();
     tma_prefetch_desc(&tmQKV);
     tma_prefetch_desc(&tmDO);
   }
-  if (warp == 1) tmem_alloc(&bars->tmem_slot, 256);
+  if (warp == 1) tmem_alloc(&bars->tmem_slot, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -453,173 +553,237 @@ __global__ void __launch_bounds__(BW_THREADS, 2)
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------------------------ TMA
-      mbar_arrive_expect_tx(&bars->fixed_full, 2 * TILE);
-      if (DKDV) {  // K_j, V_j
-        tma_load_2d(&tmQKV, smem + BW_OFF_A, &bars->fixed_full, C + h * D, row_base + tile * 128);
-        tma_load_2d(&tmQKV, smem + BW_OFF_B, &bars->fixed_full, 2 * C + h * D, row_base + tile * 128);
-      } else {     // Q_i, dO_i
-        tma_load_2d(&tmQKV, smem + BW_OFF_A, &bars->fixed_full, h * D, row_base + tile * 128);
-        tma_load_2d(&tmDO, smem + BW_OFF_B, &bars->fixed_full, h * D, row_base + tile * 128);
+      const int nfixed = has_b ? 2 : 1;
+      mbar_arrive_expect_tx(&bars->fixed_full, nfixed * 2 * TILE);
+      for (int t = 0; t < nfixed; ++t) {
+        const int row = row_base + (2 * pair + t) * 128;
+        uint8_t* f = smem + BW_OFF_F + t * 2 * TILE;
+        if (DKDV) {  // K_t, V_t
+          tma_load_2d(&tmQKV, f, &bars->fixed_full, C + h * D, row);
+          tma_load_2d(&tmQKV, f + TILE, &bars->fixed_full, 2 * C + h * D, row);
+        } else {     // Q_t, dO_t
+          tma_load_2d(&tmQKV, f, &bars->fixed_full, h * D, row);
+          tma_load_2d(&tmDO, f + TILE, &bars->fixed_full, h * D, row);
+        }
       }
-      for (int it = 0; it < n_it; ++it) {
-        const int s = it0 + it;
-        if (!mbar_wait(&bars->c_empty, (it & 1) ^ 1, abort_flag)) break;
-        mbar_arrive_expect_tx(&bars->c_full, TILE);
-        if (DKDV) tma_load_2d(&tmQKV, smem + BW_OFF_C, &bars->c_full, h * D, row_base + s * 128);          // Q_i
-        else tma_load_2d(&tmQKV, smem + BW_OFF_C, &bars->c_full, C + h * D, row_base + s * 128);           // K_j
-        if (!mbar_wait(&bars->d_empty, (it & 1) ^ 1, abort_flag)) break;
-        mbar_arrive_expect_tx(&bars->d_full, TILE);
-        if (DKDV) tma_load_2d(&tmDO, smem + BW_OFF_D, &bars->d_full, h * D, row_base + s * 128);           // dO_i
-        else tma_load_2d(&tmQKV, smem + BW_OFF_D, &bars->d_full, 2 * C + h * D, row_base + s * 128);       // V_j
+      for (int s = s_lo; s <= s_hi; ++s) {
+        const int it = s - s_lo, st = it & 1;
+        const uint32_t ph = ((it >> 1) & 1) ^ 1;
+        const int row = row_base + s * 128;
+        if (!mbar_wait(&bars->s0_empty[st], ph, abort_flag)) break;
+        mbar_arrive_expect_tx(&bars->s0_full[st], TILE);
+        if (DKDV) tma_load_2d(&tmQKV, smem + BW_OFF_S0 + st * TILE, &bars->s0_full[st], h * D, row);       // Q_i
+        else tma_load_2d(&tmQKV, smem + BW_OFF_S0 + st * TILE, &bars->s0_full[st], C + h * D, row);        // K_j
+        if (!mbar_wait(&bars->s1_empty[st], ph, abort_flag)) break;
+        mbar_arrive_expect_tx(&bars->s1_full[st], TILE);
+        if (DKDV) tma_load_2d(&tmDO, smem + BW_OFF_S1 + st * TILE, &bars->s1_full[st], h * D, row);        // dO_i
+        else tma_load_2d(&tmQKV, smem + BW_OFF_S1 + st * TILE, &bars->s1_full[st], 2 * C + h * D, row);   // V_j
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ------------------------------------------------------------------ MMA
-      constexpr uint32_t id_s = make_idesc_bf16(128, 128, false, false);  // X = A0 * C^T  (both K-major)
-      constexpr uint32_t id_g = make_idesc_bf16(128, D, false, true);     // G += P * (MN-major B)
-      const uint32_t A0 = smem_u32(smem + BW_OFF_A), A1 = smem_u32(smem + BW_OFF_B);
-      const uint32_t SC = smem_u32(smem + BW_OFF_C), SD = smem_u32(smem + BW_OFF_D);
+      constexpr uint32_t id_s = make_idesc_bf16(128, 128, false, false);           // X = A . B^T, both K-major
+      constexpr uint32_t id_g = make_idesc_bf16(128, D, DKDV, true);                // G += P(^T) . (MN-major B)
+      const uint32_t F = smem_u32(smem + BW_OFF_F);
+      const uint32_t S0 = smem_u32(smem + BW_OFF_S0), S1 = smem_u32(smem + BW_OFF_S1);
       const uint32_t SP = smem_u32(smem + BW_OFF_P);
-      bool ok = mbar_wait(&bars->fixed_full, 0, abort_flag);
-      for (int it = 0; it < n_it && ok; ++it) {
-        const uint32_t ph = it & 1;
-        // X = A0 . C^T   (dkdv: K Q_i^T = S^T ; dq: Q K_j^T = S)
-        if (!mbar_wait(&bars->c_full, ph, abort_flag)) { ok = false; break; }
-        tc_fence_after();
+      // X_t = (dkdv) streamed . fixed^T  /  (dq) fixed . streamed^T   (M = queries)
+      auto issue_x = [&](int t, uint32_t fixed_tile, uint32_t streamed_tile) {
+        const uint32_t a = DKDV ? streamed_tile : fixed_tile, bb = DKDV ? fixed_tile : streamed_tile;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
-          tc_mma_f16(tmem + BW_X, make_sw128_desc(A0 + kk * 32, 16, 1024), make_sw128_desc(SC + kk * 32, 16, 1024),
-                     id_s, kk > 0 ? 1u : 0u);
-        tc_commit(&bars->s_full);
-        // element-wise phase 1 done: X free, P (dkdv: P^T in smem) ready
-        if (!mbar_wait(&bars->ew_p, ph, abort_flag)) { ok = false; break; }
-        if (!mbar_wait(&bars->d_full, ph, abort_flag)) { ok = false; break; }
-        tc_fence_after();
-        // X = A1 . D^T   (dkdv: V dO_i^T = dP^T ; dq: dO V_j^T = dP)
+          tc_mma_f16(tmem + BW_X + t * 128, make_sw128_desc(a + kk * 32, 16, 1024),
+                     make_sw128_desc(bb + kk * 32, 16, 1024), id_s, kk > 0 ? 1u : 0u);
+      };
+      // G_t(col) += A(P or dS of sub-tile t) . B (streamed tile, MN-major)
+      auto issue_g = [&](int t, uint32_t col, uint32_t btile, bool acc) {
+        const uint32_t pa = SP + t * PBYTES;
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          tc_mma_f16(tmem + BW_X, make_sw128_desc(A1 + kk * 32, 16, 1024), make_sw128_desc(SD + kk * 32, 16, 1024),
-                     id_s, kk > 0 ? 1u : 0u);
-        if (DKDV) {
-          // dV += P^T . dO_i   (A = P^T smem, B = dO_i MN-major)
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            tc_mma_f16(tmem + BW_G1, make_sw128_desc(SP + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
-                       make_sw128_desc(SD + kk * 2048, 8192, 1024), id_g, (it > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t ad = DKDV ? make_sw128_desc(pa + kk * 2048, 16384, 1024)           // A = P^T / dS^T (MN-major)
+                                   : make_sw128_desc(pa + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);  // A = dS
+          tc_mma_f16(tmem + col, ad, make_sw128_desc(btile + kk * 2048, 8192, 1024), id_g, (acc || kk > 0) ? 1u : 0u);
         }
-        tc_commit(&bars->dp_full);
-        tc_commit(&bars->d_empty);
-        if (!mbar_wait(&bars->ew_ds, ph, abort_flag)) { ok = false; break; }
+      };
+      bool ok = mbar_wait(&bars->fixed_full, 0, abort_flag);
+      if (ok) ok = mbar_wait(&bars->s0_full[0], 0, abort_flag);
+      if (ok) {
         tc_fence_after();
-        // dkdv: dK += dS^T . Q_i (B = Q_i MN-major);  dq: dQ += dS . K_j (B = K_j MN-major)
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          tc_mma_f16(tmem + BW_G0, make_sw128_desc(SP + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
-                     make_sw128_desc(SC + kk * 2048, 8192, 1024), id_g, (it > 0 || kk > 0) ? 1u : 0u);
-        tc_commit(&bars->c_empty);
+        for (int t = 0; t < 2; ++t)
+          if (active(t, s_lo)) {
+            issue_x(t, F + t * 2 * TILE, S0);
+            tc_commit(&bars->s_full[t]);
+          }
+      }
+      for (int s = s_lo; s <= s_hi && ok; ++s) {
+        const int it = s - s_lo, st = it & 1;
+        const uint32_t ph = (it >> 1) & 1;
+        const uint32_t s0 = S0 + st * TILE, s1 = S1 + st * TILE;
+        if (!mbar_wait(&bars->s1_full[st], ph, abort_flag)) { ok = false; break; }
+        // dP_t = dO . V^T into X_t once the element-wise warps have read the scores
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (!active(t, s)) continue;
+          const uint32_t k = (uint32_t)(s - lo_of(t));
+          if (!mbar_wait(&bars->x_free[t], k & 1, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          issue_x(t, F + t * 2 * TILE + TILE, s1);
+          tc_commit(&bars->dp_full[t]);
+        }
+        if (!ok) break;
+        if (DKDV) {  // dV_t += P^T dO_i
+          for (int t = 0; t < 2 && ok; ++t) {
+            if (!active(t, s)) continue;
+            const uint32_t k = (uint32_t)(s - lo_of(t));
+            if (!mbar_wait(&bars->p_ready[t], k & 1, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+            issue_g(t, BW_G + t * 128 + 64, s1, k > 0);
+            tc_commit(&bars->pv_done[t]);
+          }
+          if (!ok) break;
+        }
+        tc_commit(&bars->s1_empty[st]);
+        // dK_t += dS^T Q_i  /  dQ_t += dS K_j, then the next scores of sub-tile t
+        // (a sub-tile that starts at s+1 gets its first scores here too)
+        bool next_ready = false;
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (active(t, s)) {
+            const uint32_t k = (uint32_t)(s - lo_of(t));
+            if (!mbar_wait(&bars->ds_ready[t], k & 1, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+            issue_g(t, BW_G + t * 128, s0, k > 0);
+            tc_commit(&bars->ds_done[t]);
+          }
+          if (s + 1 <= s_hi && active(t, s + 1)) {
+            const int st1 = (it + 1) & 1;
+            if (!next_ready) {
+              if (!mbar_wait(&bars->s0_full[st1], ((it + 1) >> 1) & 1, abort_flag)) { ok = false; break; }
+              tc_fence_after();
+              next_ready = true;
+            }
+            issue_x(t, F + t * 2 * TILE, S0 + st1 * TILE);
+            tc_commit(&bars->s_full[t]);
+          }
+        }
+        if (!ok) break;
+        tc_commit(&bars->s0_empty[st]);
       }
       if (ok) tc_commit(&bars->done);
     }
   } else {
     // --------------------------------------------------------- element-wise
+    const int t = (warp - 2) >> 2;
     const int q = warp & 3;
-    const int r = q * 32 + lane;               // tile row (= TMEM lane)
+    const int r = q * 32 + lane;                     // tile row = query row = TMEM lane
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-    uint8_t* A = smem + BW_OFF_P;
-    float* LD = reinterpret_cast<float*>(smem + BW_OFF_LD);  // [slot][lse|delta][128]
+    uint8_t* A = smem + BW_OFF_P + t * PBYTES;
     const float* lb = lse2 + (long)bh * T;
     const float* db = delta + (long)bh * T;
-    const int my_row = tile * 128 + r;         // dkdv: key index; dq: query index
-    float my_lse = 0.f, my_delta = 0.f;
-    if (!DKDV && my_row < T) {
-      my_lse = lb[my_row];
-      my_delta = db[my_row];
-    }
+    const uint32_t xcol = BW_X + t * 128;
     bool ok = true;
-    for (int it = 0; it < n_it && ok; ++it) {
-      const uint32_t ph = it & 1;
-      const int s = it0 + it;                  // streamed tile index
-      float* Lsl = LD + (it & 1) * 256;
-      if (DKDV) {
-        const int qi = s * 128 + r;
-        Lsl[r] = qi < T ? lb[qi] : 0.f;
-        Lsl[128 + r] = qi < T ? db[qi] : 0.f;
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-      }
-      // ---- phase 1: P (dkdv: P^T) from the scores
-      if (!mbar_wait(&bars->s_full, ph, abort_flag)) { ok = false; break; }
-      tc_fence_after();
-      uint32_t pk[64];  // this row's P as bf16 pairs
-      // visibility: dkdv row = key kr, column = query qc: visible iff kr <= qc < T
-      //             dq   row = query qr, column = key kc:   visible iff kc <= qr, kc < T
-      const bool edge = (s == tile) || (s * 128 + 128 > T);
+    if (t == 0 || has_b) {
+      const int lo = lo_of(t), hi = hi_of(t);
+      // lse / delta of this thread's query row; dkdv rows change with the streamed tile
+      float my_lse = 0.f, my_delta = 0.f;
+      auto load_ld = [&](int qi, float& l, float& d) {
+        l = qi < T ? lb[qi] : 0.f;
+        d = qi < T ? db[qi] : 0.f;
+      };
+      if (DKDV) load_ld(lo * 128 + r, my_lse, my_delta);
+      else load_ld((2 * pair + t) * 128 + r, my_lse, my_delta);
+      for (int s = lo; s <= hi && ok; ++s) {
+        const uint32_t k = (uint32_t)(s - lo);
+        const int qrow = (DKDV ? s : 2 * pair + t) * 128 + r;   // query index within the sequence
+        const int kbase = (DKDV ? 2 * pair + t : s) * 128;       // first key of the tile
+        float nl = 0.f, nd = 0.f;
+        if (DKDV && s < hi) load_ld(qrow + 128, nl, nd);        // prefetch the next rows' statistics
+        // ---- phase 1: P = exp2(S*scale*log2e - lse)
+        if (!mbar_wait(&bars->s_full[t], k & 1, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        // keys [kbase, kbase + lim) are visible to this query (none for rows past T)
+        const int lim = qrow < T ? min(qrow + 1, T) - kbase : 0;
+        const bool need_mask = __any_sync(0xffffffffu, lim < 128);
+        const float nb = -my_lse;
+        uint32_t pk[64];
 #pragma unroll
-      for (int ch = 0; ch < 4; ++ch) {
-        uint32_t x[32];
-        tmem_ld32_issue(tmem + lane_off + BW_X + ch * 32, x);
-        tmem_wait_ld();
-#pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          float pv[2];
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int col = ch * 32 + c + e;
-            const float lse_v = DKDV ? Lsl[col] : my_lse;
-            float p = ex2_fast(fmaf(__uint_as_float(x[c + e]), sl2, -lse_v));
-            if (edge) {
-              const int gc = s * 128 + col;
-              const bool vis = DKDV ? (gc >= my_row && gc < T) : (gc <= my_row && gc < T);
-              if (!vis) p = 0.f;
-            }
-            pv[e] = p;
+        for (int ch = 0; ch < 4; ++ch) {  // 32 columns per TMEM load keeps P + one chunk in registers
+          uint32_t x[32];
+          tmem_ld32_issue(tmem + lane_off + xcol + ch * 32, x);
+          tmem_wait_ld();
+          if (ch == 3) {  // scores read: X_t may take dP
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->x_free[t]);
           }
-          pk[ch * 16 + c / 2] = pack_bf16x2(pv[0], pv[1]);
-        }
-      }
-      if (DKDV) {  // P^T is the A operand of dV += P^T dO
+          if (need_mask) {
 #pragma unroll
-        for (int ch = 0; ch < 4; ++ch) put_row32(A, r, ch * 32, pk + ch * 16);
+            for (int c = 0; c < 32; ++c)
+              if (ch * 32 + c >= lim) x[c] = __float_as_uint(-INFINITY);
+          }
+#pragma unroll
+          for (int c = 0; c < 32; c += 2) {
+            float p0 = __uint_as_float(x[c]), p1 = __uint_as_float(x[c + 1]);
+            ffma2(p0, p1, sl2, sl2, nb, nb);
+            pk[ch * 16 + (c >> 1)] = pack_bf16x2(ex2_fast(p0), ex2_fast(p1));
+          }
+        }
+        if (DKDV) {  // P is the A operand of dV += P^T dO: the previous dS must have been consumed
+          if (k > 0 && !mbar_wait(&bars->ds_done[t], (k - 1) & 1, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          put_row128(A, r, pk);
+          fence_proxy_async_smem();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars->p_ready[t]);
+        }
+        // ---- phase 2: dS = P * (dP - delta), in place over the packed P
+        if (!mbar_wait(&bars->dp_full[t], k & 1, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) {
+          uint32_t x[32];
+          tmem_ld32_issue(tmem + lane_off + xcol + ch * 32, x);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; c += 2) {
+            const uint32_t pp = pk[ch * 16 + c / 2];
+            float d0 = __uint_as_float(x[c]), d1 = __uint_as_float(x[c + 1]);
+            fsub2(d0, d1, my_delta, my_delta);
+            pk[ch * 16 + c / 2] = pack_bf16x2(bf_lo(pp) * d0, bf_hi(pp) * d1);
+          }
+        }
+        // the dS tile overwrites P: dkdv waits for dV (P^T dO), dq for the previous dQ
+        if (DKDV) {
+          if (!mbar_wait(&bars->pv_done[t], k & 1, abort_flag)) { ok = false; break; }
+        } else if (k > 0 && !mbar_wait(&bars->ds_done[t], (k - 1) & 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        put_row128(A, r, pk);
         fence_proxy_async_smem();
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->ew_p);
-      // ---- phase 2: dS = P * (dP - delta)
-      if (!mbar_wait(&bars->dp_full, ph, abort_flag)) { ok = false; break; }
-      tc_fence_after();
-#pragma unroll
-      for (int ch = 0; ch < 4; ++ch) {
-        uint32_t x[32], ds[16];
-        tmem_ld32_issue(tmem + lane_off + BW_X + ch * 32, x);
-        tmem_wait_ld();
-#pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          const uint32_t pp = pk[ch * 16 + c / 2];
-          const int col = ch * 32 + c;
-          const float d0 = DKDV ? Lsl[128 + col] : my_delta;
-          const float d1 = DKDV ? Lsl[128 + col + 1] : my_delta;
-          ds[c / 2] = pack_bf16x2(bf_lo(pp) * (__uint_as_float(x[c]) - d0),
-                                  bf_hi(pp) * (__uint_as_float(x[c + 1]) - d1));
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars->ds_ready[t]);
+        if (DKDV) {
+          my_lse = nl;
+          my_delta = nd;
         }
-        put_row32(A, r, ch * 32, ds);
       }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->ew_ds);
-    }
-    // ---- results
-    if (ok && mbar_wait(&bars->done, 0, abort_flag)) {
-      tc_fence_after();
-      const bool st = my_row < T;
-      const long ld = 3L * C;
-      bf16* rowp = dqkv + ((long)row_base + (st ? my_row : 0)) * ld;
-      if (DKDV) {
-        store_row64(tmem + lane_off + BW_G0, rowp + C + h * D, scale, st);      // dK
-        store_row64(tmem + lane_off + BW_G1, rowp + 2 * C + h * D, 1.f, st);    // dV
-      } else {
-        store_row64(tmem + lane_off + BW_G0, rowp + h * D, scale, st);          // dQ
+      // ---- results
+      if (ok && mbar_wait(&bars->done, 0, abort_flag)) {
+        tc_fence_after();
+        const int row = (2 * pair + t) * 128 + r;  // dkdv: key; dq: query
+        const bool st = row < T;
+        const long ld = 3L * C;
+        bf16* rowp = dqkv + ((long)row_base + (st ? row : 0)) * ld;
+        const uint32_t g = tmem + lane_off + BW_G + t * 128;
+        if (DKDV) {
+          store_row64(g, rowp + C + h * D, scale, st);            // dK
+          store_row64(g + 64, rowp + 2 * C + h * D, 1.f, st);     // dV
+        } else {
+          store_row64(g, rowp + h * D, scale, st);                // dQ
+        }
       }
     }
   }
@@ -627,7 +791,7 @@ __global__ void __launch_bounds__(BW_THREADS, 2)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -711,7 +875,7 @@ void attn_bwd_tc(torch::Tensor qkv, torch::Tensor dout, torch::Tensor lse, torch
     attr = true;
   }
   const int nt = (int)((T + 127) / 128);
-  dim3 grid((unsigned)nt, (unsigned)(B * H));
+  dim3 grid((unsigned)((nt + 1) / 2), (unsigned)(B * H));
   const float scale = 0.125f;                               // 1/sqrt(64)
   const float sl2 = (float)(1.4426950408889634 / 8.0);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
