@@ -14,7 +14,8 @@
 // Backward is deterministic (no atomics): one kernel owns a key tile and
 // accumulates dK, dV over the query tiles that see it; a second kernel owns a
 // query tile and accumulates dQ over its key tiles.  Both recompute P from the
-// saved log-sum-exp.  delta = rowsum(dO * O) is computed once by a small kernel.
+// saved log-sum-exp.  delta = rowsum(dO * O) is computed once by a small kernel (the head-dim-64
+// tcgen05 path computes it inside its dQ kernel instead).
 //
 // Tensor-core path: warp-level mma.sync m16n8k16 (bf16 in, fp32 accumulate).
 #include <torch/extension.h>
@@ -527,8 +528,8 @@ std::vector<torch::Tensor> attn_fwd(torch::Tensor qkv, int64_t B, int64_t T, int
 }
 
 // Returns dqkv [B*T, 3*H*D] bf16.
-void attn_bwd_tc(torch::Tensor qkv, torch::Tensor dout, torch::Tensor lse, torch::Tensor delta, torch::Tensor dqkv,
-                 int64_t B, int64_t T, int64_t H);
+void attn_bwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torch::Tensor lse, torch::Tensor delta,
+                 torch::Tensor dqkv, int64_t B, int64_t T, int64_t H);
 
 // Head dim 64 runs the tcgen05 backward kernels (attention_tc.cu) unless `legacy`.
 torch::Tensor attn_bwd(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torch::Tensor lse, int64_t B,
@@ -540,13 +541,7 @@ torch::Tensor attn_bwd(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout,
     c10::cuda::CUDAGuard guard(qkv.device());
     auto dqkv = torch::empty_like(qkv);
     auto delta = torch::empty({B * H, T}, qkv.options().dtype(at::kFloat));
-    const long warps = B * T * H;
-    attn::delta_kernel<64><<<(unsigned)((warps * 32 + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-        reinterpret_cast<const bf16*>(out.data_ptr()), reinterpret_cast<const bf16*>(dout.data_ptr()),
-        delta.data_ptr<float>(), (int)B, (int)T, (int)H);
-    count_launch();
-    C10_CUDA_KERNEL_LAUNCH_CHECK();
-    attn_bwd_tc(qkv, dout, lse, delta, dqkv, B, T, H);
+    attn_bwd_tc(qkv, out.contiguous(), dout, lse, delta, dqkv, B, T, H);
     return dqkv;
   }
   TORCH_CHECK(dout.is_contiguous() && dout.scalar_type() == at::kBFloat16 && dout.numel() == B * T * H * D,

@@ -457,7 +457,7 @@ constexpr uint32_t BW_X = 0, BW_G = 256;        // X_t at t*128; G0_t at 256 + t
 struct BwBars {
   uint64_t fixed_full;
   uint64_t s0_full[2], s0_empty[2], s1_full[2], s1_empty[2];
-  uint64_t s_full[2], x_free[2], p_ready[2], dp_full[2], pv_done[2], ds_ready[2], ds_done[2];
+  uint64_t s_full[2], x_free[2], p_ready[2], dp_full[2], pv_done[2], x_free2[2], ds_ready[2], ds_done[2];
   uint64_t done;
   uint32_t tmem_slot;
   int abort_flag;
@@ -501,8 +501,8 @@ __device__ __forceinline__ void put_row128(uint8_t* A, int r, const uint32_t* pk
 template <bool DKDV>
 __global__ void __launch_bounds__(BW_THREADS, 1)
     bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_constant__ CUtensorMap tmDO,
-                  const float* __restrict__ lse2, const float* __restrict__ delta, bf16* __restrict__ dqkv, int T,
-                  int H, float sl2, float scale) {
+                  const float* __restrict__ lse2, float* __restrict__ delta, const bf16* __restrict__ out,
+                  const bf16* __restrict__ dout, bf16* __restrict__ dqkv, int T, int H, float sl2, float scale) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   BwBars* bars = reinterpret_cast<BwBars*>(smem + BW_OFF_BAR);
@@ -535,6 +535,7 @@ __global__ void __launch_bounds__(BW_THREADS, 1)
       mbar_init(&bars->p_ready[k], 4);
       mbar_init(&bars->dp_full[k], 1);
       mbar_init(&bars->pv_done[k], 1);
+      mbar_init(&bars->x_free2[k], 4);
       mbar_init(&bars->ds_ready[k], 4);
       mbar_init(&bars->ds_done[k], 1);
     }
@@ -643,26 +644,29 @@ __global__ void __launch_bounds__(BW_THREADS, 1)
           if (!ok) break;
         }
         tc_commit(&bars->s1_empty[st]);
-        // dK_t += dS^T Q_i  /  dQ_t += dS K_j, then the next scores of sub-tile t
-        // (a sub-tile that starts at s+1 gets its first scores here too)
+        // Per sub-tile: its next scores as soon as dP has been read out of X_t (x_free2),
+        // then dK_t += dS^T Q_i / dQ_t += dS K_j once dS is in shared memory.  The
+        // element-wise warps find the next scores ready when they finish storing dS.
         bool next_ready = false;
         for (int t = 0; t < 2 && ok; ++t) {
-          if (active(t, s)) {
-            const uint32_t k = (uint32_t)(s - lo_of(t));
-            if (!mbar_wait(&bars->ds_ready[t], k & 1, abort_flag)) { ok = false; break; }
-            tc_fence_after();
-            issue_g(t, BW_G + t * 128, s0, k > 0);
-            tc_commit(&bars->ds_done[t]);
-          }
+          const bool act = active(t, s);
+          const uint32_t k = act ? (uint32_t)(s - lo_of(t)) : 0u;
           if (s + 1 <= s_hi && active(t, s + 1)) {
             const int st1 = (it + 1) & 1;
             if (!next_ready) {
               if (!mbar_wait(&bars->s0_full[st1], ((it + 1) >> 1) & 1, abort_flag)) { ok = false; break; }
-              tc_fence_after();
               next_ready = true;
             }
+            if (act && !mbar_wait(&bars->x_free2[t], k & 1, abort_flag)) { ok = false; break; }
+            tc_fence_after();
             issue_x(t, F + t * 2 * TILE, S0 + st1 * TILE);
             tc_commit(&bars->s_full[t]);
+          }
+          if (act) {
+            if (!mbar_wait(&bars->ds_ready[t], k & 1, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+            issue_g(t, BW_G + t * 128, s0, k > 0);
+            tc_commit(&bars->ds_done[t]);
           }
         }
         if (!ok) break;
@@ -680,6 +684,7 @@ __global__ void __launch_bounds__(BW_THREADS, 1)
     const float* lb = lse2 + (long)bh * T;
     const float* db = delta + (long)bh * T;
     const uint32_t xcol = BW_X + t * 128;
+    (void)db;
     bool ok = true;
     if (t == 0 || has_b) {
       const int lo = lo_of(t), hi = hi_of(t);
@@ -689,8 +694,33 @@ __global__ void __launch_bounds__(BW_THREADS, 1)
         l = qi < T ? lb[qi] : 0.f;
         d = qi < T ? db[qi] : 0.f;
       };
-      if (DKDV) load_ld(lo * 128 + r, my_lse, my_delta);
-      else load_ld((2 * pair + t) * 128 + r, my_lse, my_delta);
+      if (DKDV) {
+        load_ld(lo * 128 + r, my_lse, my_delta);
+      } else {
+        // The dQ kernel runs first and produces delta = rowsum(dO * O) for its own
+        // query rows (fp32 sum of the bf16 products, 64 terms in order); the dK/dV
+        // kernel reads it afterwards.
+        const int qi = (2 * pair + t) * 128 + r;
+        my_lse = qi < T ? lb[qi] : 0.f;
+        if (qi < T) {
+          const long off = ((long)row_base + qi) * C + h * D;
+          const uint4* op = reinterpret_cast<const uint4*>(out + off);
+          const uint4* gp = reinterpret_cast<const uint4*>(dout + off);
+          float acc = 0.f;
+#pragma unroll
+          for (int v = 0; v < D / 8; ++v) {
+            const uint4 a = op[v], g = gp[v];
+            const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, gw[4] = {g.x, g.y, g.z, g.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              acc = fmaf(bf_lo(aw[e]), bf_lo(gw[e]), acc);
+              acc = fmaf(bf_hi(aw[e]), bf_hi(gw[e]), acc);
+            }
+          }
+          my_delta = acc;
+          delta[(long)bh * T + qi] = acc;
+        }
+      }
       for (int s = lo; s <= hi && ok; ++s) {
         const uint32_t k = (uint32_t)(s - lo);
         const int qrow = (DKDV ? s : 2 * pair + t) * 128 + r;   // query index within the sequence
@@ -744,6 +774,11 @@ __global__ void __launch_bounds__(BW_THREADS, 1)
           uint32_t x[32];
           tmem_ld32_issue(tmem + lane_off + xcol + ch * 32, x);
           tmem_wait_ld();
+          if (ch == 3) {  // dP read: X_t may take the next scores
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->x_free2[t]);
+          }
 #pragma unroll
           for (int c = 0; c < 32; c += 2) {
             const uint32_t pp = pk[ch * 16 + c / 2];
@@ -860,10 +895,16 @@ static CUtensorMap attn_map(const torch::Tensor& t, long rows, long cols) {
 
 // tcgen05 backward for head dim 64: fills dqkv [B*T, 3*H*64] from qkv, dout
 // [B*T, H*64], lse2 [B*H, T] and delta = rowsum(dout * out) [B*H, T].
-void attn_bwd_tc(torch::Tensor qkv, torch::Tensor dout, torch::Tensor lse, torch::Tensor delta, torch::Tensor dqkv,
-                 int64_t B, int64_t T, int64_t H) {
+// tcgen05 backward for head dim 64: dQ (and delta = rowsum(dO*O) into `delta`) first,
+// then dK/dV, both into dqkv [B*T, 3*H*64].
+void attn_bwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torch::Tensor lse, torch::Tensor delta,
+                 torch::Tensor dqkv, int64_t B, int64_t T, int64_t H) {
   using namespace attn_tc;
   TORCH_CHECK(dout.is_contiguous() && dout.numel() == B * T * H * D, "attn_bwd_tc: dout must be [B*T, H*64]");
+  TORCH_CHECK(out.is_contiguous() && out.numel() == B * T * H * D && out.scalar_type() == at::kBFloat16,
+              "attn_bwd_tc: out must be bf16 [B*T, H*64]");
+  TORCH_CHECK(delta.is_contiguous() && delta.numel() == B * H * T && delta.scalar_type() == at::kFloat,
+              "attn_bwd_tc: delta must be fp32 [B*H, T]");
   c10::cuda::CUDAGuard guard(qkv.device());
   bind_device_context(qkv.get_device());
   CUtensorMap mq = attn_map(qkv, B * T, 3 * H * D);
@@ -879,11 +920,13 @@ void attn_bwd_tc(torch::Tensor qkv, torch::Tensor dout, torch::Tensor lse, torch
   const float scale = 0.125f;                               // 1/sqrt(64)
   const float sl2 = (float)(1.4426950408889634 / 8.0);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  auto* out = reinterpret_cast<bf16*>(dqkv.data_ptr());
-  bwd_tc_kernel<true><<<grid, BW_THREADS, BW_SMEM, st>>>(mq, md, lse.data_ptr<float>(), delta.data_ptr<float>(), out,
-                                                         (int)T, (int)H, sl2, scale);
-  bwd_tc_kernel<false><<<grid, BW_THREADS, BW_SMEM, st>>>(mq, md, lse.data_ptr<float>(), delta.data_ptr<float>(),
-                                                          out, (int)T, (int)H, sl2, scale);
+  auto* dq = reinterpret_cast<bf16*>(dqkv.data_ptr());
+  auto* o = reinterpret_cast<const bf16*>(out.data_ptr());
+  auto* g = reinterpret_cast<const bf16*>(dout.data_ptr());
+  bwd_tc_kernel<false><<<grid, BW_THREADS, BW_SMEM, st>>>(mq, md, lse.data_ptr<float>(), delta.data_ptr<float>(), o,
+                                                          g, dq, (int)T, (int)H, sl2, scale);
+  bwd_tc_kernel<true><<<grid, BW_THREADS, BW_SMEM, st>>>(mq, md, lse.data_ptr<float>(), delta.data_ptr<float>(), o,
+                                                         g, dq, (int)T, (int)H, sl2, scale);
   count_launch(2);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

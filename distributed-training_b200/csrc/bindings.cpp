@@ -20,7 +20,7 @@ std::vector<int64_t> gemm_tiling(int64_t M, int64_t N, int64_t K);
 std::vector<torch::Tensor> layernorm_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor b, double eps);
 torch::Tensor layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor mean,
                             torch::Tensor rstd, c10::optional<torch::Tensor> dresid, torch::Tensor dw,
-                            torch::Tensor db, bool accumulate);
+                            torch::Tensor db, bool accumulate, c10::optional<torch::Tensor> dres_sum);
 void bias_grad(torch::Tensor g, torch::Tensor db, bool accumulate);
 // embed_xent.cu
 torch::Tensor embed_fwd(torch::Tensor idx, torch::Tensor tok, torch::Tensor pos, torch::Tensor bad_flag);
@@ -98,7 +98,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("workspace") = py::none());
   m.def("gemm_tiling", &gemm_tiling);
   m.def("layernorm_fwd", &layernorm_fwd);
-  m.def("layernorm_bwd", &layernorm_bwd);
+  m.def("layernorm_bwd", &layernorm_bwd, py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("mean"),
+        py::arg("rstd"), py::arg("dresid"), py::arg("dw"), py::arg("db"), py::arg("accumulate") = false,
+        py::arg("dres_sum") = py::none());
   m.def("bias_grad", &bias_grad);
   m.def("embed_fwd", &embed_fwd);
   m.def("embed_bwd", &embed_bwd);

@@ -47,174 +47,248 @@ __device__ __forceinline__ void st8(bf16* p, const float* v) {
   *reinterpret_cast<uint4*>(p) = u;
 }
 
-// One warp per row; lane l owns 8-element chunks l, l+32, l+64, ... (NCH chunks).
+__device__ __forceinline__ void unpack8(const uint4& u, float* v) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+// Two rows per warp (both rows' loads in flight together); lane l owns 8-element
+// chunks l, l+32, l+64, ... (NCH chunks) of each row.
 template <int NCH>
 __global__ void ln_fwd_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w, const bf16* __restrict__ b,
                               bf16* __restrict__ y, float* __restrict__ mean_out, float* __restrict__ rstd_out,
                               int rows, int C, float eps) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (warp >= rows) return;
-  const bf16* xr = x + (long)warp * C;
-  float v[NCH][8];
-  float s = 0.f;
+  const int r0 = warp * 2;
+  if (r0 >= rows) return;
+  uint4 raw[2][NCH];
 #pragma unroll
-  for (int c = 0; c < NCH; ++c) {
-    const int col = (c * 32 + lane) * 8;
-    if (col < C) {
-      ld8(xr + col, v[c]);
+  for (int k = 0; k < 2; ++k)
 #pragma unroll
-      for (int j = 0; j < 8; ++j) s += v[c][j];
+    for (int c = 0; c < NCH; ++c) {
+      const int col = (c * 32 + lane) * 8;
+      if (col < C && r0 + k < rows) raw[k][c] = *reinterpret_cast<const uint4*>(x + (long)(r0 + k) * C + col);
     }
-  }
-  const float mu = warp_sum(s) / C;
-  float ss = 0.f;
 #pragma unroll
-  for (int c = 0; c < NCH; ++c) {
-    const int col = (c * 32 + lane) * 8;
-    if (col < C) {
+  for (int k = 0; k < 2; ++k) {
+    const int r = r0 + k;
+    if (r >= rows) break;
+    float v[NCH][8];
+    float s = 0.f;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float d = v[c][j] - mu;
-        ss += d * d;
+    for (int c = 0; c < NCH; ++c) {
+      const int col = (c * 32 + lane) * 8;
+      if (col < C) {
+        unpack8(raw[k][c], v[c]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s += v[c][j];
       }
     }
-  }
-  const float var = warp_sum(ss) / C;
-  const float rs = rsqrtf(var + eps);
-  bf16* yr = y + (long)warp * C;
+    const float mu = warp_sum(s) / C;
+    float ss = 0.f;
 #pragma unroll
-  for (int c = 0; c < NCH; ++c) {
-    const int col = (c * 32 + lane) * 8;
-    if (col < C) {
-      float wv[8], bv[8], o[8];
-      ld8(w + col, wv);
-      ld8(b + col, bv);
+    for (int c = 0; c < NCH; ++c) {
+      const int col = (c * 32 + lane) * 8;
+      if (col < C) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] = (v[c][j] - mu) * rs * wv[j] + bv[j];
-      st8(yr + col, o);
+        for (int j = 0; j < 8; ++j) {
+          const float d = v[c][j] - mu;
+          ss += d * d;
+        }
+      }
     }
-  }
-  if (lane == 0) {
-    mean_out[warp] = mu;
-    rstd_out[warp] = rs;
+    const float var = warp_sum(ss) / C;
+    const float rs = rsqrtf(var + eps);
+    bf16* yr = y + (long)r * C;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int col = (c * 32 + lane) * 8;
+      if (col < C) {
+        float wv[8], bv[8], o[8];
+        ld8(w + col, wv);
+        ld8(b + col, bv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = (v[c][j] - mu) * rs * wv[j] + bv[j];
+        st8(yr + col, o);
+      }
+    }
+    if (lane == 0) {
+      mean_out[r] = mu;
+      rstd_out[r] = rs;
+    }
   }
 }
 
 constexpr int kLnBwdWarps = 8;
 constexpr int kLnBwdRowsPerBlock = 64;
 
-// Block b handles rows [b*64, b*64+64); warp k handles rows b*64 + k, +8, ...
-// Per-block dw/db partials go to part_w/part_b [gridDim.x, C].
+// Dynamic shared memory of ln_bwd_kernel: per-warp column accumulators [3][C].
+static inline size_t ln_bwd_smem(int C) { return (size_t)kLnBwdWarps * 3 * C * sizeof(float); }
+
+// Block b handles rows [b*64, b*64+64); warp k handles rows b*64 + k, +8, ... and
+// prefetches its next row while it computes the current one (the row's dy, x and
+// dresid stay in registers between the two passes, nothing is re-read).  Column
+// sums of g*xhat (dw), g (db) and - when part_r is given - of the residual
+// gradient dresid (the bias gradient of the layer that produced it) accumulate in
+// per-warp shared-memory rows, then combine in warp order into per-block partials
+// [gridDim.x, C].
 template <int NCH>
 __global__ void __launch_bounds__(kLnBwdWarps * 32, 2)
     ln_bwd_kernel(const bf16* __restrict__ dy, const bf16* __restrict__ x, const bf16* __restrict__ w,
                   const float* __restrict__ mean, const float* __restrict__ rstd, const bf16* __restrict__ dresid,
-                  bf16* __restrict__ dx, float* __restrict__ part_w, float* __restrict__ part_b, int rows, int C) {
-  extern __shared__ float sm[];  // [kLnBwdWarps][2][C]
+                  bf16* __restrict__ dx, float* __restrict__ part_w, float* __restrict__ part_b,
+                  float* __restrict__ part_r, int rows, int C) {
+  extern __shared__ float sm[];  // [kLnBwdWarps][3][C]
   const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float aw[NCH][8], ab[NCH][8];
-#pragma unroll
-  for (int c = 0; c < NCH; ++c)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) aw[c][j] = ab[c][j] = 0.f;
+  float* acc = sm + (size_t)wid * 3 * C;
+  for (int i = lane * 4; i < 3 * C; i += 128) *reinterpret_cast<float4*>(acc + i) = make_float4(0.f, 0.f, 0.f, 0.f);
+  __syncwarp();
+  const bool has_r = dresid != nullptr;
   const int r0 = blockIdx.x * kLnBwdRowsPerBlock;
-  for (int rr = wid; rr < kLnBwdRowsPerBlock; rr += kLnBwdWarps) {
-    const int r = r0 + rr;
-    if (r >= rows) break;
-    const float mu = mean[r], rs = rstd[r];
-    float s1 = 0.f, s2 = 0.f;
-    // pass 1: row statistics of g*w and g*w*xhat, plus the dw/db accumulators
+  const int r_end = min(r0 + kLnBwdRowsPerBlock, rows);
+  uint4 cy[NCH], cx[NCH], cr[NCH];
+  auto load = [&](int r, uint4* gy, uint4* gx, uint4* gr) {
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
       const int col = (c * 32 + lane) * 8;
       if (col < C) {
-        float g[8], xv[8], wv[8];
-        ld8(dy + (long)r * C + col, g);
-        ld8(x + (long)r * C + col, xv);
-        ld8(w + col, wv);
+        gy[c] = *reinterpret_cast<const uint4*>(dy + (long)r * C + col);
+        gx[c] = *reinterpret_cast<const uint4*>(x + (long)r * C + col);
+        gr[c] = has_r ? *reinterpret_cast<const uint4*>(dresid + (long)r * C + col) : make_uint4(0, 0, 0, 0);
+      }
+    }
+  };
+  int r = r0 + wid;
+  if (r < r_end) load(r, cy, cx, cr);
+  for (; r < r_end; r += kLnBwdWarps) {
+    constexpr bool kPrefetch = NCH <= 3;  // larger rows keep enough bytes in flight without it
+    uint4 ny[NCH], nx[NCH], nr[NCH];
+    if (kPrefetch && r + kLnBwdWarps < r_end) load(r + kLnBwdWarps, ny, nx, nr);
+    const float mu = mean[r], rs = rstd[r];
+    float s1 = 0.f, s2 = 0.f;
+    // pass 1: row statistics of g*w and g*w*xhat, plus the column accumulators
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int col = (c * 32 + lane) * 8;
+      if (col < C) {
+        float g[8], xv[8], wv[8], rv[8];
+        unpack8(cy[c], g);
+        unpack8(cx[c], xv);
+        ld8(w + col, wv);  // 1.5-6 KB of weights: L1-resident across rows
+        float4* aw = reinterpret_cast<float4*>(acc + col);
+        float4* ab = reinterpret_cast<float4*>(acc + C + col);
+        float4 w0 = aw[0], w1 = aw[1], b0 = ab[0], b1 = ab[1];
+        float dwv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        float dbv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const float xh = (xv[j] - mu) * rs;
           const float gw = g[j] * wv[j];
           s1 += gw;
           s2 += gw * xh;
-          aw[c][j] += g[j] * xh;
-          ab[c][j] += g[j];
+          dwv[j] += g[j] * xh;
+          dbv[j] += g[j];
+        }
+        aw[0] = make_float4(dwv[0], dwv[1], dwv[2], dwv[3]);
+        aw[1] = make_float4(dwv[4], dwv[5], dwv[6], dwv[7]);
+        ab[0] = make_float4(dbv[0], dbv[1], dbv[2], dbv[3]);
+        ab[1] = make_float4(dbv[4], dbv[5], dbv[6], dbv[7]);
+        if (part_r) {
+          unpack8(cr[c], rv);
+          float4* ar = reinterpret_cast<float4*>(acc + 2 * C + col);
+          float4 r0v = ar[0], r1v = ar[1];
+          ar[0] = make_float4(r0v.x + rv[0], r0v.y + rv[1], r0v.z + rv[2], r0v.w + rv[3]);
+          ar[1] = make_float4(r1v.x + rv[4], r1v.y + rv[5], r1v.z + rv[6], r1v.w + rv[7]);
         }
       }
     }
     const float m1 = warp_sum(s1) / C, m2 = warp_sum(s2) / C;
-    // pass 2: dx (operands re-read; they are still in L1)
+    // pass 2: dx from the registers
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
       const int col = (c * 32 + lane) * 8;
       if (col < C) {
-        float g[8], xv[8], wv[8], o[8], rv[8];
-        ld8(dy + (long)r * C + col, g);
-        ld8(x + (long)r * C + col, xv);
+        float g[8], xv[8], wv[8], rv[8], o[8];
+        unpack8(cy[c], g);
+        unpack8(cx[c], xv);
         ld8(w + col, wv);
-        if (dresid) ld8(dresid + (long)r * C + col, rv);
+        unpack8(cr[c], rv);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          o[j] = rs * (g[j] * wv[j] - m1 - (xv[j] - mu) * rs * m2);
-          if (dresid) o[j] += rv[j];
-        }
+        for (int j = 0; j < 8; ++j) o[j] = rs * (g[j] * wv[j] - m1 - (xv[j] - mu) * rs * m2) + rv[j];
         st8(dx + (long)r * C + col, o);
       }
     }
-  }
-  // combine the warps of this block in warp order
+    if (kPrefetch) {
 #pragma unroll
-  for (int c = 0; c < NCH; ++c) {
-    const int col = (c * 32 + lane) * 8;
-    if (col < C) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        sm[(wid * 2 + 0) * C + col + j] = aw[c][j];
-        sm[(wid * 2 + 1) * C + col + j] = ab[c][j];
+      for (int c = 0; c < NCH; ++c) {
+        cy[c] = ny[c];
+        cx[c] = nx[c];
+        cr[c] = nr[c];
       }
+    } else if (r + kLnBwdWarps < r_end) {
+      load(r + kLnBwdWarps, cy, cx, cr);
     }
   }
   __syncthreads();
-  for (int col = threadIdx.x; col < C; col += blockDim.x) {
-    float sw = 0.f, sb = 0.f;
-    for (int k = 0; k < kLnBwdWarps; ++k) {
-      sw += sm[(k * 2 + 0) * C + col];
-      sb += sm[(k * 2 + 1) * C + col];
-    }
-    part_w[(long)blockIdx.x * C + col] = sw;
-    part_b[(long)blockIdx.x * C + col] = sb;
+  // combine the warps of this block in warp order
+  const int narr = part_r ? 3 : 2;
+  for (int i = threadIdx.x; i < narr * C; i += blockDim.x) {
+    float t = 0.f;
+    for (int k = 0; k < kLnBwdWarps; ++k) t += sm[(size_t)k * 3 * C + i];
+    const int a = i / C, col = i - a * C;
+    float* dst = a == 0 ? part_w : (a == 1 ? part_b : part_r);
+    dst[(long)blockIdx.x * C + col] = t;
   }
 }
 
 // out[col] = (accumulate ? out[col] : 0) + sum_{k=0..nparts-1} part[k, col].
-// Block = 32 columns x 8 partial-lanes: lane k sums partials k, k+8, ... (coalesced
-// 128-byte rows), then lane sums are combined in lane order - a fixed order, so
-// the result is deterministic.
-constexpr int kColsumThreads = 256;
-__global__ void __launch_bounds__(kColsumThreads)
-    colsum_partials_kernel(const float* __restrict__ part, int nparts, int C, float* __restrict__ out,
-                           int accumulate) {
-  __shared__ float sm[8][33];
+// Block = 32 columns x 32 partial-lanes: lane k sums partials k, k+32, ...
+// (coalesced 128-byte rows), then the lane sums are combined in lane order - a
+// fixed order, so the result is deterministic.  blockIdx.y picks one of up to
+// three (part, out) pairs, so several reductions share a launch.
+constexpr int kColsumLanes = 32;
+struct ColsumJobs {
+  const float* part[3];
+  float* out[3];
+};
+__global__ void __launch_bounds__(32 * kColsumLanes)
+    colsum_partials_kernel(ColsumJobs jobs, int nparts, int C, int accumulate) {
+  __shared__ float sm[kColsumLanes][33];
+  const float* part = jobs.part[blockIdx.y];
+  float* out = jobs.out[blockIdx.y];
   const int cl = threadIdx.x & 31, kl = threadIdx.x >> 5;
   const int col = blockIdx.x * 32 + cl;
   float s = 0.f;
   if (col < C)
-    for (int k = kl; k < nparts; k += 8) s += part[(long)k * C + col];
+    for (int k = kl; k < nparts; k += kColsumLanes) s += part[(long)k * C + col];
   sm[kl][cl] = s;
   __syncthreads();
   if (kl == 0 && col < C) {
     float t = sm[0][cl];
 #pragma unroll
-    for (int i = 1; i < 8; ++i) t += sm[i][cl];
+    for (int i = 1; i < kColsumLanes; ++i) t += sm[i][cl];
     out[col] = accumulate ? out[col] + t : t;
   }
 }
 
+static inline void launch_colsum_multi(const ColsumJobs& jobs, int njobs, int nparts, int C, int accumulate,
+                                       cudaStream_t st) {
+  dim3 grid((C + 31) / 32, njobs);
+  colsum_partials_kernel<<<grid, 32 * kColsumLanes, 0, st>>>(jobs, nparts, C, accumulate);
+}
+
 static inline void launch_colsum(const float* part, int nparts, int C, float* out, int accumulate,
                                  cudaStream_t st) {
-  colsum_partials_kernel<<<(C + 31) / 32, kColsumThreads, 0, st>>>(part, nparts, C, out, accumulate);
+  ColsumJobs j{};
+  j.part[0] = part;
+  j.out[0] = out;
+  launch_colsum_multi(j, 1, nparts, C, accumulate, st);
 }
 
 // Bias gradient stage 1: partial column sums of a bf16 [rows, N] matrix over
@@ -263,7 +337,8 @@ std::vector<torch::Tensor> layernorm_fwd(torch::Tensor x, torch::Tensor w, torch
   auto rstd = torch::empty({rows}, x.options().dtype(at::kFloat));
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   const int threads = 256;
-  const int blocks = (rows * 32 + threads - 1) / threads;
+  const long warps = (rows + 1) / 2;  // two rows per warp
+  const int blocks = (int)((warps * 32 + threads - 1) / threads);
   const int nch = ln_chunks(C);
   auto* xp = reinterpret_cast<const bf16*>(x.data_ptr());
   auto* wp = reinterpret_cast<const bf16*>(w.data_ptr());
@@ -285,10 +360,12 @@ std::vector<torch::Tensor> layernorm_fwd(torch::Tensor x, torch::Tensor w, torch
   return {y, mean, rstd};
 }
 
-// Returns dx; writes dw, db (fp32 [C]) — accumulating when requested.
+// Returns dx; writes dw, db (fp32 [C]) - accumulating when requested - and, when
+// `dres_sum` is given, the column sums of dresid (the bias gradient of the layer
+// whose output gradient dresid is), so that bias gradient costs no extra pass.
 torch::Tensor layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor mean,
                             torch::Tensor rstd, c10::optional<torch::Tensor> dresid, torch::Tensor dw,
-                            torch::Tensor db, bool accumulate) {
+                            torch::Tensor db, bool accumulate, c10::optional<torch::Tensor> dres_sum) {
   TORCH_CHECK(dy.is_contiguous() && x.is_contiguous() && dy.scalar_type() == at::kBFloat16, "layernorm_bwd: dy/x");
   TORCH_CHECK(dw.scalar_type() == at::kFloat && db.scalar_type() == at::kFloat, "layernorm_bwd: dw/db fp32");
   c10::cuda::CUDAGuard guard(x.device());
@@ -296,26 +373,32 @@ torch::Tensor layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, 
   const int rows = (int)(x.numel() / C);
   auto dx = torch::empty_like(x);
   const int nblk = (rows + kLnBwdRowsPerBlock - 1) / kLnBwdRowsPerBlock;
-  auto part = torch::empty({2, nblk, C}, x.options().dtype(at::kFloat));
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   const bf16* dr = nullptr;
   if (dresid && dresid->defined()) {
-    TORCH_CHECK(dresid->is_contiguous() && dresid->numel() == x.numel(), "layernorm_bwd: dresid");
+    TORCH_CHECK(dresid->is_contiguous() && dresid->numel() == x.numel() && dresid->scalar_type() == at::kBFloat16,
+                "layernorm_bwd: dresid");
     dr = reinterpret_cast<const bf16*>(dresid->data_ptr());
   }
+  const bool rsum = dres_sum && dres_sum->defined();
+  TORCH_CHECK(!rsum || (dr && dres_sum->scalar_type() == at::kFloat && dres_sum->numel() == C &&
+                        dres_sum->is_contiguous()),
+              "layernorm_bwd: dres_sum needs dresid and an fp32 [C] output");
+  auto part = torch::empty({rsum ? 3 : 2, nblk, C}, x.options().dtype(at::kFloat));
   const int nch = ln_chunks(C);
-  const size_t smem = (size_t)kLnBwdWarps * 2 * C * sizeof(float);
+  const size_t smem = ln_bwd_smem(C);
   auto* dyp = reinterpret_cast<const bf16*>(dy.data_ptr());
   auto* xp = reinterpret_cast<const bf16*>(x.data_ptr());
   auto* wp = reinterpret_cast<const bf16*>(w.data_ptr());
   auto* dxp = reinterpret_cast<bf16*>(dx.data_ptr());
   float* pw = part.data_ptr<float>();
   float* pb = pw + (long)nblk * C;
+  float* pr = rsum ? pb + (long)nblk * C : nullptr;
 #define LNB(NC)                                                                                          \
   {                                                                                                      \
     auto k = ln_bwd_kernel<NC>;                                                                          \
     if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
-    k<<<nblk, kLnBwdWarps * 32, smem, st>>>(dyp, xp, wp, mean.data_ptr<float>(), rstd.data_ptr<float>(), dr, dxp, pw, pb, rows, C); \
+    k<<<nblk, kLnBwdWarps * 32, smem, st>>>(dyp, xp, wp, mean.data_ptr<float>(), rstd.data_ptr<float>(), dr, dxp, pw, pb, pr, rows, C); \
   }
   switch (nch) {
     case 1: LNB(1); break;
@@ -329,9 +412,17 @@ torch::Tensor layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, 
 #undef LNB
   count_launch();
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  launch_colsum(pw, nblk, C, dw.data_ptr<float>(), accumulate ? 1 : 0, st);
-  launch_colsum(pb, nblk, C, db.data_ptr<float>(), accumulate ? 1 : 0, st);
-  count_launch(2);
+  ColsumJobs jobs{};
+  jobs.part[0] = pw;
+  jobs.out[0] = dw.data_ptr<float>();
+  jobs.part[1] = pb;
+  jobs.out[1] = db.data_ptr<float>();
+  if (rsum) {
+    jobs.part[2] = pr;
+    jobs.out[2] = dres_sum->data_ptr<float>();
+  }
+  launch_colsum_multi(jobs, rsum ? 3 : 2, nblk, C, accumulate ? 1 : 0, st);
+  count_launch();
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return dx;
 }
@@ -459,7 +550,7 @@ extern "C" __attribute__((visibility("default"))) int dtb_layernorm_bwd_noalloc(
   float* pw = scratch;
   float* pb = scratch + nblk * C;
   const int nch = (C + 255) / 256;
-  const size_t smem = (size_t)kLnBwdWarps * 2 * C * sizeof(float);
+  const size_t smem = ln_bwd_smem(C);
   auto* dyp = static_cast<const bf16*>(dy);
   auto* xp = static_cast<const bf16*>(x);
   auto* wp = static_cast<const bf16*>(w);
@@ -471,7 +562,8 @@ extern "C" __attribute__((visibility("default"))) int dtb_layernorm_bwd_noalloc(
     if (smem > 48 * 1024 && cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=     \
                                 cudaSuccess)                                                                      \
       return DTB_NOALLOC_LAUNCH_FAILED;                                                                           \
-    k<<<(unsigned)nblk, kLnBwdWarps * 32, smem, stream>>>(dyp, xp, wp, mean, rstd, drp, dxp, pw, pb, rows, C);    \
+    k<<<(unsigned)nblk, kLnBwdWarps * 32, smem, stream>>>(dyp, xp, wp, mean, rstd, drp, dxp, pw, pb, nullptr, rows, \
+                                                          C);                                                     \
   }
   switch (nch) {
     case 1: DTB_LNB_NOALLOC(1); break;
@@ -482,8 +574,12 @@ extern "C" __attribute__((visibility("default"))) int dtb_layernorm_bwd_noalloc(
     default: DTB_LNB_NOALLOC(8); break;
   }
 #undef DTB_LNB_NOALLOC
-  launch_colsum(pw, (int)nblk, C, dw, accumulate ? 1 : 0, stream);
-  launch_colsum(pb, (int)nblk, C, db, accumulate ? 1 : 0, stream);
+  ColsumJobs jobs{};
+  jobs.part[0] = pw;
+  jobs.out[0] = dw;
+  jobs.part[1] = pb;
+  jobs.out[1] = db;
+  launch_colsum_multi(jobs, 2, (int)nblk, C, accumulate ? 1 : 0, stream);
   if (cudaGetLastError() != cudaSuccess) return DTB_NOALLOC_LAUNCH_FAILED;
   return DTB_NOALLOC_OK;
 }

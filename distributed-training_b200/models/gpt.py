@@ -266,19 +266,17 @@ class _BlockFn(torch.autograd.Function):
         # out: x3 = act @ Wout + bout + x2
         dpre = K.gemm(dy, W(blk.out.w), b_trans=True, epi=K.EPI_DGELU, aux=pre)
         K.gemm(act, dy, g_out_w, a_trans=True, epi=K.EPI_F32)
-        K.bias_grad(dy, g_out_b)
         # fc: pre = h2 @ Wfc + bfc ; act = gelu(pre)
         dh2 = K.gemm(dpre, W(blk.fc.w), b_trans=True)
         K.gemm(h2, dpre, g_fc_w, a_trans=True, epi=K.EPI_F32)
         K.bias_grad(dpre, g_fc_b)
         del dpre
-        # ln2 (+ residual gradient dy)
-        dx2 = K.layernorm_bwd(dh2, x2, W(blk.ln2.w), mu2, rs2, dy, g_ln2_w, g_ln2_b)
+        # ln2 (+ residual gradient dy, whose column sums are out's bias gradient)
+        dx2 = K.layernorm_bwd(dh2, x2, W(blk.ln2.w), mu2, rs2, dy, g_ln2_w, g_ln2_b, dres_sum=g_out_b)
         del dh2
         # proj: x2 = a @ Wproj + bproj + x
         da = K.gemm(dx2, W(blk.proj.w), b_trans=True)
         K.gemm(a, dx2, g_proj_w, a_trans=True, epi=K.EPI_F32)
-        K.bias_grad(dx2, g_proj_b)
         # attention
         dqkv = K.attn_bwd(qkv, a, da, lse, B, T, H, D)
         del da
@@ -287,8 +285,8 @@ class _BlockFn(torch.autograd.Function):
         K.gemm(h1, dqkv, g_qkv_w, a_trans=True, epi=K.EPI_F32)
         K.bias_grad(dqkv, g_qkv_b)
         del dqkv
-        # ln1 (+ residual gradient dx2)
-        dx = K.layernorm_bwd(dh1, x2d, W(blk.ln1.w), mu1, rs1, dx2, g_ln1_w, g_ln1_b)
+        # ln1 (+ residual gradient dx2, whose column sums are proj's bias gradient)
+        dx = K.layernorm_bwd(dh1, x2d, W(blk.ln1.w), mu1, rs1, dx2, g_ln1_w, g_ln1_b, dres_sum=g_proj_b)
         return (dx.view(B, T, C), None, g_ln1_w, g_ln1_b, g_qkv_w, g_qkv_b, g_proj_w, g_proj_b,
                 g_ln2_w, g_ln2_b, g_fc_w, g_fc_b, g_out_w, g_out_b)
 

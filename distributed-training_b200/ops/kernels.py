@@ -41,9 +41,10 @@ def layernorm_fwd(x: torch.Tensor, w16: torch.Tensor, b16: torch.Tensor, eps: fl
     return lib().layernorm_fwd(x, w16, b16, eps)
 
 
-def layernorm_bwd(dy, x, w16, mean, rstd, dresid, dw, db, accumulate=False):
-    """dx (bf16) = LN backward + dresid; writes dw, db (fp32)."""
-    return lib().layernorm_bwd(dy, x, w16, mean, rstd, dresid, dw, db, accumulate)
+def layernorm_bwd(dy, x, w16, mean, rstd, dresid, dw, db, accumulate=False, dres_sum=None):
+    """dx (bf16) = LN backward + dresid; writes dw, db (fp32) and, when ``dres_sum``
+    is given, the column sums of ``dresid`` (fp32 [C]) from the same pass."""
+    return lib().layernorm_bwd(dy, x, w16, mean, rstd, dresid, dw, db, accumulate, dres_sum)
 
 
 def bias_grad(g: torch.Tensor, db: torch.Tensor, accumulate: bool = False) -> None:
