@@ -386,9 +386,8 @@ __global__ void barrier_kernel(CommCtx c) { cta_barrier(c, c.epoch); }
 // Phase 3: all-gather of the bf16 working copy (and optionally the fp32 master).
 __global__ void __launch_bounds__(kCommThreads)
     zero_adamw_allgather_kernel(CommCtx c, Sigs sq_parts, int nparts, float* master, const float* grad,
-                                float* m, float* v, Peers work16, Peers master32, long n, float lr, float b1,
-                                float b2, float eps, float wd, float b1t, float b2t, float max_norm,
-                                double* sq_out, int gather_master) {
+                                float* m, float* v, Peers work16, Peers master32, long n, AdamConsts ak,
+                                float max_norm, double* sq_out, int gather_master) {
   __shared__ float s_clip;
   if (!cta_barrier(c, c.epoch)) return;
   if (threadIdx.x == 0) {
@@ -413,12 +412,8 @@ __global__ void __launch_bounds__(kCommThreads)
   bf16* w16 = reinterpret_cast<bf16*>(work16.p[c.rank]);
   for (long i = a + threadIdx.x; i < b; i += blockDim.x) {
     const long k = i - lo;  // index into the shard-local optimizer state
-    const float gg = grad[i] * cs;
-    float mm = b1 * m[k] + (1.f - b1) * gg;
-    float vv = b2 * v[k] + (1.f - b2) * (gg * gg);
-    float p = master[i];
-    p -= lr * (wd * p);
-    p -= lr * (mm / b1t) / (sqrtf(vv / b2t) + eps);
+    float mm = m[k], vv = v[k], p = master[i];
+    adamw_elem(p, grad[i] * cs, mm, vv, ak);
     m[k] = mm;
     v[k] = vv;
     master[i] = p;
@@ -638,14 +633,12 @@ int64_t zero_adamw_allgather(std::vector<int64_t> sigs, int64_t rank, int64_t ep
   Sigs sp{};
   for (size_t i = 0; i < sq_parts.size(); ++i) sp.p[i] = reinterpret_cast<uint32_t*>(sq_parts[i]);
   Peers w16 = make_peers(work16, 0), m32 = make_peers(master32, 0);
-  const float b1t = (float)(1.0 - std::pow(b1, (double)t));
-  const float b2t = (float)(1.0 - std::pow(b2, (double)t));
+  const AdamConsts ak = adam_consts(lr, b1, b2, eps, wd, t);
   double* sqo = (sq_out && sq_out->defined()) ? sq_out->data_ptr<double>() : nullptr;
   const int nb = comm_blocks(n * 2, blocks);
   zero_adamw_allgather_kernel<<<nb, kCommThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
       c, sp, (int)nparts, master.data_ptr<float>(), grad.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
-      w16, m32, n, (float)lr, (float)b1, (float)b2, (float)eps, (float)wd, b1t, b2t, (float)max_norm, sqo,
-      gather_master ? 1 : 0);
+      w16, m32, n, ak, (float)max_norm, sqo, gather_master ? 1 : 0);
   count_launch();
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return 3;

@@ -12,6 +12,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cmath>
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -290,6 +291,32 @@ __device__ __forceinline__ float gelu_tanh_grad(float x) {
   float t = tanhf(c * (x + 0.044715f * x2 * x));
   float du = c * (1.0f + 3.0f * 0.044715f * x2);
   return 0.5f * (1.0f + t) + 0.5f * x * (1.0f - t * t) * du;
+}
+
+// One AdamW element update in torch.optim.AdamW's order - decoupled decay, then
+// the moments, then the bias-corrected step - with the per-step constants folded
+// on the host: step = lr / (1 - b1^t), rb2 = 1 / sqrt(1 - b2^t), decay = 1 - lr*wd.
+// One square root and one division per element keep the kernels memory-bound.
+struct AdamConsts {
+  float b1, b2, omb1, omb2, eps, step, rb2, decay;
+};
+__host__ inline AdamConsts adam_consts(double lr, double b1, double b2, double eps, double wd, long t) {
+  AdamConsts k;
+  k.b1 = (float)b1;
+  k.b2 = (float)b2;
+  k.omb1 = (float)(1.0 - b1);
+  k.omb2 = (float)(1.0 - b2);
+  k.eps = (float)eps;
+  k.step = (float)(lr / (1.0 - std::pow(b1, (double)t)));
+  k.rb2 = (float)(1.0 / std::sqrt(1.0 - std::pow(b2, (double)t)));
+  k.decay = (float)(1.0 - lr * wd);
+  return k;
+}
+__device__ __forceinline__ void adamw_elem(float& p, float g, float& m, float& v, const AdamConsts& k) {
+  m = fmaf(k.b1, m, k.omb1 * g);
+  v = fmaf(k.b2, v, k.omb2 * (g * g));
+  p *= k.decay;
+  p -= k.step * (m / fmaf(sqrtf(v), k.rb2, k.eps));
 }
 
 // Counts kernel launches issued through this extension (host side), so the

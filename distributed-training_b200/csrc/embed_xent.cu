@@ -161,6 +161,84 @@ __global__ void __launch_bounds__(kXentThreads)
   }
 }
 
+// Streaming variant for 16-byte aligned rows: each thread walks its strided
+// 8-column chunks four at a time (the next four loads are in flight while the
+// current ones are reduced), takes the max of the 32 values, merges it into its
+// running (max, sum) once - two exponentials per 32 elements instead of per 8 -
+// and then spends one exp2 per element on (x - max) * log2(e).
+constexpr int kXentRound = 4;
+__global__ void __launch_bounds__(kXentThreads)
+    xent_fwd_stream_kernel(const bf16* __restrict__ logits, long ld, const int64_t* __restrict__ tgt, int V,
+                           float* __restrict__ lse_out, float* __restrict__ loss_out) {
+  constexpr float kLog2e = 1.4426950408889634f;
+  const long row = blockIdx.x;
+  const bf16* z = logits + row * ld;
+  const int nvec = V / 8;
+  float m = -INFINITY, s = 0.f;
+  uint4 cur[kXentRound];
+  auto load = [&](int base, uint4* dst) {
+#pragma unroll
+    for (int k = 0; k < kXentRound; ++k) {
+      const int i = base + k * kXentThreads;
+      if (i < nvec) dst[k] = *reinterpret_cast<const uint4*>(z + (long)i * 8);
+    }
+  };
+  constexpr int kStep = kXentRound * kXentThreads;
+  int base = threadIdx.x;
+  if (base < nvec) load(base, cur);
+  for (; base < nvec; base += kStep) {
+    uint4 nxt[kXentRound];
+    if (base + kStep < nvec) load(base + kStep, nxt);
+    float lm = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < kXentRound; ++k) {
+      if (base + k * kXentThreads < nvec) {
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&cur[k]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(h[e]);
+          lm = fmaxf(lm, fmaxf(f.x, f.y));
+        }
+      }
+    }
+    const float nb = -lm * kLog2e;
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int k = 0; k < kXentRound; ++k) {
+      if (base + k * kXentThreads < nvec) {
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&cur[k]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(h[e]);
+          s0 += exp2f(fmaf(f.x, kLog2e, nb));
+          s1 += exp2f(fmaf(f.y, kLog2e, nb));
+        }
+      }
+    }
+    online_merge(m, s, lm, s0 + s1);
+#pragma unroll
+    for (int k = 0; k < kXentRound; ++k) cur[k] = nxt[k];
+  }
+  for (int i = nvec * 8 + threadIdx.x; i < V; i += kXentThreads) online_merge(m, s, bf2f(z[i]), 1.f);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    online_merge(m, s, m2, s2);
+  }
+  __shared__ float sm_m[kXentThreads / 32], sm_s[kXentThreads / 32];
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) { sm_m[w] = m; sm_s[w] = s; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float M = sm_m[0], S = sm_s[0];
+    for (int k = 1; k < kXentThreads / 32; ++k) online_merge(M, S, sm_m[k], sm_s[k]);
+    const float lse = M + __logf(S);
+    lse_out[row] = lse;
+    const int64_t t = tgt[row];
+    loss_out[row] = (t >= 0 && t < V) ? lse - bf2f(z[t]) : 0.f;
+  }
+}
+
 // loss = mean(loss_rows) in a fixed order (single block).
 __global__ void mean_kernel(const float* __restrict__ x, long n, float* __restrict__ out) {
   __shared__ double sm[1024];
@@ -259,9 +337,14 @@ std::vector<torch::Tensor> xent_fwd(torch::Tensor logits, torch::Tensor tgt) {
   auto loss = torch::empty({}, logits.options().dtype(at::kFloat));
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   auto tg = tgt.contiguous();
-  xent_fwd_kernel<<<(unsigned)rows, kXentThreads, 0, st>>>(reinterpret_cast<const bf16*>(logits.data_ptr()),
-                                                          logits.stride(0), tg.data_ptr<int64_t>(), V,
-                                                          lse.data_ptr<float>(), lrow.data_ptr<float>(), vec_ok);
+  auto* zp = reinterpret_cast<const bf16*>(logits.data_ptr());
+  if (vec_ok) {
+    xent_fwd_stream_kernel<<<(unsigned)rows, kXentThreads, 0, st>>>(zp, logits.stride(0), tg.data_ptr<int64_t>(), V,
+                                                                    lse.data_ptr<float>(), lrow.data_ptr<float>());
+  } else {
+    xent_fwd_kernel<<<(unsigned)rows, kXentThreads, 0, st>>>(zp, logits.stride(0), tg.data_ptr<int64_t>(), V,
+                                                            lse.data_ptr<float>(), lrow.data_ptr<float>(), vec_ok);
+  }
   mean_kernel<<<1, 1024, 0, st>>>(lrow.data_ptr<float>(), rows, loss.data_ptr<float>());
   count_launch(2);
   C10_CUDA_KERNEL_LAUNCH_CHECK();

@@ -1,10 +1,13 @@
 // Flat-buffer optimizer kernels: AdamW, deterministic squared grad norm, casts.
 //
-// AdamW follows dtrain/optim.py:21-33 exactly in its order of operations:
-//   m = b1*m + (1-b1)*g ; v = b2*v + (1-b2)*g*g
-//   p -= lr*(wd*p)                       (decoupled decay first)
-//   p -= lr*(m/b1t) / (sqrt(v/b2t) + eps)
-// over one flat fp32 master buffer (all parameters, or a ZeRO shard), and also
+// AdamW is the update of dtrain/optim.py:21-33 (decoupled decay first, then the
+// moments, then the bias-corrected step), with the per-step constants folded on
+// the host (adamw_elem in common.cuh: one square root and one division per
+// element, the form torch.optim.AdamW uses):
+//   p *= 1 - lr*wd ; m = b1*m + (1-b1)*g ; v = b2*v + (1-b2)*g*g
+//   p -= (lr/b1t) * m / (sqrt(v)/sqrt(b2t) + eps)
+// The bit-exact reference order lives in the fp64 host path (ops/optim.py).  It
+// runs over one flat fp32 master buffer (all parameters, or a ZeRO shard), and also
 // refreshes the bf16 working copy the GEMMs read.  Global-norm clipping
 // (dtrain/optim.py:49-52, dtrain/train.py:155-158) is applied on the device: the
 // kernel reads the squared norm produced by grad_sqnorm and computes the clip
@@ -25,9 +28,8 @@ __device__ __forceinline__ float clip_factor(const double* sq, float max_norm) {
 }
 
 __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
-                             float* __restrict__ v, bf16* __restrict__ p16, long n, float lr, float b1, float b2,
-                             float eps, float wd, float b1t, float b2t, const double* __restrict__ sq,
-                             float max_norm) {
+                             float* __restrict__ v, bf16* __restrict__ p16, long n, AdamConsts ak,
+                             const double* __restrict__ sq, float max_norm) {
   const float cs = clip_factor(sq, max_norm);
   const long stride = (long)gridDim.x * blockDim.x * 4;
   for (long i = ((long)blockIdx.x * blockDim.x + threadIdx.x) * 4; i < n; i += stride) {
@@ -36,18 +38,10 @@ __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
       const float4 gv = *reinterpret_cast<const float4*>(g + i);
       float4 mv = *reinterpret_cast<float4*>(m + i);
       float4 vv = *reinterpret_cast<float4*>(v + i);
-      float* pa = &pv.x;
-      const float* ga = &gv.x;
-      float* ma = &mv.x;
-      float* va = &vv.x;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float gg = ga[j] * cs;
-        ma[j] = b1 * ma[j] + (1.f - b1) * gg;
-        va[j] = b2 * va[j] + (1.f - b2) * (gg * gg);
-        pa[j] -= lr * (wd * pa[j]);
-        pa[j] -= lr * (ma[j] / b1t) / (sqrtf(va[j] / b2t) + eps);
-      }
+      adamw_elem(pv.x, gv.x * cs, mv.x, vv.x, ak);
+      adamw_elem(pv.y, gv.y * cs, mv.y, vv.y, ak);
+      adamw_elem(pv.z, gv.z * cs, mv.z, vv.z, ak);
+      adamw_elem(pv.w, gv.w * cs, mv.w, vv.w, ak);
       *reinterpret_cast<float4*>(p + i) = pv;
       *reinterpret_cast<float4*>(m + i) = mv;
       *reinterpret_cast<float4*>(v + i) = vv;
@@ -59,12 +53,12 @@ __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
       }
     } else {
       for (long k = i; k < n; ++k) {
-        const float gg = g[k] * cs;
-        m[k] = b1 * m[k] + (1.f - b1) * gg;
-        v[k] = b2 * v[k] + (1.f - b2) * (gg * gg);
-        p[k] -= lr * (wd * p[k]);
-        p[k] -= lr * (m[k] / b1t) / (sqrtf(v[k] / b2t) + eps);
-        if (p16) p16[k] = f2bf(p[k]);
+        float pp = p[k], mm = m[k], vv2 = v[k];
+        adamw_elem(pp, g[k] * cs, mm, vv2, ak);
+        p[k] = pp;
+        m[k] = mm;
+        v[k] = vv2;
+        if (p16) p16[k] = f2bf(pp);
       }
     }
   }
@@ -150,13 +144,11 @@ void adamw_step(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor
     TORCH_CHECK(sq->scalar_type() == at::kDouble && sq->numel() >= 1, "adamw_step: sq fp64");
     sqp = sq->data_ptr<double>();
   }
-  const float b1t = (float)(1.0 - std::pow(b1, (double)t));
-  const float b2t = (float)(1.0 - std::pow(b2, (double)t));
   if (n == 0) return;
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   adamw_kernel<<<grid_for(n, 4), 256, 0, st>>>(p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(),
-                                              v.data_ptr<float>(), q, n, (float)lr, (float)b1, (float)b2,
-                                              (float)eps, (float)wd, b1t, b2t, sqp, (float)max_norm);
+                                              v.data_ptr<float>(), q, n, adam_consts(lr, b1, b2, eps, wd, t), sqp,
+                                              (float)max_norm);
   count_launch();
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
