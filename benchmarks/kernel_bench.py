@@ -115,7 +115,8 @@ def main():
         y, mu, rs = K.layernorm_fwd(x, w, b)
         dw = torch.empty(C, device=dev)
         db = torch.empty(C, device=dev)
-        rep("ln_bwd", timeit(lambda: K.layernorm_bwd(y, x, w, mu, rs, y, dw, db), a.iters), nbytes=4 * N * C * 2)
+        dres = torch.randn_like(x)
+        rep("ln_bwd", timeit(lambda: K.layernorm_bwd(y, x, w, mu, rs, dres, dw, db), a.iters), nbytes=4 * N * C * 2)
         rep("bias_grad_fc", timeit(lambda: K.bias_grad(torch.empty(N, 4 * C, device=dev, dtype=torch.bfloat16),
                                                        torch.empty(4 * C, device=dev)), a.iters),
             nbytes=N * 4 * C * 2)
