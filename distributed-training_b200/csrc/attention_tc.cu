@@ -8,15 +8,16 @@
 // One CTA = one (batch*head, pair of 128-query tiles A and B); the two tiles share
 // every K/V tile that both need.  10 warps:
 //   warp 0      TMA: Q_A, Q_B once; K_j, V_j through 3-stage rings (128 keys x 64).
-//   warp 1      owns 512 TMEM columns (S_A, S_B: 128 each; O_A, O_B: 64 each); one
-//               lane issues  S_t = Q_t K_j^T  (M=128, N=128, K=64) and
-//               O_t += P_t V_j (M=128, N=64, K=128), committing to mbarriers.
+//   warp 1      owns 512 TMEM columns (S_A, S_B: 128 each; O_A, O_B: 64 each; bf16
+//               P_A, P_B: 64 each); one lane issues  S_t = Q_t K_j^T  (M=128, N=128,
+//               K=64, both operands in shared memory) and O_t += P_t V_j (M=128,
+//               N=64, K=128, A = P_t read from TMEM), committing to mbarriers.
 //   warps 2..5  softmax for tile A, warps 6..9 for tile B: each thread owns one
 //               query row, loads its 128 scores from TMEM, applies the causal mask,
 //               keeps the running max / sum in registers (no shuffles), writes
-//               P = exp2(s*scale*log2e - m) as bf16 into 128B-swizzled shared memory
-//               (the K-major A operand of the PV MMA) and rescales its O row in
-//               TMEM when the running max moved.
+//               P = exp2(s*scale*log2e - m) as bf16 into its own TMEM lane (the A
+//               operand of the PV MMA, so P never touches shared memory) and
+//               rescales its O row in TMEM when the running max moved.
 // A tile's next scores S_t(j+1) are computed while its softmax of step j runs (the
 // scores are copied to registers first), and its PV runs while the softmax of
 // step j+1 computes exponentials, so the softmax warps run back to back and the
@@ -42,11 +43,11 @@ constexpr int STAGES = 3;
 constexpr int OFF_Q = 0;
 constexpr int OFF_K = OFF_Q + 2 * TILE;
 constexpr int OFF_V = OFF_K + STAGES * TILE;
-constexpr int OFF_P = OFF_V + STAGES * TILE;
-constexpr int OFF_BAR = OFF_P + 2 * PBYTES;
+constexpr int OFF_BAR = OFF_V + STAGES * TILE;
 constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
 constexpr uint32_t TM_S = 0;    // S_t at column t*128
 constexpr uint32_t TM_O = 256;  // O_t at column 256 + t*64
+constexpr uint32_t TM_P = 384;  // bf16 P_t (64 packed columns) at 384 + t*64: the A operand of O += P V
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
   asm volatile(
@@ -60,6 +61,11 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
       : "memory");
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(taddr), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+}
 
 // 2^x on the special-function unit (PTX ex2.approx; 2^-inf = +0).
 __device__ __forceinline__ float ex2_fast(float x) {
@@ -273,11 +279,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (j > (2 * pair + t)) continue;
           if (!mbar_wait(&bars->p_full[t], j & 1, abort_flag)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t pbase = smem_u32(smem + OFF_P + t * PBYTES);
 #pragma unroll
-          for (int kk = 0; kk < BKV / 16; ++kk)
-            tc_mma_f16(tmem + TM_O + t * D, make_sw128_desc(pbase + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
-                       make_sw128_desc(vbase + kk * 2048, 8192, 1024), id_pv, (j > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < BKV / 16; ++kk)  // A = P_t from TMEM, 8 packed columns per K=16 slice
+            tc_mma_f16_ts(tmem + TM_O + t * D, tmem + TM_P + t * 64 + kk * 8,
+                          make_sw128_desc(vbase + kk * 2048, 8192, 1024), id_pv, (j > 0 || kk > 0) ? 1u : 0u);
           tc_commit(&bars->o_done[t]);
         }
         if (!ok) break;
@@ -293,7 +298,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = q * 32 + lane;             // row within the tile (= TMEM lane)
     const int qrow = qtile * BQ + r;         // query index within the sequence
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-    uint8_t* P = smem + OFF_P + t * PBYTES;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     if (active) {
@@ -341,9 +345,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         // issued when this tile's previous P was published, so this rarely waits
         if (j > 0 && !mbar_wait(&bars->o_done[t], (j - 1) & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        // exponentials, row sum and the bf16 P row (K-major, 128B swizzle, two 64-key
-        // atoms) in one pass of 8-column chunks, so the special-function unit (ex2),
-        // the integer pipe (packing) and the shared-memory stores run concurrently
+        // exponentials, row sum and the bf16 P row (into this thread's TMEM lane, the A
+        // operand of the PV product) in one pass of 8-column chunks, so the
+        // special-function unit (ex2), the packing and the TMEM stores run concurrently
         float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
 #pragma unroll
         for (int ch = 0; ch < BKV / 8; ++ch) {
@@ -369,9 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int e = 0; e < 4; ++e)
             w[e] = kPackInt ? pack_bf16x2_pos(x[2 * e], x[2 * e + 1]) : pack_bf16x2(x[2 * e], x[2 * e + 1]);
-          const int atom = ch >> 3, k16 = ch & 7;
-          *reinterpret_cast<uint4*>(P + atom * 16384 + r * 128 + ((k16 ^ (r & 7)) << 4)) =
-              make_uint4(w[0], w[1], w[2], w[3]);
+          tmem_st4(tmem + lane_off + TM_P + t * 64 + ch * 4, w[0], w[1], w[2], w[3]);
         }
         l = l * alpha + ((s0 + s1) + (s2 + s3));
         // rescale this row of O when the running max moved (warp-uniform decision)
@@ -385,9 +387,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
             tmem_st32(tmem + lane_off + TM_O + t * D + half * 32, o);
           }
-          tmem_wait_st();
         }
-        fence_proxy_async_smem();
+        tmem_wait_st();  // P (and a rescaled O) are in TMEM before the PV product is released
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->p_full[t]);
@@ -453,6 +454,7 @@ constexpr int BW_OFF_P = 8 * TILE;              // [t] bf16 P then dS (128 query
 constexpr int BW_OFF_BAR = BW_OFF_P + 2 * PBYTES;
 constexpr int BW_SMEM = BW_OFF_BAR + 512 + 1024;
 constexpr uint32_t BW_X = 0, BW_G = 256;        // X_t at t*128; G0_t at 256 + t*128, G1_t at 256 + t*128 + 64
+constexpr uint32_t BW_DS = 64;                   // dq: bf16 dS_t (64 packed columns) at 256 + t*128 + 64
 
 struct BwBars {
   uint64_t fixed_full;
@@ -602,9 +604,11 @@ __global__ void __launch_bounds__(BW_THREADS, 1)
         const uint32_t pa = SP + t * PBYTES;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t ad = DKDV ? make_sw128_desc(pa + kk * 2048, 16384, 1024)           // A = P^T / dS^T (MN-major)
-                                   : make_sw128_desc(pa + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);  // A = dS
-          tc_mma_f16(tmem + col, ad, make_sw128_desc(btile + kk * 2048, 8192, 1024), id_g, (acc || kk > 0) ? 1u : 0u);
+          const uint64_t bd = make_sw128_desc(btile + kk * 2048, 8192, 1024);
+          if (DKDV)  // A = P^T / dS^T, read MN-major from shared memory
+            tc_mma_f16(tmem + col, make_sw128_desc(pa + kk * 2048, 16384, 1024), bd, id_g, (acc || kk > 0) ? 1u : 0u);
+          else       // A = dS from tensor memory (BW_DS columns of sub-tile t)
+            tc_mma_f16_ts(tmem + col, tmem + BW_G + t * 128 + BW_DS + kk * 8, bd, id_g, (acc || kk > 0) ? 1u : 0u);
         }
       };
       bool ok = mbar_wait(&bars->fixed_full, 0, abort_flag);
@@ -795,8 +799,15 @@ __global__ void __launch_bounds__(BW_THREADS, 1)
           break;
         }
         tc_fence_after();
-        put_row128(A, r, pk);
-        fence_proxy_async_smem();
+        if (DKDV) {
+          put_row128(A, r, pk);
+          fence_proxy_async_smem();
+        } else {  // dS row -> this thread's TMEM lane, the A operand of dQ += dS K_j
+          const uint32_t dcol = tmem + lane_off + BW_G + t * 128 + BW_DS;
+          tmem_st32(dcol, pk);
+          tmem_st32(dcol + 32, pk + 32);
+          tmem_wait_st();
+        }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars->ds_ready[t]);
