@@ -128,8 +128,9 @@ __global__ void ln_fwd_kernel(const bf16* __restrict__ x, const bf16* __restrict
 constexpr int kLnBwdWarps = 8;
 constexpr int kLnBwdRowsPerBlock = 64;
 
-// Dynamic shared memory of ln_bwd_kernel: per-warp column accumulators [3][C].
-static inline size_t ln_bwd_smem(int C) { return (size_t)kLnBwdWarps * 3 * C * sizeof(float); }
+// Dynamic shared memory of ln_bwd_kernel<NCH>: per-warp column accumulators
+// [3][NCH * 256] (rows padded to whole 256-column chunks).
+static inline size_t ln_bwd_smem(int nch) { return (size_t)kLnBwdWarps * 3 * nch * 256 * sizeof(float); }
 
 // Block b handles rows [b*64, b*64+64); warp k handles rows b*64 + k, +8, ... and
 // prefetches its next row while it computes the current one (the row's dy, x and
@@ -144,10 +145,11 @@ __global__ void __launch_bounds__(kLnBwdWarps * 32, 2)
                   const float* __restrict__ mean, const float* __restrict__ rstd, const bf16* __restrict__ dresid,
                   bf16* __restrict__ dx, float* __restrict__ part_w, float* __restrict__ part_b,
                   float* __restrict__ part_r, int rows, int C) {
-  extern __shared__ float sm[];  // [kLnBwdWarps][3][C]
+  constexpr int RS = NCH * 256;  // accumulator row stride (floats)
+  extern __shared__ float sm[];  // [kLnBwdWarps][3][RS]
   const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float* acc = sm + (size_t)wid * 3 * C;
-  for (int i = lane * 4; i < 3 * C; i += 128) *reinterpret_cast<float4*>(acc + i) = make_float4(0.f, 0.f, 0.f, 0.f);
+  float* acc = sm + (size_t)wid * 3 * RS;
+  for (int i = lane * 4; i < 3 * RS; i += 128) *reinterpret_cast<float4*>(acc + i) = make_float4(0.f, 0.f, 0.f, 0.f);
   __syncwarp();
   const bool has_r = dresid != nullptr;
   const int r0 = blockIdx.x * kLnBwdRowsPerBlock;
@@ -181,9 +183,11 @@ __global__ void __launch_bounds__(kLnBwdWarps * 32, 2)
         unpack8(cy[c], g);
         unpack8(cx[c], xv);
         ld8(w + col, wv);  // 1.5-6 KB of weights: L1-resident across rows
-        float4* aw = reinterpret_cast<float4*>(acc + col);
-        float4* ab = reinterpret_cast<float4*>(acc + C + col);
-        float4 w0 = aw[0], w1 = aw[1], b0 = ab[0], b1 = ab[1];
+        // accumulator rows are lane-interleaved (float4 (c, h) of lane l at ((2c+h)*32+l)*4), so a
+        // warp's float4 accesses are contiguous 512-byte runs without bank conflicts
+        float4* aw = reinterpret_cast<float4*>(acc) + (2 * c) * 32 + lane;
+        float4* ab = reinterpret_cast<float4*>(acc + RS) + (2 * c) * 32 + lane;
+        float4 w0 = aw[0], w1 = aw[32], b0 = ab[0], b1 = ab[32];
         float dwv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
         float dbv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
@@ -196,15 +200,15 @@ __global__ void __launch_bounds__(kLnBwdWarps * 32, 2)
           dbv[j] += g[j];
         }
         aw[0] = make_float4(dwv[0], dwv[1], dwv[2], dwv[3]);
-        aw[1] = make_float4(dwv[4], dwv[5], dwv[6], dwv[7]);
+        aw[32] = make_float4(dwv[4], dwv[5], dwv[6], dwv[7]);
         ab[0] = make_float4(dbv[0], dbv[1], dbv[2], dbv[3]);
-        ab[1] = make_float4(dbv[4], dbv[5], dbv[6], dbv[7]);
+        ab[32] = make_float4(dbv[4], dbv[5], dbv[6], dbv[7]);
         if (part_r) {
           unpack8(cr[c], rv);
-          float4* ar = reinterpret_cast<float4*>(acc + 2 * C + col);
-          float4 r0v = ar[0], r1v = ar[1];
+          float4* ar = reinterpret_cast<float4*>(acc + 2 * RS) + (2 * c) * 32 + lane;
+          float4 r0v = ar[0], r1v = ar[32];
           ar[0] = make_float4(r0v.x + rv[0], r0v.y + rv[1], r0v.z + rv[2], r0v.w + rv[3]);
-          ar[1] = make_float4(r1v.x + rv[4], r1v.y + rv[5], r1v.z + rv[6], r1v.w + rv[7]);
+          ar[32] = make_float4(r1v.x + rv[4], r1v.y + rv[5], r1v.z + rv[6], r1v.w + rv[7]);
         }
       }
     }
@@ -238,10 +242,14 @@ __global__ void __launch_bounds__(kLnBwdWarps * 32, 2)
   __syncthreads();
   // combine the warps of this block in warp order
   const int narr = part_r ? 3 : 2;
-  for (int i = threadIdx.x; i < narr * C; i += blockDim.x) {
+  for (int i = threadIdx.x; i < narr * RS; i += blockDim.x) {
+    // undo the lane interleave: index j within a row is ((2c+h)*32 + lane)*4 + e
+    const int a = i / RS, j = i - a * RS;
+    const int e = j & 3, lane_j = (j >> 2) & 31, ch = j >> 7;  // ch = 2c + h
+    const int col = ((ch >> 1) * 32 + lane_j) * 8 + (ch & 1) * 4 + e;
+    if (col >= C) continue;
     float t = 0.f;
-    for (int k = 0; k < kLnBwdWarps; ++k) t += sm[(size_t)k * 3 * C + i];
-    const int a = i / C, col = i - a * C;
+    for (int k = 0; k < kLnBwdWarps; ++k) t += sm[(size_t)k * 3 * RS + i];
     float* dst = a == 0 ? part_w : (a == 1 ? part_b : part_r);
     dst[(long)blockIdx.x * C + col] = t;
   }
@@ -386,7 +394,6 @@ torch::Tensor layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, 
               "layernorm_bwd: dres_sum needs dresid and an fp32 [C] output");
   auto part = torch::empty({rsum ? 3 : 2, nblk, C}, x.options().dtype(at::kFloat));
   const int nch = ln_chunks(C);
-  const size_t smem = ln_bwd_smem(C);
   auto* dyp = reinterpret_cast<const bf16*>(dy.data_ptr());
   auto* xp = reinterpret_cast<const bf16*>(x.data_ptr());
   auto* wp = reinterpret_cast<const bf16*>(w.data_ptr());
@@ -397,6 +404,7 @@ torch::Tensor layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, 
 #define LNB(NC)                                                                                          \
   {                                                                                                      \
     auto k = ln_bwd_kernel<NC>;                                                                          \
+    const size_t smem = ln_bwd_smem(NC);                                                                 \
     if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
     k<<<nblk, kLnBwdWarps * 32, smem, st>>>(dyp, xp, wp, mean.data_ptr<float>(), rstd.data_ptr<float>(), dr, dxp, pw, pb, pr, rows, C); \
   }
@@ -550,7 +558,6 @@ extern "C" __attribute__((visibility("default"))) int dtb_layernorm_bwd_noalloc(
   float* pw = scratch;
   float* pb = scratch + nblk * C;
   const int nch = (C + 255) / 256;
-  const size_t smem = ln_bwd_smem(C);
   auto* dyp = static_cast<const bf16*>(dy);
   auto* xp = static_cast<const bf16*>(x);
   auto* wp = static_cast<const bf16*>(w);
@@ -559,6 +566,7 @@ extern "C" __attribute__((visibility("default"))) int dtb_layernorm_bwd_noalloc(
 #define DTB_LNB_NOALLOC(NC)                                                                                       \
   {                                                                                                               \
     auto k = ln_bwd_kernel<NC>;                                                                                   \
+    const size_t smem = ln_bwd_smem(NC);                                                                          \
     if (smem > 48 * 1024 && cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=     \
                                 cudaSuccess)                                                                      \
       return DTB_NOALLOC_LAUNCH_FAILED;                                                                           \

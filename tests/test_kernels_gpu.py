@@ -94,7 +94,7 @@ def test_gemm_deterministic():
     assert torch.equal(a, b)
 
 
-@pytest.mark.parametrize("rows,C", [(37, 64), (1024, 768), (300, 1024), (64, 2048)])
+@pytest.mark.parametrize("rows,C", [(37, 64), (1024, 768), (300, 1024), (64, 2048), (129, 264), (70, 1288)])
 def test_layernorm(rows, C):
     x = torch.randn(rows, C, device="cuda").bfloat16()
     w = (1 + 0.1 * torch.randn(C, device="cuda")).bfloat16()
@@ -110,10 +110,14 @@ def test_layernorm(rows, C):
     yr.backward(dy.float())
     dw = torch.empty(C, device="cuda")
     db = torch.empty(C, device="cuda")
-    dx = K.layernorm_bwd(dy, x, w, mu, rs, dres, dw, db)
+    dsum = torch.empty(C, device="cuda")
+    dx = K.layernorm_bwd(dy, x, w, mu, rs, dres, dw, db, dres_sum=dsum)
     assert _rel(dx, xf.grad + dres.float()) < 2e-2
     assert _rel(dw, wf.grad) < 1e-3
     assert _rel(db, bf.grad) < 1e-3
+    assert _rel(dsum, dres.float().sum(0)) < 1e-4  # column sums of the residual gradient
+    dx2 = K.layernorm_bwd(dy, x, w, mu, rs, dres, dw.clone(), db.clone(), dres_sum=dsum.clone())
+    assert torch.equal(dx, dx2)
 
 
 def test_bias_grad():
