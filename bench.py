@@ -137,7 +137,8 @@ def run_ours(a, rank, world, local):
     torch.cuda.set_device(dev)
     if world > 1:
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
-        pg = NVLinkGroup(rank, world, dev, torch_exchange(), timeout=120.0)
+        pg = NVLinkGroup(rank, world, dev, torch_exchange(), timeout=120.0, blocks=a.comm_blocks,
+                         comm_priority=a.comm_priority)
     else:
         pg = NVLinkGroup(0, 1, dev, lambda k, p: [p], timeout=120.0)
     C = CONFIGS[a.config]
@@ -145,7 +146,8 @@ def run_ours(a, rank, world, local):
     args = T.parse(["--mode", C["mode"], "--dtype", "bfloat16", "--batch", str(seq), "--ctx", str(M["ctx"]),
                     "--dim", str(M["dim"]), "--heads", str(M["heads"]), "--layers", str(M["layers"]),
                     "--lr", "6e-4", "--clip", "1.0", "--bucket-mb", str(a.bucket_mb), "--data", "synthetic",
-                    "--vocab", str(M["vocab"]), "--algo", a.algo, "--accum", str(accum)])
+                    "--vocab", str(M["vocab"]), "--algo", a.algo, "--accum", str(accum)]
+                   + ([] if a.overlap else ["--no-overlap"]))
     cfg = GPTConfig(dtype="bfloat16", **M)
     tr = T.Trainer(args, cfg, dev, pg)
     data = SyntheticData(M["vocab"])
@@ -187,6 +189,9 @@ def run_ours(a, rank, world, local):
         "config": {"model": C["name"], "global_batch": seq * accum * world,
                    "seq_len": M["ctx"], "parallelism": f"{'dp' if C['mode'] == 'ddp' else 'zero1-dp'}{world}",
                    "grad_accum": accum, "bucket_mb": a.bucket_mb if C["mode"] == "ddp" else None,
+                   "grad_sync": ("per-bucket all-reduce overlapped with backward" if a.overlap else
+                                 "one all-reduce of the flat gradient after backward") if C["mode"] == "ddp" else
+                   "reduce-scatter + fused AdamW/all-gather",
                    "optimizer": "AdamW, clip 1.0", "allreduce_order": a.algo,
                    "l2": "no flush: weights/activations/logits per step >> 126 MB L2"},
         "e2e": {"value": tokens * a.steps / (ms_e2e / 1e3), "unit": "tokens/s",
@@ -294,6 +299,11 @@ def main():
     ap.add_argument("--bucket-mb", type=float, default=1.0)
     ap.add_argument("--algo", choices=["ring", "direct"], default="ring")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="gpt2-small-ddp")
+    ap.add_argument("--comm-blocks", type=int, default=0, help="CTAs per collective kernel (0: by size)")
+    ap.add_argument("--comm-priority", type=int, default=0, help="CUDA priority of the collective stream")
+    ap.add_argument("--overlap", action="store_true",
+                    help="all-reduce each gradient bucket during backward (default: one all-reduce of the flat "
+                         "gradient after backward, measured faster on B200)")
     a = ap.parse_args()
     if a.warmup < 3:
         a.warmup = 3

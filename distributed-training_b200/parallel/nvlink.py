@@ -103,9 +103,14 @@ class GPUWork:
 class NVLinkGroup:
     backend = "nvlink"
 
-    def __init__(self, rank: int, world: int, device, exchange, timeout: float = 60.0, blocks: int = 0):
+    def __init__(self, rank: int, world: int, device, exchange, timeout: float = 60.0, blocks: int = 0,
+                 comm_priority: int = 0):
         """``exchange(key, payload: bytes) -> list[bytes]`` is the bootstrap all-gather
-        (over the rendezvous store or torch.distributed); it is used only at set-up."""
+        (over the rendezvous store or torch.distributed); it is used only at set-up.
+        ``blocks`` caps the CTAs of one collective kernel (0: sized by the message);
+        ``comm_priority`` is the CUDA priority of the stream that runs the asynchronous
+        collectives (lower is more urgent: -1 lets their CTAs take SMs ahead of queued
+        compute work)."""
         if world > int(lib().comm_max_ranks()):
             raise ValueError(f"NVLinkGroup supports up to {lib().comm_max_ranks()} ranks per node")
         self.rank, self.world = int(rank), int(world)
@@ -121,7 +126,7 @@ class NVLinkGroup:
             self._sig = self._new_buffer(_SIG_BYTES)
             # native state: signal pads, registered buffers, flag epoch, timeout
             self._eng = lib().CommEngine(self.rank, self.world, self._sig.ptrs, float(timeout), self.blocks)
-            self.comm_stream = torch.cuda.Stream(device=self.device)
+            self.comm_stream = torch.cuda.Stream(device=self.device, priority=int(comm_priority))
         self._staging: SymmetricBuffer | None = None
         self._sq_parts = None
         self.barrier()

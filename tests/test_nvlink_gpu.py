@@ -240,13 +240,13 @@ def test_zero1_matches_ddp_adamw_on_gpu():
     assert sum(r[2] for r in res) == 8 * n  # fp32 m and v, sharded exactly once across ranks
 
 
-def _ddp_step(pg, bucket_mb):
+def _ddp_step(pg, bucket_mb, overlap=True):
     import torch
     from dtrain_b200.models.gpt import GPT, GPTConfig
     from dtrain_b200.parallel.ddp import DDP
     cfg = GPTConfig(vocab=512, ctx=128, dim=128, heads=2, layers=2, dtype="bfloat16")
     m = GPT(cfg, seed=0)
-    ddp = DDP(m, pg, bucket_mb=bucket_mb)
+    ddp = DDP(m, pg, bucket_mb=bucket_mb, overlap=overlap)
     g = torch.Generator().manual_seed(0)
     xs = torch.randint(0, 512, (2 * pg.world, 128), generator=g)
     ys = torch.randint(0, 512, (2 * pg.world, 128), generator=g)
@@ -260,10 +260,10 @@ def _ddp_step(pg, bucket_mb):
 
 
 @needs2
-@pytest.mark.parametrize("bucket_mb", [0.01, 25.0])
-def test_ddp_gradients_match_single_process_and_agree_across_ranks(bucket_mb):
+@pytest.mark.parametrize("bucket_mb,overlap", [(0.01, True), (25.0, True), (1.0, False)])
+def test_ddp_gradients_match_single_process_and_agree_across_ranks(bucket_mb, overlap):
     from dtrain_b200.models.gpt import GPT, GPTConfig
-    res = _run(2, _ddp_step, bucket_mb)
+    res = _run(2, _ddp_step, bucket_mb, overlap)
     assert np.array_equal(res[0], res[1]), "DDP gradients must be bit-identical across ranks"
     cfg = GPTConfig(vocab=512, ctx=128, dim=128, heads=2, layers=2, dtype="bfloat16")
     m = GPT(cfg, seed=0)
