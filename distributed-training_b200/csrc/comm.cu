@@ -178,6 +178,52 @@ __device__ __forceinline__ float4 reduce_vec4(const Peers& in, long i, int W, in
   }
 }
 
+// Vectorised bf16 reduction of 8 elements starting at i (one 16-byte load per
+// rank, all issued before the first add), summed in fp32 in the fixed order
+// first, first+1, ... exactly like reduce_elem<bf16>.
+template <int WT>
+__device__ __forceinline__ void reduce_vec8_bf16(const Peers& in, long i, int W, int first, float* acc) {
+  auto add8 = [&](const uint4& u, bool init) {
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(h[e]);
+      acc[2 * e] = init ? f.x : acc[2 * e] + f.x;
+      acc[2 * e + 1] = init ? f.y : acc[2 * e + 1] + f.y;
+    }
+  };
+  if constexpr (WT > 0) {
+    uint4 v[WT];
+#pragma unroll
+    for (int k = 0; k < WT; ++k) {
+      int r = first + k;
+      r -= (r >= WT) ? WT : 0;
+      v[k] = __ldcg(reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(in.p[r]) + i));
+    }
+#pragma unroll
+    for (int k = 0; k < WT; ++k) add8(v[k], k == 0);
+  } else {
+    int r = first;
+    for (int k = 0; k < W; ++k) {
+      add8(__ldcg(reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(in.p[r]) + i)), k == 0);
+      r = (r + 1 == W) ? 0 : r + 1;
+    }
+  }
+}
+
+template <typename TO>
+__device__ __forceinline__ void store8(TO* out, const float* v);
+template <>
+__device__ __forceinline__ void store8<float>(float* out, const float* v) {
+  *reinterpret_cast<float4*>(out) = make_float4(v[0], v[1], v[2], v[3]);
+  *reinterpret_cast<float4*>(out + 4) = make_float4(v[4], v[5], v[6], v[7]);
+}
+template <>
+__device__ __forceinline__ void store8<bf16>(bf16* out, const float* v) {
+  *reinterpret_cast<uint4*>(out) = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
+                                              pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+}
+
 // Reduce elements [a, b) into `out` (index space of the buffer), scaled.
 // If sq != nullptr, also accumulate sum of squares of the written values (fp64).
 // All ranks' buffers share one byte offset from 256-byte aligned bases, so they
@@ -224,6 +270,56 @@ __device__ __forceinline__ void reduce_range(const Peers& in, TO* out, long a, l
     for (long i = max(ve, head) + threadIdx.x; i < b; i += blockDim.x) {
       const float v = reduce_elem<TI>(in, i, W, first) * scale;
       out[i] = v;
+      s += (double)v * v;
+    }
+  } else if constexpr (std::is_same<TI, bf16>::value) {
+    // 8 bf16 per vector: input phase 16 B, output phase 16 B (bf16) or 32 B (fp32)
+    const uintptr_t ain = reinterpret_cast<uintptr_t>(reinterpret_cast<const bf16*>(in.p[first]) + a);
+    const uintptr_t aout = reinterpret_cast<uintptr_t>(out + a);
+    constexpr uintptr_t kOutAlign = 16;
+    long head = a, ve = a;
+    if ((ain & 1) == 0) {
+      const long to_in = (long)(((16 - (ain & 15)) & 15) / 2);
+      const uintptr_t out_at = aout + to_in * sizeof(TO);
+      if ((out_at & (kOutAlign - 1)) == 0) {
+        head = min(b, a + to_in);
+        ve = head + ((b - head) & ~7L);
+      }
+    }
+    for (long i = a + threadIdx.x; i < head; i += blockDim.x) {
+      const float v = reduce_elem<TI>(in, i, W, first) * scale;
+      stf<TO>(out + i, v);
+      s += (double)v * v;
+    }
+    // two vectors per thread per iteration: 2*WT 16-byte loads in flight
+    const long step = (long)blockDim.x * 8;
+    long i = head + threadIdx.x * 8;
+    for (; i + step < ve; i += 2 * step) {
+      float v0[8], v1[8];
+      reduce_vec8_bf16<WT>(in, i, W, first, v0);
+      reduce_vec8_bf16<WT>(in, i + step, W, first, v1);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        v0[e] *= scale;
+        v1[e] *= scale;
+        if (sq) s += (double)v0[e] * v0[e] + (double)v1[e] * v1[e];
+      }
+      store8<TO>(out + i, v0);
+      store8<TO>(out + i + step, v1);
+    }
+    for (; i < ve; i += step) {
+      float v[8];
+      reduce_vec8_bf16<WT>(in, i, W, first, v);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        v[e] *= scale;
+        if (sq) s += (double)v[e] * v[e];
+      }
+      store8<TO>(out + i, v);
+    }
+    for (long i = max(ve, head) + threadIdx.x; i < b; i += blockDim.x) {
+      const float v = reduce_elem<TI>(in, i, W, first) * scale;
+      stf<TO>(out + i, v);
       s += (double)v * v;
     }
   } else {

@@ -267,7 +267,9 @@ class NVLinkGroup:
         return flat[b[self.rank]:b[self.rank + 1]]
 
     def _rs_blocks(self) -> int:
-        return self.blocks or 32
+        # a fixed CTA count (the ZeRO update reads exactly this many squared-norm
+        # partials per rank); 64 CTAs keep enough peer loads in flight for NVLink
+        return self.blocks or 64
 
     def all_gather(self, flat: torch.Tensor):
         if self.world > 1:
