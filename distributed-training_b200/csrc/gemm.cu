@@ -381,6 +381,214 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// -------------------------------------------------------------------------
+// 2-SM variant: a cluster of two CTAs computes 256x256 output tiles with
+// tcgen05 cta_group::2 (M=256, N=256, K=16 per instruction).  CTA r of the pair
+// loads A rows [m0 + 128r, +128) and B columns [n0 + 128r, +128) into its own
+// shared memory (32 KB per k-block instead of the 48 KB a 1-SM 128x256 tile
+// needs), the leader's single MMA thread multiplies the pair's operands, and
+// each CTA's TMEM receives its 128 rows of the 256x256 accumulator.  This halves
+// B's shared-memory and L2 traffic per SM, which bounds the 1-SM mainloop.
+// Barriers: full (leader; TMA bytes of both CTAs), empty / tile-full (both CTAs,
+// arrived by the leader's multicast commit), tile-empty (leader; 2x8 epilogue
+// warps, the peer's arrive remotely), done (end-of-kernel handshake).  Every
+// wait is bounded; the only cluster barrier is the one after set-up.
+struct Gemm2Cfg {
+  static constexpr int A_BYTES = kBM * kBK * 2;        // 16 KB: this CTA's 128 rows
+  static constexpr int B_BYTES = 128 * kBK * 2;        // 16 KB: this CTA's 128 columns
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = 6;
+  static constexpr int TMEM_COLS = 512;                // two 256-column accumulators
+  static constexpr int EPI_BYTES = kEpiWarps * kEpiSlab;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
+};
+
+template <bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmAux,
+                    GemmArgs args) {
+  using Cfg = Gemm2Cfg;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* epi_smem = smem + Cfg::STAGES * Cfg::STAGE_BYTES;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(epi_smem + Cfg::EPI_BYTES);
+  uint64_t* empty_bar = full_bar + Cfg::STAGES;
+  uint64_t* tfull_bar = empty_bar + Cfg::STAGES;  // [2]
+  uint64_t* tempty_bar = tfull_bar + 2;           // [2]
+  uint64_t* done_bar = tempty_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Cfg::STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull_bar[b], 1);
+      mbar_init(&tempty_bar[b], 2 * kEpiWarps);
+    }
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init_cluster();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs' barriers initialised and TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int M = args.M, N = args.N, K = args.K;
+  const int mt = (M + 255) / 256;
+  const int nt = (N + 255) / 256;
+  const int kb_total = (K + kBK - 1) / kBK;
+  const int splits = args.splits;
+  const int units = mt * nt * splits;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ TMA producer (both CTAs)
+      const uint32_t lead_full0 = mapa_shared(&full_bar[0], 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int u = pair; u < units && ok; u += npairs) {
+        const int t = u / splits, sp = u % splits;
+        int mi, ni;
+        tile_coords(t, mt, nt, mi, ni);
+        const int m0 = mi * 256 + (int)rank * 128, n0 = ni * 256 + (int)rank * 128;
+        const int kb0 = (int)((long)kb_total * sp / splits), kb1 = (int)((long)kb_total * (sp + 1) / splits);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag)) { ok = false; break; }
+          uint8_t* sA = smem + stage * Cfg::STAGE_BYTES;
+          uint8_t* sB = sA + Cfg::A_BYTES;
+          const uint32_t fb = lead_full0 + (uint32_t)(stage * sizeof(uint64_t));
+          if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * Cfg::STAGE_BYTES);
+          const int k0 = kb * kBK;
+          if (!A_MN) {
+            tma_load_2d_pair(&tmA, sA, fb, k0, m0);
+          } else {
+            tma_load_2d_pair(&tmA, sA, fb, m0, k0);
+            tma_load_2d_pair(&tmA, sA + 8192, fb, m0 + 64, k0);
+          }
+          if (!B_MN) {
+            tma_load_2d_pair(&tmB, sB, fb, k0, n0);
+          } else {
+            tma_load_2d_pair(&tmB, sB, fb, n0, k0);
+            tma_load_2d_pair(&tmB, sB + 8192, fb, n0 + 64, k0);
+          }
+          if (++stage == Cfg::STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ------------------------------------------------------------ MMA issuer (leader only)
+      constexpr uint32_t idesc = make_idesc_bf16(256, 256, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int ab = 0;
+      uint32_t aphase = 0;
+      bool ok = true;
+      for (int u = pair; u < units && ok; u += npairs) {
+        const int sp = u % splits;
+        const int kb0 = (int)((long)kb_total * sp / splits), kb1 = (int)((long)kb_total * (sp + 1) / splits);
+        if (!mbar_wait(&tempty_bar[ab], aphase ^ 1, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(ab * 256);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t aBase = smem_u32(smem + stage * Cfg::STAGE_BYTES);
+          const uint32_t bBase = aBase + Cfg::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t ad = A_MN ? make_sw128_desc(aBase + kk * 2048, 8192, 1024)
+                                     : make_sw128_desc(aBase + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? make_sw128_desc(bBase + kk * 2048, 8192, 1024)
+                                     : make_sw128_desc(bBase + kk * 32, 16, 1024);
+            tc_mma_f16_pair(d_tmem, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit_pair(&empty_bar[stage], 0x3);
+          if (++stage == Cfg::STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        tc_commit_pair(&tfull_bar[ab], 0x3);
+        if (++ab == 2) { ab = 0; aphase ^= 1; }
+      }
+    }
+  } else {
+    // -------------------------------------------------------------- epilogue (both CTAs)
+    const int ew = warp - 2;
+    const int q = warp & 3;
+    const int half = ew >> 2;
+    uint8_t* slab = epi_smem + ew * kEpiSlab;
+    const uint32_t lead_tempty0 = mapa_shared(&tempty_bar[0], 0);
+    int ab = 0;
+    uint32_t aphase = 0;
+    for (int u = pair; u < units; u += npairs) {
+      const int t = u / splits, sp = u % splits;
+      int mi, ni;
+      tile_coords(t, mt, nt, mi, ni);
+      const int m0 = mi * 256 + (int)rank * 128, n0 = ni * 256;
+      if (!mbar_wait(&tfull_bar[ab], aphase, abort_flag)) break;
+      tc_fence_after();
+      const int row0 = m0 + q * 32;
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * 256);
+      const int c_begin = half * 128, c_end = c_begin + 128;
+#pragma unroll 1
+      for (int c = c_begin; c < c_end; c += 64) {
+        if (n0 + c >= N) break;  // warp-uniform
+        uint32_t r0[32], r1[32];
+        tmem_ld32_issue(tbase + c, r0);
+        tmem_ld32_issue(tbase + c + 32, r1);
+        tmem_wait_ld();
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r0[j]);
+        if (lane == 0) bulk_wait_read0();
+        __syncwarp();
+        epi_chunk(args, &tmOut, &tmAux, slab, lane, row0, n0 + c, sp, v);
+        if (n0 + c + 32 < N) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r1[j]);
+          if (lane == 0) bulk_wait_read0();
+          __syncwarp();
+          epi_chunk(args, &tmOut, &tmAux, slab, lane, row0, n0 + c + 32, sp, v);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(lead_tempty0 + (uint32_t)(ab * sizeof(uint64_t)));
+      if (++ab == 2) { ab = 0; aphase ^= 1; }
+    }
+    if (lane == 0) bulk_wait0();
+    __syncwarp();
+  }
+
+  // Neither CTA releases the pair's TMEM before the other has finished with it.
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mbar_arrive_cluster(mapa_shared(done_bar, rank ^ 1));
+    mbar_wait(done_bar, 0, abort_flag);
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
 // Deterministic split-K reduction: out = alpha * sum_{s=0..S-1} ws[s] (+ out).
 __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int S, long MN, int N, float* out_f32,
                                      bf16* out_bf16, long ldo, float alpha, int accumulate) {
@@ -492,6 +700,81 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+static int max_pair_clusters() {
+  static int n = -1;
+  if (n < 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * 74, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = Gemm2Cfg::SMEM_BYTES;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaFuncSetAttribute(gemm_tc2_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         Gemm2Cfg::SMEM_BYTES);
+    int c = 0;
+    if (cudaOccupancyMaxActiveClusters(&c, gemm_tc2_kernel<false, true>, &cfg) != cudaSuccess || c <= 0) {
+      cudaGetLastError();
+      c = num_sms() / 2;
+    }
+    n = c;
+  }
+  return n;
+}
+
+template <bool A_MN, bool B_MN>
+static void launch_gemm2(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const CUtensorMap& tx,
+                         const GemmArgs& a, cudaStream_t st) {
+  static bool attr_set = false;
+  auto kern = gemm_tc2_kernel<A_MN, B_MN>;
+  if (!attr_set) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Gemm2Cfg::SMEM_BYTES);
+    attr_set = true;
+  }
+  const int units = ((a.M + 255) / 256) * ((a.N + 255) / 256) * a.splits;
+  const int pairs = std::min(units, max_pair_clusters());
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = Gemm2Cfg::SMEM_BYTES;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, to, tx, a));
+  count_launch();
+}
+
+// Split-K factor for the 2-SM path: the same makespan model over pair tiles
+// (256x256) and co-resident CTA pairs.
+static int choose_splits2(int M, int N, int K, bool allow_split) {
+  const int pairs = max_pair_clusters();
+  const long tiles = (long)((M + 255) / 256) * ((N + 255) / 256);
+  const int kb = (K + kBK - 1) / kBK;
+  const double kb_seconds = 2.0 * 256 * 256 * kBK / (2 * 1.4e15 / num_sms());
+  int splits = 1;
+  double best = 1e30;
+  for (int s = 1; s <= 16; ++s) {
+    if (s > 1 && (!allow_split || kb / s < 8)) break;
+    const long waves = (tiles * s + pairs - 1) / pairs;
+    const double t = waves * (double)((kb + s - 1) / s) * kb_seconds +
+                     (s > 1 ? (double)M * N * 4.0 * (s + 1) / 6.0e12 + 4e-6 : 0.0);
+    if (t < best * 0.97) {
+      best = t;
+      splits = s;
+    }
+  }
+  return splits;
+}
+
 // Picks the tile width and split-K factor.  128x256 tiles sustain ~1.4 PFLOP/s
 // on the main loop while 128x128 tiles measured ~0.8, so BN=256 is used whenever
 // N > 128.  The split-K factor s minimises a makespan model of the persistent
@@ -580,16 +863,23 @@ void gemm(torch::Tensor a, bool a_trans, torch::Tensor b, bool b_trans, torch::T
   const bool can_split = (epi == EPI_F32) || (epi == EPI_BF16 && !args.bias && !args.resid);
   int bn, splits;
   choose_tiling((int)M, (int)N, (int)K, bn, splits, can_split);
-  if (force_bn > 0) bn = (int)force_bn;
+  // 2-SM 256x256 pair tiles whenever the 1-SM choice is 128x256 and M spans a pair
+  // (force_bn: 128 / 256 pick a 1-SM width, 512 the 2-SM path)
+  bool pair2 = (bn == 256 && M > 128);
+  if (pair2) splits = choose_splits2((int)M, (int)N, (int)K, can_split);
+  if (force_bn > 0) {
+    pair2 = (force_bn == 512);
+    bn = pair2 ? 256 : (int)force_bn;
+  }
   if (force_splits > 0) splits = (int)force_splits;
-  TORCH_CHECK(bn == 128 || bn == 256, "gemm: BN must be 128 or 256");
+  TORCH_CHECK(bn == 128 || bn == 256, "gemm: BN must be 128 or 256 (or 512 for the 2-SM path)");
   if (splits > 1 && !can_split) splits = 1;
 
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   // A map: K-major [M rows, K cols] box {64, 128}; MN-major [K rows, M cols] box {64, 64}
   CUtensorMap ta = a_trans ? make_map(a.data_ptr(), K, M, a.stride(0), 64, 64)
                            : make_map(a.data_ptr(), M, K, a.stride(0), 64, kBM);
-  CUtensorMap tb = b_trans ? make_map(b.data_ptr(), N, K, b.stride(0), 64, bn)
+  CUtensorMap tb = b_trans ? make_map(b.data_ptr(), N, K, b.stride(0), 64, pair2 ? 128 : bn)
                            : make_map(b.data_ptr(), K, N, b.stride(0), 64, 64);
 
   GemmArgs run = args;
@@ -616,7 +906,12 @@ void gemm(torch::Tensor a, bool a_trans, torch::Tensor b, bool b_trans, torch::T
   else if (!a_trans && b_trans) launch_gemm<BNV, false, false>(ta, tb, to, tx, run, st); \
   else if (a_trans && !b_trans) launch_gemm<BNV, true, true>(ta, tb, to, tx, run, st);   \
   else launch_gemm<BNV, true, false>(ta, tb, to, tx, run, st);
-  if (bn == 256) {
+  if (pair2) {
+    if (!a_trans && !b_trans) launch_gemm2<false, true>(ta, tb, to, tx, run, st);
+    else if (!a_trans && b_trans) launch_gemm2<false, false>(ta, tb, to, tx, run, st);
+    else if (a_trans && !b_trans) launch_gemm2<true, true>(ta, tb, to, tx, run, st);
+    else launch_gemm2<true, false>(ta, tb, to, tx, run, st);
+  } else if (bn == 256) {
     DTB_GEMM_DISPATCH(256)
   } else {
     DTB_GEMM_DISPATCH(128)

@@ -31,7 +31,7 @@ GEMM_SHAPES = [(128, 256, 64), (300, 264, 200), (1024, 768, 768), (513, 2304, 76
 
 @pytest.mark.parametrize("M,N,K_", GEMM_SHAPES)
 @pytest.mark.parametrize("layout", ["nn", "nt", "tn"])
-@pytest.mark.parametrize("bn", [128, 256])
+@pytest.mark.parametrize("bn", [0, 128, 256, 512])  # 0: the heuristic's choice; 512: 2-SM pair tiles
 def test_gemm_layouts(M, N, K_, layout, bn):
     dev = "cuda"
     if layout == "tn":  # M is the contiguous dimension of the stored A: keep rows 16-byte aligned
