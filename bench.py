@@ -147,7 +147,7 @@ def run_ours(a, rank, world, local):
                     "--dim", str(M["dim"]), "--heads", str(M["heads"]), "--layers", str(M["layers"]),
                     "--lr", "6e-4", "--clip", "1.0", "--bucket-mb", str(a.bucket_mb), "--data", "synthetic",
                     "--vocab", str(M["vocab"]), "--algo", a.algo, "--accum", str(accum)]
-                   + ([] if a.overlap else ["--no-overlap"]))
+                   + ([] if a.overlap else ["--no-overlap"]) + (["--cuda-graph"] if a.cuda_graph else []))
     cfg = GPTConfig(dtype="bfloat16", **M)
     tr = T.Trainer(args, cfg, dev, pg)
     data = SyntheticData(M["vocab"])
@@ -165,9 +165,10 @@ def run_ours(a, rank, world, local):
     sampler = ClockSampler(local) if local == 0 else None
     if sampler:
         sampler.start()
-    l0 = K.launch_count()
+    l0, r0 = K.launch_count(), tr.graph_replays
     ms = _timed(lambda i: device_step(a.warmup + i), a.steps, world)
-    launches = K.launch_count() - l0
+    # eager launches counted on the host, plus the kernels each graph replay runs
+    launches = K.launch_count() - l0 + (tr.graph_replays - r0) * tr.graph_launches
     clocks = sampler.stop() if sampler else None
     pg.check()
 
@@ -189,10 +190,13 @@ def run_ours(a, rank, world, local):
         "config": {"model": C["name"], "global_batch": seq * accum * world,
                    "seq_len": M["ctx"], "parallelism": f"{'dp' if C['mode'] == 'ddp' else 'zero1-dp'}{world}",
                    "grad_accum": accum, "bucket_mb": a.bucket_mb if C["mode"] == "ddp" else None,
-                   "grad_sync": ("per-bucket all-reduce overlapped with backward" if a.overlap else
+                   "grad_sync": ("per-bucket all-reduce overlapped with backward"
+                                 if (tr.ddp is not None and tr.ddp.overlap) else
                                  "one all-reduce of the flat gradient after backward") if C["mode"] == "ddp" else
                    "reduce-scatter + fused AdamW/all-gather",
                    "optimizer": "AdamW, clip 1.0", "allreduce_order": a.algo,
+                   "cuda_graph": ("forward+backward captured once and replayed; gradient sync and optimizer "
+                                  "eager" if a.cuda_graph else False),
                    "l2": "no flush: weights/activations/logits per step >> 126 MB L2"},
         "e2e": {"value": tokens * a.steps / (ms_e2e / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": 2 * seq * accum * M["ctx"] * 8, "d2h_bytes_per_step": 4,
@@ -201,6 +205,8 @@ def run_ours(a, rank, world, local):
         "gpu_launches_per_step": launches / max(1, a.steps),
         "clocks": clocks,
     }
+    tr._graph = None  # release the captured graph before the groups go away
+    torch.cuda.synchronize()
     pg.close()
     if world > 1:
         dist.destroy_process_group()
@@ -301,6 +307,9 @@ def main():
     ap.add_argument("--config", choices=sorted(CONFIGS), default="gpt2-small-ddp")
     ap.add_argument("--comm-blocks", type=int, default=0, help="CTAs per collective kernel (0: by size)")
     ap.add_argument("--comm-priority", type=int, default=0, help="CUDA priority of the collective stream")
+    ap.add_argument("--no-cuda-graph", dest="cuda_graph", action="store_false",
+                    help="launch every kernel from Python each step instead of replaying the captured "
+                         "forward+backward graph")
     ap.add_argument("--overlap", action="store_true",
                     help="all-reduce each gradient bucket during backward (default: one all-reduce of the flat "
                          "gradient after backward, measured faster on B200)")

@@ -57,6 +57,9 @@ def parse(argv=None):
     ap.add_argument("--algo", choices=["ring", "direct"], default="ring")
     ap.add_argument("--ar-method", choices=["auto", "oneshot", "twoshot"], default="auto")
     ap.add_argument("--device", default=None, help="cpu | cuda (default: cuda for bfloat16, else cpu)")
+    ap.add_argument("--cuda-graph", action="store_true",
+                    help="GPU: capture forward+backward of a step in a CUDA graph and replay it (removes the "
+                         "per-kernel host launch cost; the gradient sync and the optimizer run eagerly)")
     ap.add_argument("--ckpt-dir", default=None)
     ap.add_argument("--ckpt-every", type=int, default=0)
     ap.add_argument("--resume", action="store_true", help="resume from the latest checkpoint if any")
@@ -102,7 +105,10 @@ class Trainer:
             pass
         if a.mode == "ddp":
             from .parallel.ddp import DDP
-            self.ddp = DDP(self.model, pg, bucket_mb=a.bucket_mb, overlap=not a.no_overlap, algo=a.algo,
+            # a captured backward cannot launch per-bucket collectives (their flag epochs
+            # advance every call), so graph mode syncs the flat gradient after replay
+            overlap = not a.no_overlap and not (getattr(a, "cuda_graph", False) and self.gpu)
+            self.ddp = DDP(self.model, pg, bucket_mb=a.bucket_mb, overlap=overlap, algo=a.algo,
                            method=a.ar_method)
         elif a.mode == "zero":
             from .parallel.zero import ZeroAdamW
@@ -116,6 +122,15 @@ class Trainer:
                 self.opt = AdamW([p.data for p in self.params], lr=a.lr, weight_decay=a.wd)
         self._sq = torch.zeros(1, dtype=torch.float64, device=device) if self.gpu else None
         self._pinned: dict = {}
+        # CUDA-graph state (--cuda-graph): static inputs, the captured forward+backward,
+        # its loss output, and how many of this extension's kernels one replay launches
+        self.use_graph = bool(getattr(a, "cuda_graph", False)) and self.gpu
+        self._graph = None
+        self._graph_key = None
+        self._static_in: list = []
+        self._static_loss = None
+        self.graph_launches = 0
+        self.graph_replays = 0
         self.last_grad_norm = 0.0
         self.comm_wait = 0.0
 
@@ -140,9 +155,71 @@ class Trainer:
         else:
             self.opt.lr = lr
 
+    def _fwd_bwd(self, batches_dev, n_micro: int):
+        """Forward and backward over all micro-batches (device tensors); returns the mean loss."""
+        loss_acc = torch.zeros((), dtype=torch.float64, device=self.device)
+        for mi, vrs in enumerate(batches_dev):
+            last = mi == len(batches_dev) - 1
+            for xt, yt in vrs:
+                _, loss = self.model(xt, yt)
+                scaled = loss * (1.0 / n_micro)
+                if self.ddp is not None and not last:
+                    with self.ddp.no_sync():
+                        scaled.backward()
+                else:
+                    scaled.backward()
+                loss_acc = loss_acc + loss.detach().double() / n_micro
+        return loss_acc
+
+    def _step_graph(self, batches):
+        """Forward+backward by CUDA-graph replay.  The first call (and any change of
+        batch shapes) warms up on a side stream and captures; every call copies its
+        batch into the static input buffers first.  Gradients land in the flat
+        gradient buffer, whose addresses the graph keeps."""
+        key = tuple(tuple((tuple(np.shape(x)), tuple(np.shape(y))) for x, y in vrs) for vrs in batches)
+        n_micro = sum(len(v) for v in batches)
+        if self._graph is None or key != self._graph_key:
+            from .ops import kernels as K
+            self._static_in = [[(self.to_device(x, ("gx", mi, vi)).clone(), self.to_device(y, ("gy", mi, vi)).clone())
+                                for vi, (x, y) in enumerate(vrs)] for mi, vrs in enumerate(batches)]
+            side = torch.cuda.Stream(device=self.device)
+            side.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(side):
+                for _ in range(2):
+                    self.model.zero_grad()
+                    self._fwd_bwd(self._static_in, n_micro)
+            torch.cuda.current_stream(self.device).wait_stream(side)
+            torch.cuda.synchronize(self.device)
+            self.model.zero_grad()
+            g = torch.cuda.CUDAGraph()
+            before = K.launch_count()
+            with torch.cuda.graph(g):
+                self._static_loss = self._fwd_bwd(self._static_in, n_micro)
+            self.graph_launches = K.launch_count() - before
+            self._graph, self._graph_key = g, key
+        for mi, vrs in enumerate(batches):
+            for vi, (x, y) in enumerate(vrs):
+                sx, sy = self._static_in[mi][vi]
+                sx.copy_(self.to_device(x, ("x", mi, vi)), non_blocking=True)
+                sy.copy_(self.to_device(y, ("y", mi, vi)), non_blocking=True)
+        self._graph.replay()
+        self.graph_replays += 1
+        return self._static_loss
+
     def step(self, batches, return_loss: bool = True):
         """``batches``: list over micro-steps of lists over virtual ranks of (x, y)."""
         a = self.a
+        if self.use_graph:
+            loss_acc = self._step_graph(batches)
+            if self.ddp is not None:
+                before = self.ddp.comm_wait_s
+                self.ddp.finish()
+                self.comm_wait = self.ddp.comm_wait_s - before
+            if self.zero is not None:
+                self.zero.step()
+            else:
+                self._clip_and_update()
+            return self._reduce_loss(loss_acc) if return_loss else None
         self.model.zero_grad()
         n_micro = sum(len(v) for v in batches)
         loss_acc = torch.zeros((), dtype=torch.float64, device=self.device) if self.gpu else 0.0

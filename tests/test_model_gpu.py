@@ -82,3 +82,31 @@ def test_init_matches_reference_initialiser():
     rng = np.random.default_rng(7)
     tok = (rng.standard_normal((CFG["vocab"], CFG["dim"])) * 0.02).astype(np.float32)
     assert np.array_equal(m.tok.detach().numpy(), tok)
+
+
+@pytest.mark.parametrize("accum", [1, 2])
+def test_cuda_graph_step_matches_eager(accum):
+    """--cuda-graph replays a captured forward+backward: parameters and losses must be
+    bit-identical to launching every kernel eagerly (same kernels, same order)."""
+    from dtrain_b200 import train as T
+    from dtrain_b200.models.gpt import GPTConfig
+
+    def run(graph):
+        args = T.parse(["--mode", "single", "--dtype", "bfloat16", "--batch", "2", "--ctx", "128", "--dim", "128",
+                        "--heads", "2", "--layers", "2", "--vocab", "512", "--data", "synthetic", "--lr", "3e-3",
+                        "--accum", str(accum)] + (["--cuda-graph"] if graph else []))
+        cfg = GPTConfig(vocab=512, ctx=128, dim=128, heads=2, layers=2, dtype="bfloat16")
+        tr = T.Trainer(args, cfg, torch.device("cuda", 0), None)
+        g = torch.Generator().manual_seed(3)
+        losses = []
+        for _ in range(4):
+            batches = [[(torch.randint(0, 512, (2, 128), generator=g), torch.randint(0, 512, (2, 128), generator=g))]
+                       for _ in range(accum)]
+            losses.append(tr.step(batches))
+        torch.cuda.synchronize()
+        return losses, tr.model.flat.master.clone(), tr
+    l_e, p_e, _ = run(False)
+    l_g, p_g, tr = run(True)
+    assert tr.graph_replays == 4 and tr.graph_launches > 0
+    assert l_e == l_g
+    assert torch.equal(p_e, p_g)
