@@ -54,7 +54,7 @@ CONFIGS = {
     "gpt-1.3b-zero": dict(model=dict(vocab=50304, ctx=2048, dim=2048, heads=16, layers=24), seq=4, mode="zero",
                           accum=1, name="1.3B (24L, d2048, 16H, ctx 2048, vocab 50304)"),
 }
-BASELINE_VALUE = None  # BASELINE.md publishes no number for this config (CPU-only reference numbers)
+BASELINE_VALUE = None  # the reference publishes no GPU number for this config (its numbers are CPU-only)
 
 
 def _env_rank():
