@@ -18,6 +18,7 @@ at step N").
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import math
 import os
@@ -80,6 +81,19 @@ def _default_device(a) -> torch.device:
     if a.dtype in ("bfloat16", "bf16"):
         return torch.device("cuda", int(os.environ.get("LOCAL_RANK", os.environ.get("RANK", "0"))))
     return torch.device("cpu")
+
+
+@contextlib.contextmanager
+def _nvtx(name: str):
+    """NVTX range around a phase of the step (visible in Nsight timelines; no-op on CPU)."""
+    if torch.cuda.is_available():
+        torch.cuda.nvtx.range_push(name)
+        try:
+            yield
+        finally:
+            torch.cuda.nvtx.range_pop()
+    else:
+        yield
 
 
 class Trainer:
@@ -206,21 +220,8 @@ class Trainer:
         self.graph_replays += 1
         return self._static_loss
 
-    def step(self, batches, return_loss: bool = True):
-        """``batches``: list over micro-steps of lists over virtual ranks of (x, y)."""
-        a = self.a
-        if self.use_graph:
-            loss_acc = self._step_graph(batches)
-            if self.ddp is not None:
-                before = self.ddp.comm_wait_s
-                self.ddp.finish()
-                self.comm_wait = self.ddp.comm_wait_s - before
-            if self.zero is not None:
-                self.zero.step()
-            else:
-                self._clip_and_update()
-            return self._reduce_loss(loss_acc) if return_loss else None
-        self.model.zero_grad()
+    def _eager_fwd_bwd(self, batches):
+        """Forward and backward over host or device micro-batches, kernels launched eagerly."""
         n_micro = sum(len(v) for v in batches)
         loss_acc = torch.zeros((), dtype=torch.float64, device=self.device) if self.gpu else 0.0
         for mi, vrs in enumerate(batches):
@@ -239,14 +240,38 @@ class Trainer:
                     loss_acc = loss_acc + loss.detach().double() / n_micro
                 else:
                     loss_acc += float(loss.detach()) / n_micro
-        if self.ddp is not None:
-            before = self.ddp.comm_wait_s
-            self.ddp.finish()
-            self.comm_wait = self.ddp.comm_wait_s - before
-        if self.zero is not None:
-            self.zero.step()
-        else:
-            self._clip_and_update()
+        return loss_acc
+
+    def step(self, batches, return_loss: bool = True):
+        """``batches``: list over micro-steps of lists over virtual ranks of (x, y)."""
+        a = self.a
+        if self.use_graph:
+            with _nvtx("forward+backward (graph replay)"):
+                loss_acc = self._step_graph(batches)
+            with _nvtx("gradient sync"):
+                if self.ddp is not None:
+                    before = self.ddp.comm_wait_s
+                    self.ddp.finish()
+                    self.comm_wait = self.ddp.comm_wait_s - before
+            with _nvtx("optimizer"):
+                if self.zero is not None:
+                    self.zero.step()
+                else:
+                    self._clip_and_update()
+            return self._reduce_loss(loss_acc) if return_loss else None
+        self.model.zero_grad()
+        with _nvtx("forward+backward"):
+            loss_acc = self._eager_fwd_bwd(batches)
+        with _nvtx("gradient sync"):
+            if self.ddp is not None:
+                before = self.ddp.comm_wait_s
+                self.ddp.finish()
+                self.comm_wait = self.ddp.comm_wait_s - before
+        with _nvtx("optimizer"):
+            if self.zero is not None:
+                self.zero.step()
+            else:
+                self._clip_and_update()
         if not return_loss:
             return None
         return self._reduce_loss(loss_acc)
@@ -271,6 +296,22 @@ class Trainer:
         if self.gpu and self.model.flat is not None and self.model.flat.work is not None:
             return math.sqrt(float(self._sq.item()))
         return self.last_grad_norm
+
+    def max_over_ranks(self, value: float) -> float:
+        """Max of a per-rank host value (the collectives sum, so each rank fills its own slot)."""
+        if self.pg is None or self.world == 1:
+            return float(value)
+        if self.gpu:
+            v = torch.zeros(self.world, dtype=torch.float32, device=self.device)
+            v[self.rank] = float(value)
+            self.pg.allreduce(v, "direct")
+            out = float(v.max().item())
+            self.pg.check()
+            return out
+        v = np.zeros(self.world)
+        v[self.rank] = value
+        self.pg.allreduce(v)
+        return float(v.max())
 
     def _reduce_loss(self, loss_acc) -> float:
         pg = self.pg
@@ -382,6 +423,11 @@ def main(argv=None):
     restarts = int(os.environ.get("DTRAIN_RESTART_COUNT", "0"))
     tokens_per_step = a.batch * a.ctx * a.accum * max(world, a.emulate_world)
     vworlds = a.emulate_world if a.mode == "single" else 1
+    # GPU jobs that log also record the device time of each step (every rank takes
+    # part in the max, so the decision depends only on the shared flags)
+    timing = bool(tr.gpu and a.log)
+    if timing:
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
     for step in range(start, a.steps):
         if step == a.fail_at_step and rank == a.fail_rank and restarts == 0:
@@ -390,6 +436,8 @@ def main(argv=None):
             print(f"[rank {rank}] injected failure at step {step}", file=sys.stderr, flush=True)
             os._exit(17)
         t0 = time.perf_counter()
+        if timing:
+            ev0.record()
         lr = lr_at(step, a)
         tr.set_lr(lr)
         batches = []
@@ -402,9 +450,17 @@ def main(argv=None):
             batches.append(vr_batches)
         loss = tr.step(batches)
         dt = time.perf_counter() - t0
+        dev_ms = None
+        if timing:
+            ev1.record()
+            ev1.synchronize()
+            dev_ms = tr.max_over_ranks(ev0.elapsed_time(ev1))
         if log:
             rec = {"step": step + 1, "lr": lr, "loss": loss, "grad_norm": tr.grad_norm(), "step_s": dt,
                    "tokens_per_s": tokens_per_step / dt, "comm_wait_s": tr.comm_wait}
+            if dev_ms is not None:  # device-timed (CUDA events on the training stream), max over ranks
+                rec["step_ms_max_over_ranks"] = dev_ms
+                rec["tokens_per_s_device"] = tokens_per_step / (dev_ms / 1e3)
             log.write(json.dumps(rec) + "\n")
             log.flush()
         if a.ckpt_dir and a.ckpt_every and (step + 1) % a.ckpt_every == 0:
