@@ -55,12 +55,18 @@ struct Sigs {
 };
 
 struct CommCtx {
-  Sigs sig;           // every rank's signal pad [kMaxCommBlocks][kMaxRanks]
+  Sigs sig;           // every rank's signal pad [kMaxCommBlocks][kMaxRanks] + descriptor ring
   int rank, world;
   uint32_t epoch;     // first epoch this launch may use
+  uint32_t tag;       // descriptor of this collective (kind, element count, dtype)
   uint64_t timeout_ns;
   int* host_status;   // host-mapped status word (device pointer)
 };
+
+// After the flags, each rank's signal pad holds a ring of kDescSlots 64-bit
+// descriptors (epoch << 32 | tag) of its own recent collectives.
+constexpr int kFlagWords = kMaxCommBlocks * kMaxRanks;
+constexpr int kDescSlots = 16;
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -68,6 +74,12 @@ __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint64_t ld_acquire_sys64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
 
@@ -100,6 +112,37 @@ __device__ bool cta_barrier(const CommCtx& c, uint32_t epoch) {
   }
   __syncthreads();
   return failed == 0;
+}
+
+// First barrier of a collective, with desynchronisation detection: CTA 0 publishes
+// this rank's descriptor of the collective for its epoch before arriving and, once
+// every peer has arrived at the epoch, compares the peers' descriptors for the same
+// epoch with its own.  Ranks that issued different collectives (or sizes) at the
+// same point get kStatusSeqMismatch and return instead of mixing unrelated data.
+// (A peer cannot overwrite that slot before this rank reaches the collective's next
+// barrier, so the ring never aliases.)
+__device__ bool cta_enter(const CommCtx& c) {
+  const uint64_t mine = ((uint64_t)c.epoch << 32) | c.tag;
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    uint64_t* ring = reinterpret_cast<uint64_t*>(c.sig.p[c.rank] + kFlagWords);
+    *reinterpret_cast<volatile uint64_t*>(ring + (c.epoch % kDescSlots)) = mine;
+    __threadfence_system();
+  }
+  if (!cta_barrier(c, c.epoch)) return false;
+  if (blockIdx.x != 0) return true;
+  __shared__ int mismatch;
+  if (threadIdx.x == 0) mismatch = 0;
+  __syncthreads();
+  if (threadIdx.x < c.world && threadIdx.x != c.rank) {
+    const uint64_t* ring = reinterpret_cast<const uint64_t*>(c.sig.p[threadIdx.x] + kFlagWords);
+    if (ld_acquire_sys64(ring + (c.epoch % kDescSlots)) != mine) {
+      atomicExch(&mismatch, 1);
+      atomicCAS(c.host_status, 0, kStatusSeqMismatch);
+      set_status(kStatusSeqMismatch);
+    }
+  }
+  __syncthreads();
+  return mismatch == 0;
 }
 
 // [lo, hi) of chunk `c` of an n-element buffer split over W ranks: the first
@@ -371,7 +414,7 @@ __device__ __forceinline__ void copy_range(const T* src, T* dst, long a, long b)
 template <typename TI, typename TO, int WT>
 __global__ void __launch_bounds__(kCommThreads)
     allreduce_oneshot_kernel(CommCtx c, Peers in, TO* out, long n, int order, float scale) {
-  if (!cta_barrier(c, c.epoch)) return;
+  if (!cta_enter(c)) return;
   for (int ch = 0; ch < c.world; ++ch) {
     long lo, hi, a, b;
     chunk_bounds(n, c.world, ch, lo, hi);
@@ -389,7 +432,7 @@ __global__ void __launch_bounds__(kCommThreads)
 template <typename T, int WT>
 __global__ void __launch_bounds__(kCommThreads)
     allreduce_twoshot_kernel(CommCtx c, Peers in, T* out, long n, int order, float scale) {
-  if (!cta_barrier(c, c.epoch)) return;
+  if (!cta_enter(c)) return;
   long lo, hi, a, b;
   chunk_bounds(n, c.world, c.rank, lo, hi);
   cta_slice(lo, hi, a, b);
@@ -417,7 +460,7 @@ template <typename TI, typename TO, int WT>
 __global__ void __launch_bounds__(kCommThreads)
     reduce_scatter_kernel(CommCtx c, Peers in, TO* out, long n, int order, float scale, double* sq_part) {
   __shared__ double red[kCommThreads / 32];
-  if (!cta_barrier(c, c.epoch)) return;
+  if (!cta_enter(c)) return;
   long lo, hi, a, b;
   chunk_bounds(n, c.world, c.rank, lo, hi);
   cta_slice(lo, hi, a, b);
@@ -441,7 +484,7 @@ __global__ void __launch_bounds__(kCommThreads)
 // All-gather in place: every rank copies chunk p from rank p into `out`.
 template <typename T>
 __global__ void __launch_bounds__(kCommThreads) all_gather_kernel(CommCtx c, Peers in, T* out, long n) {
-  if (!cta_barrier(c, c.epoch)) return;
+  if (!cta_enter(c)) return;
   for (int k = 1; k < c.world; ++k) {
     const int p = (c.rank + k) % c.world;
     long lo, hi, a, b;
@@ -457,7 +500,7 @@ __global__ void __launch_bounds__(kCommThreads) all_gather_kernel(CommCtx c, Pee
 __global__ void __launch_bounds__(kCommThreads)
     broadcast_kernel(CommCtx c, Peers in, void* out, long nbytes, int root, const float* cast_src, bf16* out16,
                      long n16) {
-  if (!cta_barrier(c, c.epoch)) return;
+  if (!cta_enter(c)) return;
   if (c.rank != root && out) {
     long a, b;
     cta_slice(0, nbytes, a, b);
@@ -471,7 +514,7 @@ __global__ void __launch_bounds__(kCommThreads)
   }
 }
 
-__global__ void barrier_kernel(CommCtx c) { cta_barrier(c, c.epoch); }
+__global__ void barrier_kernel(CommCtx c) { cta_enter(c); }
 
 // ZeRO-1 update, fused with the global-norm exchange and the parameter all-gather.
 // Phase 1: every CTA sums all ranks' per-CTA squared-norm partials (written by
@@ -485,7 +528,7 @@ __global__ void __launch_bounds__(kCommThreads)
                                 float* m, float* v, Peers work16, Peers master32, long n, AdamConsts ak,
                                 float max_norm, double* sq_out, int gather_master) {
   __shared__ float s_clip;
-  if (!cta_barrier(c, c.epoch)) return;
+  if (!cta_enter(c)) return;
   if (threadIdx.x == 0) {
     double tot = 0.0;
     for (int r = 0; r < c.world; ++r) {
@@ -577,7 +620,16 @@ void comm_status_clear() {
   *reinterpret_cast<volatile int*>(g_host_status) = 0;
 }
 
-static CommCtx make_ctx(const std::vector<int64_t>& sigs, int64_t rank, int64_t epoch, double timeout_s) {
+// Descriptor of a collective: its kind, element count and dtype, mixed into 32 bits.
+static uint32_t op_tag(uint32_t kind, int64_t n, int64_t dtype) {
+  uint64_t h = (uint64_t)n * 0x9E3779B97F4A7C15ull;
+  h ^= (uint64_t)kind << 56 ^ (uint64_t)dtype << 48;
+  h ^= h >> 29;
+  return (uint32_t)(h ^ (h >> 32));
+}
+
+static CommCtx make_ctx(const std::vector<int64_t>& sigs, int64_t rank, int64_t epoch, double timeout_s,
+                        uint32_t tag) {
   ensure_status();
   CommCtx c{};
   const int W = (int)sigs.size();
@@ -587,6 +639,7 @@ static CommCtx make_ctx(const std::vector<int64_t>& sigs, int64_t rank, int64_t 
   c.rank = (int)rank;
   c.world = W;
   c.epoch = (uint32_t)epoch;
+  c.tag = tag;
   c.timeout_ns = (uint64_t)(timeout_s * 1e9);
   c.host_status = g_dev_status;
   return c;
@@ -609,7 +662,7 @@ static int comm_blocks(long bytes, int64_t want) {
 int64_t allreduce(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> bufs,
                   int64_t byte_offset, int64_t n, int64_t in_dtype, int64_t out_ptr, int64_t out_dtype, int64_t algo,
                   int64_t order, double scale, double timeout_s, int64_t blocks) {
-  CommCtx c = make_ctx(sigs, rank, epoch, timeout_s);
+  CommCtx c = make_ctx(sigs, rank, epoch, timeout_s, op_tag(1 + (uint32_t)algo, n, in_dtype * 8 + out_dtype));
   Peers in = make_peers(bufs, byte_offset);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   const long esz = in_dtype == DT_F32 ? 4 : 2;
@@ -657,7 +710,7 @@ int64_t allreduce(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::v
 int64_t reduce_scatter(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> bufs,
                        int64_t byte_offset, int64_t n, int64_t dtype, int64_t out_ptr, int64_t order, double scale,
                        int64_t sq_part_ptr, double timeout_s, int64_t blocks) {
-  CommCtx c = make_ctx(sigs, rank, epoch, timeout_s);
+  CommCtx c = make_ctx(sigs, rank, epoch, timeout_s, op_tag(4, n, dtype));
   Peers in = make_peers(bufs, byte_offset);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   const int nb = comm_blocks(n * (dtype == DT_F32 ? 4 : 2), blocks);
@@ -683,7 +736,7 @@ int64_t reduce_scatter(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, s
 
 int64_t all_gather(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> bufs,
                    int64_t byte_offset, int64_t n, int64_t dtype, double timeout_s, int64_t blocks) {
-  CommCtx c = make_ctx(sigs, rank, epoch, timeout_s);
+  CommCtx c = make_ctx(sigs, rank, epoch, timeout_s, op_tag(5, n, dtype));
   Peers in = make_peers(bufs, byte_offset);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   const int nb = comm_blocks(n * (dtype == DT_F32 ? 4 : 2), blocks);
@@ -699,7 +752,7 @@ int64_t all_gather(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::
 int64_t broadcast(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> bufs,
                   int64_t byte_offset, int64_t nbytes, int64_t root, int64_t cast_src, int64_t out16, int64_t n16,
                   double timeout_s, int64_t blocks) {
-  CommCtx c = make_ctx(sigs, rank, epoch, timeout_s);
+  CommCtx c = make_ctx(sigs, rank, epoch, timeout_s, op_tag(6, nbytes, root));
   Peers in = make_peers(bufs, byte_offset);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   const int nb = comm_blocks(nbytes, blocks);
@@ -712,7 +765,7 @@ int64_t broadcast(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::v
 }
 
 int64_t device_barrier(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, double timeout_s) {
-  CommCtx c = make_ctx(sigs, rank, epoch, timeout_s);
+  CommCtx c = make_ctx(sigs, rank, epoch, timeout_s, op_tag(7, 0, 0));
   barrier_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(c);
   count_launch();
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -725,7 +778,7 @@ int64_t zero_adamw_allgather(std::vector<int64_t> sigs, int64_t rank, int64_t ep
                              double lr, double b1, double b2, double eps, double wd, int64_t t, double max_norm,
                              c10::optional<torch::Tensor> sq_out, bool gather_master, double timeout_s,
                              int64_t blocks) {
-  CommCtx c = make_ctx(sigs, rank, epoch, timeout_s);
+  CommCtx c = make_ctx(sigs, rank, epoch, timeout_s, op_tag(8, n, gather_master ? 1 : 0));
   Sigs sp{};
   for (size_t i = 0; i < sq_parts.size(); ++i) sp.p[i] = reinterpret_cast<uint32_t*>(sq_parts[i]);
   Peers w16 = make_peers(work16, 0), m32 = make_peers(master32, 0);

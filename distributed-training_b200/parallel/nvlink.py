@@ -33,7 +33,8 @@ from .comm import partition
 DT = {torch.float32: 0, torch.bfloat16: 1}
 ORDER_RANK, ORDER_CYCLIC = 0, 1
 ALGO_ONESHOT, ALGO_TWOSHOT = 0, 1
-_SIG_BYTES = 128 * 8 * 4  # [max CTAs][max ranks] uint32 flags
+# [max CTAs][max ranks] uint32 flags, then a ring of 16 uint64 collective descriptors
+_SIG_BYTES = 8192
 # "auto" picks one-shot only below this size: its out-of-place result costs a copy
 # back, and measured on 8 B200s the two-shot kernel was as fast down to 4 KB.
 _ONESHOT_MAX_BYTES = 0
@@ -186,8 +187,12 @@ class NVLinkGroup:
         return self._staging
 
     def check(self):
-        """Raise CommError if any collective kernel timed out waiting for a peer."""
+        """Raise CommError if a collective kernel timed out waiting for a peer, or found
+        that the ranks had issued different collectives (desynchronised ranks)."""
         code = int(lib().comm_status())
+        if code == 3:
+            raise CommError(f"NVLink collective failed on rank {self.rank} (device status 3): collective desync - "
+                            "the ranks issued different collectives (kind, size or dtype) at the same point")
         if code:
             raise CommError(f"NVLink collective failed on rank {self.rank} (device status {code}): "
                             "a peer did not arrive within the timeout")

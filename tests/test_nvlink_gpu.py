@@ -187,6 +187,34 @@ def test_peer_that_never_arrives_gives_commerror_not_a_hang():
     assert res[0][0] == "commerror" and res[0][2] == 20.0
 
 
+def _desync(pg):
+    import torch
+    from dtrain_b200.utils.store import CommError
+    x = pg.alloc(2048, torch.float32)
+    x.fill_(1.0)
+    pg.timeout = 5.0
+    # same kernel shape (one CTA) but different sizes: a programming error on the host
+    n = 1000 if pg.rank == 0 else 1008
+    pg.allreduce(x[:n], "ring", method="twoshot")
+    out = "no error"
+    try:
+        pg.synchronize()
+    except CommError as e:
+        y = torch.ones(4, device=x.device) * 3
+        out = ("commerror", "desync" in str(e), float(y.sum().item()))
+    pg._exchange("desync-test-done", b"")
+    return out
+
+
+@needs2
+def test_desynchronised_collectives_give_commerror():
+    """Ranks that issue different collectives at the same point are told so (the
+    descriptor ring in the signal pads), without a hang and with a usable context."""
+    res = _run(2, _desync)
+    for r in res:
+        assert r[0] == "commerror" and r[1] and r[2] == 12.0
+
+
 def _zero_vs_ddp(pg):
     import torch
     from dtrain_b200.models.gpt import GPT, GPTConfig
