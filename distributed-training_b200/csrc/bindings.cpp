@@ -15,6 +15,9 @@ void gemm(torch::Tensor a, bool a_trans, torch::Tensor b, bool b_trans, torch::T
           c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> resid, c10::optional<torch::Tensor> aux,
           double alpha, bool accumulate, int64_t force_bn, int64_t force_splits,
           c10::optional<torch::Tensor> workspace);
+void gemm_gather(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t epi, c10::optional<torch::Tensor> bias,
+                 c10::optional<torch::Tensor> resid, c10::optional<torch::Tensor> aux, std::vector<int64_t> peers,
+                 int64_t rank, int64_t woff, int64_t nflat, torch::Tensor state, int64_t site);
 std::vector<int64_t> gemm_tiling(int64_t M, int64_t N, int64_t K);
 // layernorm.cu
 std::vector<torch::Tensor> layernorm_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor b, double eps);
@@ -64,7 +67,7 @@ int64_t zero_adamw_allgather(std::vector<int64_t> sigs, int64_t rank, int64_t ep
                              torch::Tensor v, std::vector<int64_t> work16, std::vector<int64_t> master32, int64_t n,
                              double lr, double b1, double b2, double eps, double wd, int64_t t, double max_norm,
                              c10::optional<torch::Tensor> sq_out, bool gather_master, double timeout_s,
-                             int64_t blocks);
+                             int64_t blocks, c10::optional<torch::Tensor> keep, c10::optional<torch::Tensor> gen_word);
 int64_t comm_max_blocks();
 int64_t comm_max_ranks();
 
@@ -96,6 +99,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("epi"), py::arg("bias") = py::none(), py::arg("resid") = py::none(), py::arg("aux") = py::none(),
         py::arg("alpha") = 1.0, py::arg("accumulate") = false, py::arg("force_bn") = 0, py::arg("force_splits") = 0,
         py::arg("workspace") = py::none());
+  m.def("gemm_gather", &gemm_gather, py::arg("a"), py::arg("b"), py::arg("out"), py::arg("epi"),
+        py::arg("bias") = py::none(), py::arg("resid") = py::none(), py::arg("aux") = py::none(), py::arg("peers"),
+        py::arg("rank"), py::arg("woff"), py::arg("nflat"), py::arg("state"), py::arg("site"));
   m.def("gemm_tiling", &gemm_tiling);
   m.def("layernorm_fwd", &layernorm_fwd);
   m.def("layernorm_bwd", &layernorm_bwd, py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("mean"),

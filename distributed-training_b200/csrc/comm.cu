@@ -523,12 +523,19 @@ __global__ void barrier_kernel(CommCtx c) { cta_enter(c); }
 // Phase 2: AdamW on this rank's shard [lo, hi) of the flat fp32 master (dtrain/zero.py:45-62),
 //          writing the fp32 master and the bf16 working copy (symmetric).
 // Phase 3: all-gather of the bf16 working copy (and optionally the fp32 master).
+//          With `keep` (nkeep sorted [lo, hi) intervals of the flat buffer) only those
+//          ranges of the bf16 copy are gathered here: the Linear weights are left to
+//          the forward GEMMs that gather them tile by tile (gemm.cu, gemm_gather),
+//          which start pulling once `gen_out` (written here) moves past the
+//          generation they last gathered.
 __global__ void __launch_bounds__(kCommThreads)
     zero_adamw_allgather_kernel(CommCtx c, Sigs sq_parts, int nparts, float* master, const float* grad,
                                 float* m, float* v, Peers work16, Peers master32, long n, AdamConsts ak,
-                                float max_norm, double* sq_out, int gather_master) {
+                                float max_norm, double* sq_out, int gather_master, const long* keep, int nkeep,
+                                int* gen_out) {
   __shared__ float s_clip;
   if (!cta_enter(c)) return;
+  if (gen_out && blockIdx.x == 0 && threadIdx.x == 0) *gen_out = (int)(c.epoch + 1u);
   if (threadIdx.x == 0) {
     double tot = 0.0;
     for (int r = 0; r < c.world; ++r) {
@@ -562,8 +569,17 @@ __global__ void __launch_bounds__(kCommThreads)
   for (int kk = 1; kk < c.world; ++kk) {
     const int p = (c.rank + kk) % c.world;
     chunk_bounds(n, c.world, p, lo, hi);
+    if (w16 && keep) {
+      for (int k = 0; k < nkeep; ++k) {
+        const long klo = max(lo, keep[2 * k]), khi = min(hi, keep[2 * k + 1]);
+        if (klo >= khi) continue;
+        long ka, kb;
+        cta_slice(klo, khi, ka, kb);
+        copy_range<bf16>(reinterpret_cast<const bf16*>(work16.p[p]), w16, ka, kb);
+      }
+    }
     cta_slice(lo, hi, a, b);
-    if (w16) copy_range<bf16>(reinterpret_cast<const bf16*>(work16.p[p]), w16, a, b);
+    if (w16 && !keep) copy_range<bf16>(reinterpret_cast<const bf16*>(work16.p[p]), w16, a, b);
     if (gather_master)
       copy_range<float>(reinterpret_cast<const float*>(master32.p[p]), master, a, b);
   }
@@ -777,17 +793,32 @@ int64_t zero_adamw_allgather(std::vector<int64_t> sigs, int64_t rank, int64_t ep
                              torch::Tensor v, std::vector<int64_t> work16, std::vector<int64_t> master32, int64_t n,
                              double lr, double b1, double b2, double eps, double wd, int64_t t, double max_norm,
                              c10::optional<torch::Tensor> sq_out, bool gather_master, double timeout_s,
-                             int64_t blocks) {
-  CommCtx c = make_ctx(sigs, rank, epoch, timeout_s, op_tag(8, n, gather_master ? 1 : 0));
+                             int64_t blocks, c10::optional<torch::Tensor> keep, c10::optional<torch::Tensor> gen_word) {
+  const int64_t nkeep_tag = (keep && keep->defined()) ? keep->size(0) + 1 : 0;
+  CommCtx c = make_ctx(sigs, rank, epoch, timeout_s, op_tag(8, n, (gather_master ? 1 : 0) + 2 * nkeep_tag));
   Sigs sp{};
   for (size_t i = 0; i < sq_parts.size(); ++i) sp.p[i] = reinterpret_cast<uint32_t*>(sq_parts[i]);
   Peers w16 = make_peers(work16, 0), m32 = make_peers(master32, 0);
   const AdamConsts ak = adam_consts(lr, b1, b2, eps, wd, t);
   double* sqo = (sq_out && sq_out->defined()) ? sq_out->data_ptr<double>() : nullptr;
+  const long* kp = nullptr;
+  int nkeep = 0;
+  if (keep && keep->defined()) {
+    TORCH_CHECK(keep->is_cuda() && keep->scalar_type() == at::kLong && keep->is_contiguous() && keep->dim() == 2 &&
+                    keep->size(1) == 2,
+                "zero_adamw_allgather: keep must be a [k, 2] int64 CUDA tensor");
+    kp = keep->data_ptr<int64_t>();
+    nkeep = (int)keep->size(0);
+  }
+  int* gw = nullptr;
+  if (gen_word && gen_word->defined()) {
+    TORCH_CHECK(gen_word->is_cuda() && gen_word->scalar_type() == at::kInt, "zero_adamw_allgather: gen_word int32");
+    gw = gen_word->data_ptr<int>();
+  }
   const int nb = comm_blocks(n * 2, blocks);
   zero_adamw_allgather_kernel<<<nb, kCommThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
       c, sp, (int)nparts, master.data_ptr<float>(), grad.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
-      w16, m32, n, ak, (float)max_norm, sqo, gather_master ? 1 : 0);
+      w16, m32, n, ak, (float)max_norm, sqo, gather_master ? 1 : 0, kp, nkeep, gw);
   count_launch();
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return 3;

@@ -42,7 +42,30 @@ enum GemmEpi : int {
   EPI_PARTIAL = 4,  // ws[split](f32) = acc   (split-K partial, reduced by splitk_reduce)
 };
 
+// All-gather fused into the GEMM (ZeRO-1 forward): B is a weight stored in a flat bf16
+// buffer partitioned over the ranks with the reference's partition rule
+// (dtrain/comm.py:220-226); each rank's own partition is current and the rest is
+// pulled from the owners' peer-mapped copies by the gather warps, k-block by k-block,
+// while the MMA pipeline consumes the k-blocks already in place.
+constexpr int kGatherRanks = 8;
+constexpr int kGatherMaxKb = 128;   // K <= 8192
+constexpr int kGatherWarps = 2;
+// state[] layout (int32): [0, 128) per-k-block arrival counters, then
+enum : int { GS_TICKET = 128, GS_DONE = 129, GS_FAIL = 130, GS_GEN = 131, GS_SITES = 256 };
+
+struct GatherArgs {
+  const bf16* peer[kGatherRanks];  // every rank's copy of B[0][0] (peer-mapped)
+  bf16* local;                     // this rank's copy (the TMA source)
+  long woff;                       // flat index of B[0][0] in the partitioned buffer
+  long nflat;                      // elements of the partitioned buffer
+  int rank, world;
+  int sub;                         // work units per k-block
+  int site;                        // this weight's slot in state[GS_SITES + site]
+  int* state;
+};
+
 struct GemmArgs {
+  GatherArgs g;
   int M, N, K;
   int epi;
   int splits;        // split-K factor (>= 1)
@@ -205,8 +228,50 @@ __device__ __forceinline__ void epi_chunk(const GemmArgs& a, const CUtensorMap* 
   }
 }
 
-template <int BN, bool A_MN, bool B_MN>
-__global__ void __launch_bounds__(kThreads, 1)
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+__device__ __forceinline__ void gather_bar() {
+  asm volatile("bar.sync 1, %0;" ::"r"(kGatherWarps * 32) : "memory");
+}
+
+// [lo, hi) of partition c of n elements over W ranks (first n % W get one more).
+__device__ __forceinline__ void part_bounds(long n, int W, int c, long& lo, long& hi) {
+  const long base = n / W, extra = n % W;
+  lo = c * base + min((long)c, extra);
+  hi = lo + base + (c < extra ? 1 : 0);
+}
+
+// Copy B elements [s, e) (indices relative to B[0][0]) from src to dst with the
+// gather warps: 16-byte peer loads, eight in flight per thread, scalar edges.
+__device__ __forceinline__ void gather_copy(const bf16* __restrict__ src, bf16* __restrict__ dst, long s, long e,
+                                            int t) {
+  constexpr int NT = kGatherWarps * 32;
+  const long vs = min(e, (s + 7) & ~7L), ve = max(vs, e & ~7L);
+  for (long i = s + t; i < vs; i += NT) dst[i] = src[i];
+  for (long i = ve + t; i < e; i += NT) dst[i] = src[i];
+  const uint4* s4 = reinterpret_cast<const uint4*>(src + vs);
+  uint4* d4 = reinterpret_cast<uint4*>(dst + vs);
+  const long nv = (ve - vs) >> 3;
+  constexpr int U = 8;  // 8 KB in flight per CTA covers the NVLink load latency at ~770 GB/s over 148 SMs
+  long i = t;
+  for (; i + (U - 1) * NT < nv; i += U * NT) {
+    uint4 r[U];
+#pragma unroll
+    for (int j = 0; j < U; ++j) r[j] = __ldcg(s4 + i + j * NT);
+#pragma unroll
+    for (int j = 0; j < U; ++j) d4[i + j * NT] = r[j];
+  }
+  for (; i < nv; i += NT) d4[i] = __ldcg(s4 + i);
+}
+
+template <int BN, bool A_MN, bool B_MN, bool GATHER = false>
+__global__ void __launch_bounds__(GATHER ? kThreads + kGatherWarps * 32 : kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmAux,
                    GemmArgs args) {
@@ -220,6 +285,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tempty_bar = tfull_bar + 2;           // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* gather_gen = abort_flag + 1;  // GATHER: generation to reach, 0 = nothing to pull
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -234,6 +300,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tempty_bar[b], kEpiWarps);
     }
     *abort_flag = 0;
+    if (GATHER) {
+      // The weight needs pulling when the optimizer published a generation this
+      // call site has not gathered yet.  Only the grid's last CTA updates the
+      // site's generation (at exit), so every CTA reads the same pair here.
+      const int need = *reinterpret_cast<volatile int*>(args.g.state + GS_GEN);
+      const int have = *reinterpret_cast<volatile int*>(args.g.state + GS_SITES + args.g.site);
+      *gather_gen = (need != have) ? need : 0;
+    }
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -250,6 +324,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int kb_total = (K + kBK - 1) / kBK;
   const int splits = args.splits;
   const int units = mt * nt * splits;
+  const bool gathering = GATHER && *gather_gen != 0;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -257,6 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      uint64_t ready_lo = 0, ready_hi = 0;  // GATHER: k-blocks known to be in place (kb < 128)
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
         const int t = u / splits, sp = u % splits;
         int mi, ni;
@@ -264,6 +340,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int m0 = mi * kBM, n0 = ni * BN;
         const int kb0 = (int)((long)kb_total * sp / splits), kb1 = (int)((long)kb_total * (sp + 1) / splits);
         for (int kb = kb0; kb < kb1; ++kb) {
+          if (GATHER && gathering && !((((kb < 64) ? ready_lo : ready_hi) >> (kb & 63)) & 1ull)) {
+            // wait until every work unit of this k-block has landed in local memory
+            const int* cnt = args.g.state + kb;
+            if (ld_acquire_gpu(cnt) < args.g.sub) {
+              const uint64_t t0 = globaltimer_ns();
+              for (uint32_t i = 1;; ++i) {
+                if (ld_acquire_gpu(cnt) >= args.g.sub) break;
+                if ((i & 63u) == 0u) {
+                  if (*abort_flag) { ok = false; break; }
+                  if (globaltimer_ns() - t0 > kPipeWaitNs) {
+                    set_status(kStatusMbarTimeout);
+                    *abort_flag = 1;
+                    ok = false;
+                    break;
+                  }
+                }
+              }
+              if (!ok) break;
+            }
+            // generic-proxy stores of other CTAs -> this CTA's TMA (async proxy) reads
+            fence_proxy_async_global();
+            if (kb < 64) ready_lo |= 1ull << kb;
+            else ready_hi |= 1ull << (kb & 63);
+          }
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag)) { ok = false; break; }
           uint8_t* sA = smem + stage * Cfg::STAGE_BYTES;
           uint8_t* sB = sA + Cfg::A_BYTES;
@@ -323,6 +423,43 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (++ab == 2) { ab = 0; aphase ^= 1; }
       }
     }
+  } else if (GATHER && warp >= 2 + kEpiWarps) {
+    // -------------------------------------------------------------- gather warps
+    // Work units (k-block kb, piece s) are handed out by a grid-wide ticket in
+    // k-block order, so whichever CTAs are resident pull the earliest k-blocks
+    // first and no CTA waits on a CTA that has not started.
+    if (gathering) {
+      __shared__ int s_ticket;
+      const int gt = threadIdx.x - (2 + kEpiWarps) * 32;
+      const GatherArgs& g = args.g;
+      const int total = kb_total * g.sub;
+      for (;;) {
+        if (gt == 0) s_ticket = atomicAdd(g.state + GS_TICKET, 1);
+        gather_bar();
+        const int u = s_ticket;
+        gather_bar();
+        if (u >= total) break;
+        const int kb = u / g.sub, pc = u - kb * g.sub;
+        const long r1 = min((long)K, (long)(kb + 1) * kBK);
+        const long e0 = (long)kb * kBK * N, e1 = r1 * N;
+        const long len = e1 - e0;
+        const long step = (((len + g.sub - 1) / g.sub) + 7) & ~7L;
+        const long s = min(e1, e0 + pc * step), e = min(e1, s + step);
+        for (int p = 0; p < g.world; ++p) {
+          if (p == g.rank) continue;
+          long lo, hi;
+          part_bounds(g.nflat, g.world, p, lo, hi);
+          const long a0 = max(s, lo - g.woff), a1 = min(e, hi - g.woff);
+          if (a0 < a1) gather_copy(g.peer[p], g.local, a0, a1, gt);
+        }
+        fence_proxy_async_global();
+        gather_bar();
+        if (gt == 0) {
+          __threadfence();
+          atomicAdd(g.state + kb, 1);
+        }
+      }
+    }
   } else {
     // -------------------------------------------------------------- epilogue
     const int ew = warp - 2;       // 0..7
@@ -378,6 +515,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+  if (GATHER && threadIdx.x == 0) {
+    // The last CTA to leave resets the counters for the next launch and records
+    // that this call site now holds generation `gather_gen` (unless a wait failed).
+    int* st = args.g.state;
+    if (*abort_flag) atomicOr(st + GS_FAIL, 1);
+    __threadfence();
+    if (atomicAdd(st + GS_DONE, 1) == (int)gridDim.x - 1) {
+      __threadfence();
+      volatile int* vs = st;
+      for (int i = 0; i < kb_total; ++i) vs[i] = 0;
+      vs[GS_TICKET] = 0;
+      if (*gather_gen != 0 && vs[GS_FAIL] == 0) vs[GS_SITES + args.g.site] = *gather_gen;
+      vs[GS_FAIL] = 0;
+      vs[GS_DONE] = 0;
+      __threadfence();
+    }
   }
 }
 
@@ -682,12 +836,12 @@ static int num_sms() {
   return n;
 }
 
-template <int BN, bool A_MN, bool B_MN>
+template <int BN, bool A_MN, bool B_MN, bool GATHER = false>
 static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const CUtensorMap& tx,
                         const GemmArgs& a, cudaStream_t st) {
   using Cfg = GemmCfg<BN>;
   static bool attr_set = false;
-  auto kern = gemm_tc_kernel<BN, A_MN, B_MN>;
+  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, GATHER>;
   if (!attr_set) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
     attr_set = true;
@@ -695,7 +849,7 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
   const int mt = (a.M + kBM - 1) / kBM, nt = (a.N + BN - 1) / BN;
   const int units = mt * nt * a.splits;
   const int grid = std::min(units, num_sms());
-  kern<<<grid, kThreads, Cfg::SMEM_BYTES, st>>>(ta, tb, to, tx, a);
+  kern<<<grid, GATHER ? kThreads + kGatherWarps * 32 : kThreads, Cfg::SMEM_BYTES, st>>>(ta, tb, to, tx, a);
   count_launch();
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -802,10 +956,11 @@ static void choose_tiling(int M, int N, int K, int& bn, int& splits, bool allow_
 }
 
 // a: stored [M,K] (a_trans=false) or [K,M] (a_trans=true); b: stored [K,N] (b_trans=false) or [N,K] (b_trans=true).
-void gemm(torch::Tensor a, bool a_trans, torch::Tensor b, bool b_trans, torch::Tensor out, int64_t epi,
-          c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> resid, c10::optional<torch::Tensor> aux,
-          double alpha, bool accumulate, int64_t force_bn, int64_t force_splits,
-          c10::optional<torch::Tensor> workspace) {
+// `gather` (forward GEMMs of ZeRO-1 only): B's peer partitions are pulled in the kernel.
+static void gemm_impl(torch::Tensor a, bool a_trans, torch::Tensor b, bool b_trans, torch::Tensor out, int64_t epi,
+                      c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> resid,
+                      c10::optional<torch::Tensor> aux, double alpha, bool accumulate, int64_t force_bn,
+                      int64_t force_splits, c10::optional<torch::Tensor> workspace, const GatherArgs* gather) {
   TORCH_CHECK(a.is_cuda() && b.is_cuda() && out.is_cuda(), "gemm: CUDA tensors expected");
   TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm: bf16 operands expected");
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && out.dim() == 2, "gemm: 2-D tensors expected");
@@ -859,16 +1014,24 @@ void gemm(torch::Tensor a, bool a_trans, torch::Tensor b, bool b_trans, torch::T
   }
   TORCH_CHECK((epi != EPI_GELU && epi != EPI_DGELU) || auxt.defined(), "gemm: gelu epilogues need aux");
 
+  if (gather) {
+    TORCH_CHECK(!a_trans && !b_trans && (epi == EPI_BF16 || epi == EPI_GELU) && !accumulate,
+                "gemm_gather: forward GEMMs (X @ W, bf16 / GELU epilogue) only");
+    TORCH_CHECK(b.is_contiguous() && (K + kBK - 1) / kBK <= kGatherMaxKb, "gemm_gather: B must be contiguous, K <= 8192");
+    args.g = *gather;
+    args.g.local = reinterpret_cast<bf16*>(b.data_ptr());
+    args.g.sub = (int)std::max<long>(1, std::min<long>(4096, ((long)kBK * N * 2 + 16383) / 16384));
+  }
   // split-K is only wired for the fp32 / bf16 plain epilogues without bias or residual
-  const bool can_split = (epi == EPI_F32) || (epi == EPI_BF16 && !args.bias && !args.resid);
+  const bool can_split = !gather && ((epi == EPI_F32) || (epi == EPI_BF16 && !args.bias && !args.resid));
   int bn, splits;
   choose_tiling((int)M, (int)N, (int)K, bn, splits, can_split);
   // 2-SM 256x256 pair tiles whenever the 1-SM choice is 128x256 and M spans a pair
   // (force_bn: 128 / 256 pick a 1-SM width, 512 the 2-SM path)
-  bool pair2 = (bn == 256 && M > 128);
+  bool pair2 = (bn == 256 && M > 128 && !gather);
   if (pair2) splits = choose_splits2((int)M, (int)N, (int)K, can_split);
   if (force_bn > 0) {
-    pair2 = (force_bn == 512);
+    pair2 = (force_bn == 512) && !gather;
     bn = pair2 ? 256 : (int)force_bn;
   }
   if (force_splits > 0) splits = (int)force_splits;
@@ -906,7 +1069,10 @@ void gemm(torch::Tensor a, bool a_trans, torch::Tensor b, bool b_trans, torch::T
   else if (!a_trans && b_trans) launch_gemm<BNV, false, false>(ta, tb, to, tx, run, st); \
   else if (a_trans && !b_trans) launch_gemm<BNV, true, true>(ta, tb, to, tx, run, st);   \
   else launch_gemm<BNV, true, false>(ta, tb, to, tx, run, st);
-  if (pair2) {
+  if (gather) {
+    if (bn == 256) launch_gemm<256, false, true, true>(ta, tb, to, tx, run, st);
+    else launch_gemm<128, false, true, true>(ta, tb, to, tx, run, st);
+  } else if (pair2) {
     if (!a_trans && !b_trans) launch_gemm2<false, true>(ta, tb, to, tx, run, st);
     else if (!a_trans && b_trans) launch_gemm2<false, false>(ta, tb, to, tx, run, st);
     else if (a_trans && !b_trans) launch_gemm2<true, true>(ta, tb, to, tx, run, st);
@@ -930,6 +1096,42 @@ void gemm(torch::Tensor a, bool a_trans, torch::Tensor b, bool b_trans, torch::T
     count_launch();
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
+}
+
+void gemm(torch::Tensor a, bool a_trans, torch::Tensor b, bool b_trans, torch::Tensor out, int64_t epi,
+          c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> resid, c10::optional<torch::Tensor> aux,
+          double alpha, bool accumulate, int64_t force_bn, int64_t force_splits,
+          c10::optional<torch::Tensor> workspace) {
+  gemm_impl(a, a_trans, b, b_trans, out, epi, bias, resid, aux, alpha, accumulate, force_bn, force_splits, workspace,
+            nullptr);
+}
+
+// Forward GEMM out = X @ W (+ epilogue) with W's all-gather fused in: `b` is this
+// rank's copy of W inside a flat bf16 buffer of `nflat` elements partitioned over
+// `peers.size()` ranks (W starts at flat index `woff`; peers[r] is rank r's address
+// of W[0][0], peer-mapped).  When state[GS_GEN] differs from state[GS_SITES + site]
+// the kernel first pulls the other ranks' partitions of W into `b`, k-block by
+// k-block, while the MMAs consume the k-blocks already in place; otherwise it is the
+// plain GEMM.  All calls that share `state` must run on one stream.
+void gemm_gather(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t epi, c10::optional<torch::Tensor> bias,
+                 c10::optional<torch::Tensor> resid, c10::optional<torch::Tensor> aux, std::vector<int64_t> peers,
+                 int64_t rank, int64_t woff, int64_t nflat, torch::Tensor state, int64_t site) {
+  const int W = (int)peers.size();
+  TORCH_CHECK(W >= 1 && W <= kGatherRanks && rank >= 0 && rank < W, "gemm_gather: 1..8 ranks");
+  TORCH_CHECK(state.is_cuda() && state.scalar_type() == at::kInt && state.is_contiguous() &&
+                  state.numel() > GS_SITES + site && site >= 0,
+              "gemm_gather: state must be an int32 CUDA tensor with room for the site");
+  TORCH_CHECK(woff >= 0 && woff + b.numel() <= nflat, "gemm_gather: W outside the flat buffer");
+  TORCH_CHECK(reinterpret_cast<int64_t>(b.data_ptr()) == peers[rank], "gemm_gather: peers[rank] must be b");
+  GatherArgs g{};
+  for (int r = 0; r < W; ++r) g.peer[r] = reinterpret_cast<const bf16*>(peers[r]);
+  g.woff = woff;
+  g.nflat = nflat;
+  g.rank = (int)rank;
+  g.world = W;
+  g.site = (int)site;
+  g.state = state.data_ptr<int>();
+  gemm_impl(a, false, b, false, out, epi, bias, resid, aux, 1.0, false, 0, 0, c10::nullopt, &g);
 }
 
 // Returns the (BN, splits) the heuristic would pick, for tests and tuning.

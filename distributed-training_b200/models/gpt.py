@@ -130,6 +130,13 @@ class GPT(nn.Module):
         self._bad_ids = None
 
     # ---------------------------------------------------------------- params
+    def gemm_weights(self):
+        """The weights whose first consumer in the forward is a GEMM (Linear.w)."""
+        ws = []
+        for b in self.blocks:
+            ws += [b.qkv.w, b.proj.w, b.fc.w, b.out.w]
+        return ws + [self.head.w]
+
     def named_parameters_list(self):
         return list(self.named_parameters())
 
@@ -222,6 +229,17 @@ class _EmbedFn(torch.autograd.Function):
         return None, None, dtok, dpos
 
 
+def _lin(fp: FlatParams, x: torch.Tensor, w, **kw) -> torch.Tensor:
+    """Forward GEMM ``x @ w`` on the bf16 working copy.  Under ZeRO-1 on GPUs
+    (``fp.gather`` set) the weight's all-gather from the other ranks runs inside
+    the GEMM kernel."""
+    K = _K()
+    g = fp.gather
+    if g is not None and id(w) in g.sites:
+        return K.gemm_gather(x, fp.work_view(w), g, id(w), **kw)
+    return K.gemm(x, fp.work_view(w), **kw)
+
+
 class _BlockFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, blk, *params):
@@ -234,13 +252,13 @@ class _BlockFn(torch.autograd.Function):
         N = B * T
         x2d = x.reshape(N, C)
         h1, mu1, rs1 = K.layernorm_fwd(x2d, W(blk.ln1.w), W(blk.ln1.b))
-        qkv = K.gemm(h1, W(blk.qkv.w), bias=W(blk.qkv.b))
+        qkv = _lin(fp, h1, blk.qkv.w, bias=W(blk.qkv.b))
         a, lse = K.attn_fwd(qkv, B, T, H, D)
-        x2 = K.gemm(a, W(blk.proj.w), bias=W(blk.proj.b), resid=x2d)
+        x2 = _lin(fp, a, blk.proj.w, bias=W(blk.proj.b), resid=x2d)
         h2, mu2, rs2 = K.layernorm_fwd(x2, W(blk.ln2.w), W(blk.ln2.b))
         pre = torch.empty(N, 4 * C, dtype=torch.bfloat16, device=x.device)
-        act = K.gemm(h2, W(blk.fc.w), epi=K.EPI_GELU, bias=W(blk.fc.b), aux=pre)
-        x3 = K.gemm(act, W(blk.out.w), bias=W(blk.out.b), resid=x2)
+        act = _lin(fp, h2, blk.fc.w, epi=K.EPI_GELU, bias=W(blk.fc.b), aux=pre)
+        x3 = _lin(fp, act, blk.out.w, bias=W(blk.out.b), resid=x2)
         ctx.save_for_backward(x2d, h1, mu1, rs1, qkv, a, lse, x2, h2, mu2, rs2, pre, act)
         ctx.blk = blk
         ctx.dims = (B, T, C, H, D)
@@ -304,7 +322,7 @@ class _HeadLossFn(torch.autograd.Function):
         N = B * T
         x2d = x.reshape(N, C)
         h, mu, rs = K.layernorm_fwd(x2d, W(gpt.ln.w), W(gpt.ln.b))
-        logits = K.gemm(h, W(gpt.head.w))
+        logits = _lin(fp, h, gpt.head.w)
         loss, lse = K.xent_fwd(logits, targets)
         ctx.save_for_backward(x2d, h, mu, rs, lse, targets)
         ctx.logits = logits
@@ -337,4 +355,4 @@ def _head_logits(gpt: GPT, x: torch.Tensor) -> torch.Tensor:
     W = gpt.flat.work_view
     B, T, C = x.shape
     h, _, _ = K.layernorm_fwd(x.reshape(B * T, C), W(gpt.ln.w), W(gpt.ln.b))
-    return K.gemm(h, W(gpt.head.w)).view(B, T, -1)
+    return _lin(gpt.flat, h, gpt.head.w).view(B, T, -1)

@@ -43,6 +43,8 @@ class FlatParams:
                 self.master[o:o + k].copy_(p.detach().reshape(-1))
                 p.data = self.master[o:o + k].view(p.shape)
         self.work = None
+        # set by ZeRO-1 on GPUs: forward GEMMs all-gather their weights in-kernel
+        self.gather = None
         if with_work:
             if work_buffer is None:
                 work_buffer = torch.empty(self.n, dtype=torch.bfloat16, device=self.device)

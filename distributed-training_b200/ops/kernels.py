@@ -36,6 +36,18 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, *, a
     return out
 
 
+def gemm_gather(a: torch.Tensor, b: torch.Tensor, plan, key, *, epi: int = EPI_BF16,
+                bias: torch.Tensor | None = None, resid: torch.Tensor | None = None,
+                aux: torch.Tensor | None = None) -> torch.Tensor:
+    """Forward GEMM ``a @ b`` whose B (a weight in the ZeRO-partitioned bf16 buffer)
+    is all-gathered inside the kernel: ``plan`` describes the partitioned buffer
+    (``parallel/zero.py:GatherPlan``) and ``key`` names the weight in it."""
+    site, woff, peers = plan.sites[key]
+    out = torch.empty(a.shape[0], b.shape[1], dtype=torch.bfloat16, device=a.device)
+    lib().gemm_gather(a, b, out, epi, bias, resid, aux, peers, plan.rank, woff, plan.nflat, plan.state, site)
+    return out
+
+
 def layernorm_fwd(x: torch.Tensor, w16: torch.Tensor, b16: torch.Tensor, eps: float = 1e-5):
     """Returns (y bf16, mean fp32 [rows], rstd fp32 [rows])."""
     return lib().layernorm_fwd(x, w16, b16, eps)

@@ -19,7 +19,15 @@ GPU path (``NVLinkGroup``), two kernels per step:
    fixed order (identical global norm everywhere), applies the clip factor and
    AdamW to its slice of the partition - fp32 master plus bf16 working copy - and
    after a cross-GPU barrier pulls the peers' updated bf16 partitions straight
-   into the working buffer the next forward's GEMMs read.
+   into the working buffer the next forward's GEMMs read;
+3. with ``gather_gemm`` (the default for bf16 models on 2+ GPUs) step 2 pulls
+   only the parameters that are not Linear weights (embeddings, LayerNorm,
+   biases) and publishes a new generation number; each Linear weight is pulled
+   by the first forward GEMM that reads it (``gemm_gather``): gather warps inside
+   the GEMM copy the other ranks' partitions k-block by k-block into local memory
+   while the tensor cores consume the k-blocks already in place.  Later forwards
+   of the same step (gradient accumulation) see the generation already gathered
+   and skip the copy.
 
 The fp32 masters of other partitions are gathered only when needed
 (``gather_params()``, e.g. before a checkpoint), which halves the all-gather
@@ -38,8 +46,49 @@ from ..ops.optim import AdamW, clip_scale
 from .comm import partition
 
 
+GS_GEN = 131     # gemm.cu: state word holding the generation the weights must reach
+GS_SITES = 256   # gemm.cu: first per-weight "generation gathered" word
+
+
+def keep_intervals(n: int, skip: list[tuple[int, int]]) -> list[tuple[int, int]]:
+    """Complement of the (possibly unsorted, non-overlapping) ``skip`` intervals in [0, n)."""
+    out, cur = [], 0
+    for lo, hi in sorted(skip):
+        if lo > cur:
+            out.append((cur, lo))
+        cur = max(cur, hi)
+    if cur < n:
+        out.append((cur, n))
+    return out
+
+
+class GatherPlan:
+    """What the in-GEMM all-gather needs to know about the partitioned bf16 buffer:
+    per weight (keyed by ``id(param)``) its site slot, flat offset and every
+    rank's address of it, plus the shared int32 state words (``gemm.cu: GS_*``)."""
+
+    def __init__(self, fp, weights, work_ptrs: list[int], rank: int):
+        self.rank = rank
+        self.nflat = fp.n
+        self.sites = {}
+        skip = []
+        for s, w in enumerate(weights):
+            off, k = fp.slot(fp.index[id(w)])
+            self.sites[id(w)] = (s, off, [p + 2 * off for p in work_ptrs])
+            skip.append((off, off + k))
+        self.state = torch.zeros(GS_SITES + max(len(weights), 1), dtype=torch.int32, device=fp.device)
+        self.gen_word = self.state[GS_GEN:GS_GEN + 1]
+        keep = keep_intervals(fp.n, skip)
+        self.keep = torch.tensor(keep if keep else [(0, 0)], dtype=torch.int64, device=fp.device).reshape(-1, 2)
+
+    def mark_gathered(self):
+        """Record (on the device) that every weight holds the current generation."""
+        self.state[GS_SITES:GS_SITES + len(self.sites)].copy_(self.gen_word.expand(len(self.sites)))
+
+
 class ZeroAdamW:
-    def __init__(self, model, pg, max_grad_norm: float | None = None, gather_master: bool | None = None, **adam):
+    def __init__(self, model, pg, max_grad_norm: float | None = None, gather_master: bool | None = None,
+                 gather_gemm: bool = True, **adam):
         self.pg = pg
         self.model = model
         self.params = list(model.parameters())
@@ -58,6 +107,10 @@ class ZeroAdamW:
             self._sq_parts = pg.alloc(128, torch.float64)
             self._sq_total = torch.zeros(1, dtype=torch.float64, device=pg.device)
             self.gather_master = (not fused) if gather_master is None else gather_master
+            self.plan = None
+            if fused and gather_gemm and pg.world > 1 and hasattr(model, "gemm_weights"):
+                self.plan = GatherPlan(fp, model.gemm_weights(), self._ptrs_of(fp.work), pg.rank)
+                fp.gather = self.plan
         else:
             dtype = self.params[0].dtype
             self.flat = torch.empty(n, dtype=dtype)
@@ -116,7 +169,9 @@ class ZeroAdamW:
             pg._sigs, pg.rank, pg.epoch, sq_ptrs, nparts, self.flat, self.gflat, opt.m[0], opt.v[0],
             [self._ptrs_of(fp.work)[r] if fp.work is not None else 0 for r in range(W)],
             self._ptrs_of(self.flat), self.n, opt.lr, opt.b1, opt.b2, opt.eps, opt.wd, opt.t,
-            float(self.max_grad_norm or 0.0), self._sq_total, bool(self.gather_master), pg.timeout, 0)
+            float(self.max_grad_norm or 0.0), self._sq_total, bool(self.gather_master), pg.timeout, 0,
+            self.plan.keep if self.plan is not None else None,
+            self.plan.gen_word if self.plan is not None else None)
         pg._advance(used)
 
     def _ptrs_of(self, t: torch.Tensor):
@@ -144,9 +199,14 @@ class ZeroAdamW:
         self.pg.all_gather(self.flat.numpy())
 
     def gather_params(self):
-        """Make ``flat`` hold every partition's current fp32 parameters on every rank."""
+        """Make ``flat`` hold every partition's current fp32 parameters on every rank
+        (and the bf16 working copy every partition's weights, which the forward GEMMs
+        would otherwise pull on their next call)."""
         if self.gpu and not self.gather_master and self.pg.world > 1:
             self.pg.all_gather(self.flat)
+        if self.gpu and self.plan is not None:
+            self.pg.all_gather(self.fp.work)
+            self.plan.mark_gathered()
 
     def state_bytes(self) -> int:
         return self.opt.state_bytes()

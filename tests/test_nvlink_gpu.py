@@ -268,6 +268,45 @@ def test_zero1_matches_ddp_adamw_on_gpu():
     assert sum(r[2] for r in res) == 8 * n  # fp32 m and v, sharded exactly once across ranks
 
 
+def _zero_gather_gemm_vs_kernel_gather(pg):
+    import torch
+    from dtrain_b200.models.gpt import GPT, GPTConfig
+    from dtrain_b200.parallel.zero import ZeroAdamW
+    cfg = GPTConfig(vocab=512, ctx=128, dim=256, heads=4, layers=2, dtype="bfloat16")
+    g = torch.Generator().manual_seed(2)
+    batches = [(torch.randint(0, 512, (2, 128), generator=g).cuda(), torch.randint(0, 512, (2, 128), generator=g).cuda())
+               for _ in range(4 * pg.world)]
+    mine = batches[pg.rank::pg.world]
+    out = []
+    for gather_gemm in (True, False):
+        m = GPT(cfg, seed=0)
+        zero = ZeroAdamW(m, pg, max_grad_norm=1.0, gather_gemm=gather_gemm, lr=3e-3)
+        assert (zero.plan is not None) == gather_gemm
+        losses = []
+        for i, (x, y) in enumerate(mine):
+            if i % 2 == 0:
+                m.zero_grad()
+            _, loss = m(x, y)  # the second micro-step's forward finds the weights already gathered
+            loss.backward()
+            losses.append(float(loss.item()))
+            if i % 2 == 1:
+                zero.step()
+        zero.gather_params()
+        pg.synchronize()
+        out.append((zero.flat.clone(), zero.fp.work.clone(), losses))
+    (f1, w1, l1), (f2, w2, l2) = out
+    return ((f1 - f2).abs().max().item(), f2.abs().max().item(), bool(torch.equal(w1, f1.bfloat16())),
+            max(abs(a - b) for a, b in zip(l1, l2)))
+
+
+@needs2
+def test_zero1_gather_in_gemm_matches_gather_in_optimizer_kernel():
+    for diff, scale, work_ok, dloss in _run(2, _zero_gather_gemm_vs_kernel_gather):
+        assert diff <= 1e-5 * max(1.0, scale), diff
+        assert work_ok
+        assert dloss < 1e-3, dloss
+
+
 def _ddp_step(pg, bucket_mb, overlap=True):
     import torch
     from dtrain_b200.models.gpt import GPT, GPTConfig
