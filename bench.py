@@ -147,7 +147,8 @@ def run_ours(a, rank, world, local):
                     "--dim", str(M["dim"]), "--heads", str(M["heads"]), "--layers", str(M["layers"]),
                     "--lr", "6e-4", "--clip", "1.0", "--bucket-mb", str(a.bucket_mb), "--data", "synthetic",
                     "--vocab", str(M["vocab"]), "--algo", a.algo, "--accum", str(accum)]
-                   + ([] if a.overlap else ["--no-overlap"]) + (["--cuda-graph"] if a.cuda_graph else []))
+                   + ([] if a.overlap else ["--no-overlap"]) + (["--cuda-graph"] if a.cuda_graph else [])
+                   + (["--no-gather-gemm"] if a.no_gather_gemm else []))
     cfg = GPTConfig(dtype="bfloat16", **M)
     tr = T.Trainer(args, cfg, dev, pg)
     data = SyntheticData(M["vocab"])
@@ -193,7 +194,9 @@ def run_ours(a, rank, world, local):
                    "grad_sync": ("per-bucket all-reduce overlapped with backward"
                                  if (tr.ddp is not None and tr.ddp.overlap) else
                                  "one all-reduce of the flat gradient after backward") if C["mode"] == "ddp" else
-                   "reduce-scatter + fused AdamW/all-gather",
+                   ("reduce-scatter + fused AdamW/all-gather" if a.no_gather_gemm else
+                    "reduce-scatter + fused AdamW (non-GEMM params gathered there); Linear weights all-gathered "
+                    "inside the forward GEMMs"),
                    "optimizer": "AdamW, clip 1.0", "allreduce_order": a.algo,
                    "cuda_graph": ("forward+backward captured once and replayed; gradient sync and optimizer "
                                   "eager" if a.cuda_graph else False),
@@ -310,6 +313,9 @@ def main():
     ap.add_argument("--no-cuda-graph", dest="cuda_graph", action="store_false",
                     help="launch every kernel from Python each step instead of replaying the captured "
                          "forward+backward graph")
+    ap.add_argument("--no-gather-gemm", action="store_true",
+                    help="ZeRO: all-gather the parameters in the optimizer kernel instead of inside the forward "
+                         "GEMMs")
     ap.add_argument("--overlap", action="store_true",
                     help="all-reduce each gradient bucket during backward (default: one all-reduce of the flat "
                          "gradient after backward, measured faster on B200)")
