@@ -1,6 +1,6 @@
 """Per-kernel timings of the sm_100a kernels on the GPT-2-small training shapes.
 
-    python benchmarks/kernel_bench.py [--only gemm,attn,ln,xent,adamw] [--iters 20]
+    python benchmarks/kernel_bench.py [--only gemm,gather,attn,ln,xent,adamw] [--iters 20]
 
 Each kernel is timed with CUDA events on the current stream after warm-up, with
 a synchronize on both sides and a cold L2 (see ``timeit``); the median over
@@ -58,10 +58,61 @@ def timeit(fn, iters):
     return ts[len(ts) // 2] * 1e3  # us
 
 
+def gather_cases(a, rep, N, C, V):
+    """ZeRO-1 forward GEMM with the weight's all-gather fused in (``gemm_gather``).
+
+    One GPU emulates ``--gather-world`` ranks: each rank's copy of the weight is a
+    separate buffer on this GPU holding only its own partition, so the pulled
+    bytes come from local HBM here, not over NVLink.  Reported per shape:
+    ``gather_pull`` (the call that pulls (W-1)/W of the weight; every timed call
+    uses a fresh call site so it pulls), ``gather_nopull`` (same kernel, weight
+    already gathered), ``gemm_plain`` (the ordinary GEMM's own tiling choice) and
+    ``copy_then_gemm`` (the unfused sequence: copy the other partitions, then GEMM).
+    """
+    from types import SimpleNamespace
+
+    from dtrain_b200.parallel.comm import partition
+    from dtrain_b200.parallel.zero import GS_GEN, GS_SITES
+
+    W = a.gather_world
+    shapes = {"qkv": (C, 3 * C), "proj": (C, C), "fc": (C, 4 * C), "out": (4 * C, C), "head": (C, V)}
+    for name in a.gather_shapes.split(","):
+        kin, kout = shapes[name]
+        n = kin * kout
+        bounds = partition(n, W)
+        truth = (torch.randn(n, device="cuda") * 0.02).bfloat16()
+        copies = [truth.clone() for _ in range(W)]
+        x = torch.randn(N, kin, device="cuda").bfloat16()
+        nsites = a.iters + 8
+        state = torch.zeros(GS_SITES + nsites, dtype=torch.int32, device="cuda")
+        state[GS_GEN] = 1
+        peers = [c.data_ptr() for c in copies]
+        plan = SimpleNamespace(rank=0, nflat=n, state=state, sites={i: (i, 0, peers) for i in range(nsites)})
+        w = copies[0].view(kin, kout)
+        f = 2.0 * N * kin * kout
+        pulled = (n - (bounds[1] - bounds[0])) * 2
+        it = iter(range(nsites))
+        rep(f"gather_pull_{name}_w{W}", timeit(lambda: K.gemm_gather(x, w, plan, next(it)), a.iters), f, pulled)
+        state[GS_SITES:] = 1
+        rep(f"gather_nopull_{name}_w{W}", timeit(lambda: K.gemm_gather(x, w, plan, 0), a.iters), f)
+        rep(f"gemm_plain_{name}", timeit(lambda: K.gemm(x, w), a.iters), f)
+        flat0 = copies[0]
+
+        def unfused():
+            for r in range(1, W):
+                flat0[bounds[r]:bounds[r + 1]].copy_(copies[r][bounds[r]:bounds[r + 1]])
+            return K.gemm(x, w)
+        rep(f"copy_then_gemm_{name}_w{W}", timeit(unfused, a.iters), f, pulled)
+        del truth, copies, x
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default="gemm,attn,ln,xent,adamw")
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--gather-world", type=int, default=2,
+                    help="ranks emulated on this GPU by the 'gather' case (fused all-gather -> GEMM)")
+    ap.add_argument("--gather-shapes", default="qkv,fc,out,head")
     a = ap.parse_args()
     pk_tf, pk_bw, tag = peaks()
     only = set(a.only.split(","))
@@ -97,6 +148,8 @@ def main():
             gw = torch.empty(kin, kout, device=dev)
             rep(f"gemm_dw_{name}", timeit(lambda: K.gemm(x, dy, gw, a_trans=True, epi=K.EPI_F32), a.iters), f)
             del x, w, dy, gw
+    if "gather" in only:
+        gather_cases(a, rep, N, C, V)
     if "attn" in only:
         D = C // H
         qkv = torch.randn(B * T, 3 * C, device=dev).bfloat16()
