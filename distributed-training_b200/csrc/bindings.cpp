@@ -62,6 +62,12 @@ int64_t broadcast(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::v
                   int64_t byte_offset, int64_t nbytes, int64_t root, int64_t cast_src, int64_t out16, int64_t n16,
                   double timeout_s, int64_t blocks);
 int64_t device_barrier(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, double timeout_s);
+int64_t zero_rs_adamw(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> grads,
+                      std::vector<int64_t> sq_parts, torch::Tensor master, torch::Tensor m, torch::Tensor v,
+                      std::vector<int64_t> work16, std::vector<int64_t> master32, int64_t n, double lr, double b1,
+                      double b2, double eps, double wd, int64_t t, double scale, double max_norm,
+                      c10::optional<torch::Tensor> sq_out, bool gather_master, double timeout_s, int64_t blocks,
+                      c10::optional<torch::Tensor> keep, c10::optional<torch::Tensor> gen_word);
 int64_t zero_adamw_allgather(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> sq_parts,
                              int64_t nparts, torch::Tensor master, torch::Tensor grad, torch::Tensor m,
                              torch::Tensor v, std::vector<int64_t> work16, std::vector<int64_t> master32, int64_t n,
@@ -133,6 +139,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("broadcast", &broadcast);
   m.def("device_barrier", &device_barrier);
   m.def("zero_adamw_allgather", &zero_adamw_allgather);
+  m.def("zero_rs_adamw", &zero_rs_adamw);
   m.def("comm_max_blocks", &comm_max_blocks);
   py::class_<CommEngine>(m, "CommEngine")
       .def(py::init<int64_t, int64_t, std::vector<int64_t>, double, int64_t>())

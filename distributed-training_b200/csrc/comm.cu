@@ -586,6 +586,128 @@ __global__ void __launch_bounds__(kCommThreads)
   cta_barrier(c, c.epoch + 2);
 }
 
+// Grid-wide barrier across ranks: returns once every CTA of every rank has arrived
+// at `epoch`.  CTA b of rank r publishes slot [b][r] in every rank's signal pad
+// (as cta_barrier does) and then polls all gridDim.x * world slots of its own pad.
+// Needs every CTA of the grid resident at once (comm grids are at most 128 CTAs of
+// 512 threads, four per SM); a CTA that cannot be scheduled makes the others time out.
+__device__ bool grid_barrier(const CommCtx& c, uint32_t epoch) {
+  __shared__ int failed;
+  __syncthreads();
+  if (threadIdx.x == 0) failed = 0;
+  __syncthreads();
+  if (threadIdx.x < c.world) {
+    __threadfence_system();
+    st_release_sys(c.sig.p[threadIdx.x] + blockIdx.x * kMaxRanks + c.rank, epoch);
+  }
+  const int slots = (int)gridDim.x * c.world;
+  for (int t = threadIdx.x; t < slots; t += blockDim.x) {
+    const uint32_t* f = c.sig.p[c.rank] + (t / c.world) * kMaxRanks + (t % c.world);
+    uint64_t t0 = 0;
+    for (uint32_t i = 0;; ++i) {
+      if ((int)(ld_acquire_sys(f) - epoch) >= 0) break;
+      if ((i & 63u) == 0u) {
+        if (*reinterpret_cast<volatile int*>(&failed)) break;
+        const uint64_t now = globaltimer_ns();
+        if (t0 == 0) t0 = now;
+        else if (now - t0 > c.timeout_ns) {
+          atomicExch(&failed, 1);
+          atomicCAS(c.host_status, 0, kStatusPeerTimeout);
+          set_status(kStatusPeerTimeout);
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  return failed == 0;
+}
+
+// ZeRO-1 step in ONE kernel: gradient reduce-scatter fused with the global-norm
+// clip, the sharded AdamW update and the parameter all-gather (dtrain/zero.py:45-62).
+// Phase 1: CTA b sums its slice of this rank's partition over all ranks' fp32
+//          gradients in ring order from the owner (bit-equal to dtrain's ring
+//          reduce-scatter), scales by 1/W, writes it in place and publishes the
+//          slice's fp64 sum of squares in this rank's peer-mapped sq pad.
+// Phase 2: grid-wide cross-rank barrier; every CTA then sums all ranks' partials
+//          in rank-then-CTA order (the same global norm everywhere) -> clip factor.
+// Phase 3: AdamW on the same slice (the CTA reads the gradient it has just
+//          written), fp32 master + bf16 working copy.
+// Phase 4: per-CTA barrier, then the all-gather of the bf16 working copy (only the
+//          `keep` intervals when the forward GEMMs gather the Linear weights) and
+//          optionally of the fp32 masters; a last barrier keeps this rank's
+//          partition unchanged until every peer has pulled it.
+template <int WT>
+__global__ void __launch_bounds__(kCommThreads)
+    zero_rs_adamw_kernel(CommCtx c, Peers grads, Sigs sq_parts, float* master, float* m, float* v, Peers work16,
+                         Peers master32, long n, AdamConsts ak, float scale, float max_norm, double* sq_out,
+                         int gather_master, const long* keep, int nkeep, int* gen_out) {
+  __shared__ double red[kCommThreads / 32];
+  __shared__ float s_clip;
+  if (!cta_enter(c)) return;
+  if (gen_out && blockIdx.x == 0 && threadIdx.x == 0) *gen_out = (int)(c.epoch + 1u);
+  long lo, hi, a, b;
+  chunk_bounds(n, c.world, c.rank, lo, hi);
+  cta_slice(lo, hi, a, b);
+  float* grad = reinterpret_cast<float*>(grads.p[c.rank]);
+  double s = 0.0;
+  reduce_range<float, float, WT>(grads, grad, a, b, c.world, c.rank, scale, &s);
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+    reinterpret_cast<double*>(sq_parts.p[c.rank])[blockIdx.x] = t;
+  }
+  if (!grid_barrier(c, c.epoch + 1)) return;
+  if (threadIdx.x == 0) {
+    double tot = 0.0;
+    for (int r = 0; r < c.world; ++r) {
+      const double* pp = reinterpret_cast<const double*>(sq_parts.p[r]);
+      double rs = 0.0;
+      for (int k = 0; k < (int)gridDim.x; ++k) rs += __ldcg(pp + k);
+      tot += rs;
+    }
+    float cs = 1.f;
+    const double nrm = sqrt(tot);
+    if (max_norm > 0.f && nrm > (double)max_norm && nrm != 0.0) cs = (float)((double)max_norm / (nrm + 1e-6));
+    s_clip = cs;
+    if (blockIdx.x == 0 && sq_out) sq_out[0] = tot;
+  }
+  __syncthreads();
+  const float cs = s_clip;
+  bf16* w16 = reinterpret_cast<bf16*>(work16.p[c.rank]);
+  for (long i = a + threadIdx.x; i < b; i += blockDim.x) {
+    const long k = i - lo;
+    float mm = m[k], vv = v[k], p = master[i];
+    adamw_elem(p, grad[i] * cs, mm, vv, ak);
+    m[k] = mm;
+    v[k] = vv;
+    master[i] = p;
+    if (w16) w16[i] = f2bf(p);
+  }
+  if (!cta_barrier(c, c.epoch + 2)) return;
+  for (int kk = 1; kk < c.world; ++kk) {
+    const int p = (c.rank + kk) % c.world;
+    long plo, phi, pa, pb;
+    chunk_bounds(n, c.world, p, plo, phi);
+    if (w16 && keep) {
+      for (int k = 0; k < nkeep; ++k) {
+        const long klo = max(plo, keep[2 * k]), khi = min(phi, keep[2 * k + 1]);
+        if (klo >= khi) continue;
+        long ka, kb;
+        cta_slice(klo, khi, ka, kb);
+        copy_range<bf16>(reinterpret_cast<const bf16*>(work16.p[p]), w16, ka, kb);
+      }
+    }
+    cta_slice(plo, phi, pa, pb);
+    if (w16 && !keep) copy_range<bf16>(reinterpret_cast<const bf16*>(work16.p[p]), w16, pa, pb);
+    if (gather_master) copy_range<float>(reinterpret_cast<const float*>(master32.p[p]), master, pa, pb);
+  }
+  cta_barrier(c, c.epoch + 3);
+}
+
 // ---------------------------------------------------------------- host side
 // Symmetric allocation: cudaMalloc + IPC export.  Returns (ptr, handle bytes).
 std::tuple<int64_t, torch::Tensor> symm_alloc(int64_t nbytes) {
@@ -822,6 +944,59 @@ int64_t zero_adamw_allgather(std::vector<int64_t> sigs, int64_t rank, int64_t ep
   count_launch();
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return 3;
+}
+
+// One-kernel ZeRO-1 step (zero_rs_adamw_kernel).  `grads` are every rank's
+// addresses of the flat fp32 gradient, `sq_parts` every rank's fp64 pad of at least
+// `blocks` (or 64) slots.  Returns the epochs consumed.
+int64_t zero_rs_adamw(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> grads,
+                      std::vector<int64_t> sq_parts, torch::Tensor master, torch::Tensor m, torch::Tensor v,
+                      std::vector<int64_t> work16, std::vector<int64_t> master32, int64_t n, double lr, double b1,
+                      double b2, double eps, double wd, int64_t t, double scale, double max_norm,
+                      c10::optional<torch::Tensor> sq_out, bool gather_master, double timeout_s, int64_t blocks,
+                      c10::optional<torch::Tensor> keep, c10::optional<torch::Tensor> gen_word) {
+  const int64_t nkeep_tag = (keep && keep->defined()) ? keep->size(0) + 1 : 0;
+  CommCtx c = make_ctx(sigs, rank, epoch, timeout_s, op_tag(9, n, (gather_master ? 1 : 0) + 2 * nkeep_tag));
+  TORCH_CHECK(grads.size() == sigs.size() && sq_parts.size() == sigs.size(), "zero_rs_adamw: one pointer per rank");
+  Sigs sp{};
+  for (size_t i = 0; i < sq_parts.size(); ++i) sp.p[i] = reinterpret_cast<uint32_t*>(sq_parts[i]);
+  Peers g = make_peers(grads, 0), w16 = make_peers(work16, 0), m32 = make_peers(master32, 0);
+  const AdamConsts ak = adam_consts(lr, b1, b2, eps, wd, t);
+  double* sqo = (sq_out && sq_out->defined()) ? sq_out->data_ptr<double>() : nullptr;
+  const long* kp = nullptr;
+  int nkeep = 0;
+  if (keep && keep->defined()) {
+    TORCH_CHECK(keep->is_cuda() && keep->scalar_type() == at::kLong && keep->is_contiguous() && keep->dim() == 2 &&
+                    keep->size(1) == 2,
+                "zero_rs_adamw: keep must be a [k, 2] int64 CUDA tensor");
+    kp = keep->data_ptr<int64_t>();
+    nkeep = (int)keep->size(0);
+  }
+  int* gw = nullptr;
+  if (gen_word && gen_word->defined()) {
+    TORCH_CHECK(gen_word->is_cuda() && gen_word->scalar_type() == at::kInt, "zero_rs_adamw: gen_word int32");
+    gw = gen_word->data_ptr<int>();
+  }
+  const int nb = comm_blocks(n * 4, blocks);
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  float* mp = master.data_ptr<float>();
+  float* mm = m.data_ptr<float>();
+  float* vp = v.data_ptr<float>();
+  const float sc = (float)scale, mn = (float)max_norm;
+  const int gm = gather_master ? 1 : 0;
+#define DTB_ZRA(WTV)                                                                                             \
+  zero_rs_adamw_kernel<WTV><<<nb, kCommThreads, 0, st>>>(c, g, sp, mp, mm, vp, w16, m32, n, ak, sc, mn, sqo, gm, kp, \
+                                                         nkeep, gw)
+  switch (c.world) {
+    case 2: DTB_ZRA(2); break;
+    case 4: DTB_ZRA(4); break;
+    case 8: DTB_ZRA(8); break;
+    default: DTB_ZRA(0);
+  }
+#undef DTB_ZRA
+  count_launch();
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return 4;
 }
 
 // Native per-group state so a collective on a peer-mapped tensor costs one call

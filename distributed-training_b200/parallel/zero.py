@@ -10,7 +10,9 @@ of partition r only.  Each step: reduce-scatter the gradient (this rank receives
 the summed gradient of its partition), scale by 1/W, global-norm clip, AdamW on
 the partition, all-gather the parameters.
 
-GPU path (``NVLinkGroup``), two kernels per step:
+GPU path (``NVLinkGroup``), one kernel per step on 2+ GPUs (``zero_rs_adamw``,
+``fuse_rs=True``) doing what the two-kernel path (``fuse_rs=False``, and one GPU)
+does in two launches with a kernel boundary as the grid-wide sync:
 
 1. ``reduce_scatter`` kernel: the owner of each partition reads it from every
    peer over NVLink, sums in ring order, scales by 1/W, writes it in place and
@@ -20,6 +22,9 @@ GPU path (``NVLinkGroup``), two kernels per step:
    AdamW to its slice of the partition - fp32 master plus bf16 working copy - and
    after a cross-GPU barrier pulls the peers' updated bf16 partitions straight
    into the working buffer the next forward's GEMMs read;
+In the fused kernel a grid-wide cross-rank flag barrier separates 1 from 2 and
+each CTA updates exactly the slice of the partition it reduced.
+
 3. with ``gather_gemm`` (the default for bf16 models on 2+ GPUs) step 2 pulls
    only the parameters that are not Linear weights (embeddings, LayerNorm,
    biases) and publishes a new generation number; each Linear weight is pulled
@@ -88,7 +93,7 @@ class GatherPlan:
 
 class ZeroAdamW:
     def __init__(self, model, pg, max_grad_norm: float | None = None, gather_master: bool | None = None,
-                 gather_gemm: bool = True, **adam):
+                 gather_gemm: bool = True, fuse_rs: bool = True, **adam):
         self.pg = pg
         self.model = model
         self.params = list(model.parameters())
@@ -107,6 +112,7 @@ class ZeroAdamW:
             self._sq_parts = pg.alloc(128, torch.float64)
             self._sq_total = torch.zeros(1, dtype=torch.float64, device=pg.device)
             self.gather_master = (not fused) if gather_master is None else gather_master
+            self.fuse_rs = fuse_rs
             self.plan = None
             if fused and gather_gemm and pg.world > 1 and hasattr(model, "gemm_weights"):
                 self.plan = GatherPlan(fp, model.gemm_weights(), self._ptrs_of(fp.work), pg.rank)
@@ -153,6 +159,21 @@ class ZeroAdamW:
                 fp.grad_view(p).copy_(p.grad)
         W = pg.world
         nparts = pg._rs_blocks()
+        from ..ops._ext import lib
+        sq_ptrs = [b.ptrs for b in pg.buffers if b.contains(self._sq_parts) is not None][0]
+        opt = self.opt
+        if W > 1 and self.fuse_rs:
+            # one kernel: reduce-scatter + norm exchange + clip + AdamW + all-gather
+            opt.t += 1
+            used = lib().zero_rs_adamw(
+                pg._sigs, pg.rank, pg.epoch, self._ptrs_of(self.gflat), sq_ptrs, self.flat, opt.m[0], opt.v[0],
+                [self._ptrs_of(fp.work)[r] if fp.work is not None else 0 for r in range(W)],
+                self._ptrs_of(self.flat), self.n, opt.lr, opt.b1, opt.b2, opt.eps, opt.wd, opt.t, 1.0 / W,
+                float(self.max_grad_norm or 0.0), self._sq_total, bool(self.gather_master), pg.timeout, nparts,
+                self.plan.keep if self.plan is not None else None,
+                self.plan.gen_word if self.plan is not None else None)
+            pg._advance(used)
+            return
         if W > 1:
             pg.reduce_scatter(self.gflat, scale=1.0 / W, sq_parts=self._sq_parts)
         else:
@@ -161,10 +182,7 @@ class ZeroAdamW:
             self._sq_parts.zero_()
             K.grad_sqnorm(self.gflat, self._sq_parts[:1])
             nparts = 1
-        opt = self.opt
         opt.t += 1
-        from ..ops._ext import lib
-        sq_ptrs = [b.ptrs for b in pg.buffers if b.contains(self._sq_parts) is not None][0]
         used = lib().zero_adamw_allgather(
             pg._sigs, pg.rank, pg.epoch, sq_ptrs, nparts, self.flat, self.gflat, opt.m[0], opt.v[0],
             [self._ptrs_of(fp.work)[r] if fp.work is not None else 0 for r in range(W)],

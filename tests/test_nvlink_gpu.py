@@ -268,7 +268,7 @@ def test_zero1_matches_ddp_adamw_on_gpu():
     assert sum(r[2] for r in res) == 8 * n  # fp32 m and v, sharded exactly once across ranks
 
 
-def _zero_gather_gemm_vs_kernel_gather(pg):
+def _zero_variants(pg):
     import torch
     from dtrain_b200.models.gpt import GPT, GPTConfig
     from dtrain_b200.parallel.zero import ZeroAdamW
@@ -278,9 +278,10 @@ def _zero_gather_gemm_vs_kernel_gather(pg):
                for _ in range(4 * pg.world)]
     mine = batches[pg.rank::pg.world]
     out = []
-    for gather_gemm in (True, False):
+    # (weights gathered inside the forward GEMMs, reduce-scatter fused into the update kernel)
+    for gather_gemm, fuse_rs in ((True, True), (False, True), (False, False)):
         m = GPT(cfg, seed=0)
-        zero = ZeroAdamW(m, pg, max_grad_norm=1.0, gather_gemm=gather_gemm, lr=3e-3)
+        zero = ZeroAdamW(m, pg, max_grad_norm=1.0, gather_gemm=gather_gemm, fuse_rs=fuse_rs, lr=3e-3)
         assert (zero.plan is not None) == gather_gemm
         losses = []
         for i, (x, y) in enumerate(mine):
@@ -293,18 +294,22 @@ def _zero_gather_gemm_vs_kernel_gather(pg):
                 zero.step()
         zero.gather_params()
         pg.synchronize()
-        out.append((zero.flat.clone(), zero.fp.work.clone(), losses))
-    (f1, w1, l1), (f2, w2, l2) = out
+        out.append((zero.flat.clone(), zero.fp.work.clone(), losses, zero.last_grad_norm))
+    (f1, w1, l1, n1), (f2, w2, l2, n2), (f3, w3, l3, n3) = out
     return ((f1 - f2).abs().max().item(), f2.abs().max().item(), bool(torch.equal(w1, f1.bfloat16())),
-            max(abs(a - b) for a, b in zip(l1, l2)))
+            max(abs(a - b) for a, b in zip(l1, l2)), bool(torch.equal(f2, f3)), bool(torch.equal(w2, w3)),
+            l2 == l3, n2 == n3)
 
 
 @needs2
-def test_zero1_gather_in_gemm_matches_gather_in_optimizer_kernel():
-    for diff, scale, work_ok, dloss in _run(2, _zero_gather_gemm_vs_kernel_gather):
+def test_zero1_gather_in_gemm_and_one_kernel_update_match_the_two_kernel_path():
+    for diff, scale, work_ok, dloss, master_same, work_same, loss_same, norm_same in _run(2, _zero_variants):
+        # all-gather inside the GEMMs vs inside the optimizer kernel (GEMM tiling differs: 1-SM vs 2-SM)
         assert diff <= 1e-5 * max(1.0, scale), diff
         assert work_ok
         assert dloss < 1e-3, dloss
+        # reduce-scatter fused into the update kernel vs separate kernels: the same sums in the same order
+        assert master_same and work_same and loss_same and norm_same
 
 
 def _ddp_step(pg, bucket_mb, overlap=True):
