@@ -148,7 +148,7 @@ def run_ours(a, rank, world, local):
                     "--lr", "6e-4", "--clip", "1.0", "--bucket-mb", str(a.bucket_mb), "--data", "synthetic",
                     "--vocab", str(M["vocab"]), "--algo", a.algo, "--accum", str(accum)]
                    + ([] if a.overlap else ["--no-overlap"]) + (["--cuda-graph"] if a.cuda_graph else [])
-                   + (["--no-gather-gemm"] if a.no_gather_gemm else []))
+                   + (["--gather-gemm"] if a.gather_gemm else []))
     cfg = GPTConfig(dtype="bfloat16", **M)
     tr = T.Trainer(args, cfg, dev, pg)
     data = SyntheticData(M["vocab"])
@@ -194,9 +194,9 @@ def run_ours(a, rank, world, local):
                    "grad_sync": ("per-bucket all-reduce overlapped with backward"
                                  if (tr.ddp is not None and tr.ddp.overlap) else
                                  "one all-reduce of the flat gradient after backward") if C["mode"] == "ddp" else
-                   ("reduce-scatter + fused AdamW/all-gather" if a.no_gather_gemm else
-                    "reduce-scatter + fused AdamW (non-GEMM params gathered there); Linear weights all-gathered "
-                    "inside the forward GEMMs"),
+                   ("one kernel: reduce-scatter + clip + AdamW (non-GEMM params gathered there); Linear weights "
+                    "all-gathered inside the forward GEMMs" if a.gather_gemm else
+                    "one kernel: reduce-scatter + clip + AdamW + all-gather"),
                    "optimizer": "AdamW, clip 1.0", "allreduce_order": a.algo,
                    "cuda_graph": ("forward+backward captured once and replayed; gradient sync and optimizer "
                                   "eager" if a.cuda_graph else False),
@@ -313,9 +313,9 @@ def main():
     ap.add_argument("--no-cuda-graph", dest="cuda_graph", action="store_false",
                     help="launch every kernel from Python each step instead of replaying the captured "
                          "forward+backward graph")
-    ap.add_argument("--no-gather-gemm", action="store_true",
-                    help="ZeRO: all-gather the parameters in the optimizer kernel instead of inside the forward "
-                         "GEMMs")
+    ap.add_argument("--gather-gemm", action="store_true",
+                    help="ZeRO: all-gather the Linear weights inside the forward GEMMs instead of in the optimizer "
+                         "kernel (measured 1.6%% slower on 2 GPUs, GPT-2-medium)")
     ap.add_argument("--overlap", action="store_true",
                     help="all-reduce each gradient bucket during backward (default: one all-reduce of the flat "
                          "gradient after backward, measured faster on B200)")

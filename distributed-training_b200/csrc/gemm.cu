@@ -270,6 +270,95 @@ __device__ __forceinline__ void gather_copy(const bf16* __restrict__ src, bf16* 
   for (; i < nv; i += NT) d4[i] = __ldcg(s4 + i);
 }
 
+// ---- in-GEMM all-gather roles, shared by the 1-SM and 2-SM kernels ----------
+// Thread 0 at set-up: the generation to pull (0: the weight is already current).
+// Only the grid's last CTA updates the site's generation (at exit), so every CTA
+// reads the same pair here.
+__device__ __forceinline__ int gather_generation(const GatherArgs& g) {
+  const int need = *reinterpret_cast<volatile int*>(g.state + GS_GEN);
+  const int have = *reinterpret_cast<volatile int*>(g.state + GS_SITES + g.site);
+  return (need != have) ? need : 0;
+}
+
+// TMA producer: before the first B load of k-block kb, wait (bounded) until every
+// work unit of that k-block has landed in local memory.  `ready_lo/hi` remember the
+// k-blocks already seen complete.  Returns false on timeout or abort.
+__device__ __forceinline__ bool gather_wait_kb(const GatherArgs& g, int kb, uint64_t& ready_lo, uint64_t& ready_hi,
+                                               volatile int* abort_flag) {
+  if ((((kb < 64) ? ready_lo : ready_hi) >> (kb & 63)) & 1ull) return true;
+  const int* cnt = g.state + kb;
+  if (ld_acquire_gpu(cnt) < g.sub) {
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 1;; ++i) {
+      if (ld_acquire_gpu(cnt) >= g.sub) break;
+      if ((i & 63u) == 0u) {
+        if (*abort_flag) return false;
+        if (globaltimer_ns() - t0 > kPipeWaitNs) {
+          set_status(kStatusMbarTimeout);
+          *abort_flag = 1;
+          return false;
+        }
+      }
+    }
+  }
+  // generic-proxy stores of other CTAs -> this CTA's TMA (async proxy) reads
+  fence_proxy_async_global();
+  if (kb < 64) ready_lo |= 1ull << kb;
+  else ready_hi |= 1ull << (kb & 63);
+  return true;
+}
+
+// Gather warps: work units (k-block kb, piece) are handed out by a grid-wide ticket
+// in k-block order, so whichever CTAs are resident pull the earliest k-blocks first
+// and no CTA waits on a CTA that has not started.
+__device__ __forceinline__ void gather_worker(const GatherArgs& g, int K, int N, int kb_total, int gt) {
+  __shared__ int s_ticket;
+  const int total = kb_total * g.sub;
+  for (;;) {
+    if (gt == 0) s_ticket = atomicAdd(g.state + GS_TICKET, 1);
+    gather_bar();
+    const int u = s_ticket;
+    gather_bar();
+    if (u >= total) break;
+    const int kb = u / g.sub, pc = u - kb * g.sub;
+    const long r1 = min((long)K, (long)(kb + 1) * kBK);
+    const long e0 = (long)kb * kBK * N, e1 = r1 * N;
+    const long step = ((((e1 - e0) + g.sub - 1) / g.sub) + 7) & ~7L;
+    const long s = min(e1, e0 + pc * step), e = min(e1, s + step);
+    for (int p = 0; p < g.world; ++p) {
+      if (p == g.rank) continue;
+      long lo, hi;
+      part_bounds(g.nflat, g.world, p, lo, hi);
+      const long a0 = max(s, lo - g.woff), a1 = min(e, hi - g.woff);
+      if (a0 < a1) gather_copy(g.peer[p], g.local, a0, a1, gt);
+    }
+    fence_proxy_async_global();
+    gather_bar();
+    if (gt == 0) {
+      __threadfence();
+      atomicAdd(g.state + kb, 1);
+    }
+  }
+}
+
+// Thread 0 at exit: the last CTA to leave resets the counters for the next launch
+// and records that this call site now holds generation `gen` (unless a wait failed).
+__device__ __forceinline__ void gather_exit(const GatherArgs& g, int kb_total, int gen, bool aborted) {
+  int* st = g.state;
+  if (aborted) atomicOr(st + GS_FAIL, 1);
+  __threadfence();
+  if (atomicAdd(st + GS_DONE, 1) == (int)gridDim.x - 1) {
+    __threadfence();
+    volatile int* vs = st;
+    for (int i = 0; i < kb_total; ++i) vs[i] = 0;
+    vs[GS_TICKET] = 0;
+    if (gen != 0 && vs[GS_FAIL] == 0) vs[GS_SITES + g.site] = gen;
+    vs[GS_FAIL] = 0;
+    vs[GS_DONE] = 0;
+    __threadfence();
+  }
+}
+
 template <int BN, bool A_MN, bool B_MN, bool GATHER = false>
 __global__ void __launch_bounds__(GATHER ? kThreads + kGatherWarps * 32 : kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -300,14 +389,7 @@ __global__ void __launch_bounds__(GATHER ? kThreads + kGatherWarps * 32 : kThrea
       mbar_init(&tempty_bar[b], kEpiWarps);
     }
     *abort_flag = 0;
-    if (GATHER) {
-      // The weight needs pulling when the optimizer published a generation this
-      // call site has not gathered yet.  Only the grid's last CTA updates the
-      // site's generation (at exit), so every CTA reads the same pair here.
-      const int need = *reinterpret_cast<volatile int*>(args.g.state + GS_GEN);
-      const int have = *reinterpret_cast<volatile int*>(args.g.state + GS_SITES + args.g.site);
-      *gather_gen = (need != have) ? need : 0;
-    }
+    if (GATHER) *gather_gen = gather_generation(args.g);
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -340,29 +422,9 @@ __global__ void __launch_bounds__(GATHER ? kThreads + kGatherWarps * 32 : kThrea
         const int m0 = mi * kBM, n0 = ni * BN;
         const int kb0 = (int)((long)kb_total * sp / splits), kb1 = (int)((long)kb_total * (sp + 1) / splits);
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (GATHER && gathering && !((((kb < 64) ? ready_lo : ready_hi) >> (kb & 63)) & 1ull)) {
-            // wait until every work unit of this k-block has landed in local memory
-            const int* cnt = args.g.state + kb;
-            if (ld_acquire_gpu(cnt) < args.g.sub) {
-              const uint64_t t0 = globaltimer_ns();
-              for (uint32_t i = 1;; ++i) {
-                if (ld_acquire_gpu(cnt) >= args.g.sub) break;
-                if ((i & 63u) == 0u) {
-                  if (*abort_flag) { ok = false; break; }
-                  if (globaltimer_ns() - t0 > kPipeWaitNs) {
-                    set_status(kStatusMbarTimeout);
-                    *abort_flag = 1;
-                    ok = false;
-                    break;
-                  }
-                }
-              }
-              if (!ok) break;
-            }
-            // generic-proxy stores of other CTAs -> this CTA's TMA (async proxy) reads
-            fence_proxy_async_global();
-            if (kb < 64) ready_lo |= 1ull << kb;
-            else ready_hi |= 1ull << (kb & 63);
+          if (GATHER && gathering && !gather_wait_kb(args.g, kb, ready_lo, ready_hi, abort_flag)) {
+            ok = false;
+            break;
           }
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag)) { ok = false; break; }
           uint8_t* sA = smem + stage * Cfg::STAGE_BYTES;
@@ -425,41 +487,7 @@ __global__ void __launch_bounds__(GATHER ? kThreads + kGatherWarps * 32 : kThrea
     }
   } else if (GATHER && warp >= 2 + kEpiWarps) {
     // -------------------------------------------------------------- gather warps
-    // Work units (k-block kb, piece s) are handed out by a grid-wide ticket in
-    // k-block order, so whichever CTAs are resident pull the earliest k-blocks
-    // first and no CTA waits on a CTA that has not started.
-    if (gathering) {
-      __shared__ int s_ticket;
-      const int gt = threadIdx.x - (2 + kEpiWarps) * 32;
-      const GatherArgs& g = args.g;
-      const int total = kb_total * g.sub;
-      for (;;) {
-        if (gt == 0) s_ticket = atomicAdd(g.state + GS_TICKET, 1);
-        gather_bar();
-        const int u = s_ticket;
-        gather_bar();
-        if (u >= total) break;
-        const int kb = u / g.sub, pc = u - kb * g.sub;
-        const long r1 = min((long)K, (long)(kb + 1) * kBK);
-        const long e0 = (long)kb * kBK * N, e1 = r1 * N;
-        const long len = e1 - e0;
-        const long step = (((len + g.sub - 1) / g.sub) + 7) & ~7L;
-        const long s = min(e1, e0 + pc * step), e = min(e1, s + step);
-        for (int p = 0; p < g.world; ++p) {
-          if (p == g.rank) continue;
-          long lo, hi;
-          part_bounds(g.nflat, g.world, p, lo, hi);
-          const long a0 = max(s, lo - g.woff), a1 = min(e, hi - g.woff);
-          if (a0 < a1) gather_copy(g.peer[p], g.local, a0, a1, gt);
-        }
-        fence_proxy_async_global();
-        gather_bar();
-        if (gt == 0) {
-          __threadfence();
-          atomicAdd(g.state + kb, 1);
-        }
-      }
-    }
+    if (gathering) gather_worker(args.g, K, N, kb_total, threadIdx.x - (2 + kEpiWarps) * 32);
   } else {
     // -------------------------------------------------------------- epilogue
     const int ew = warp - 2;       // 0..7
@@ -516,23 +544,7 @@ __global__ void __launch_bounds__(GATHER ? kThreads + kGatherWarps * 32 : kThrea
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
   }
-  if (GATHER && threadIdx.x == 0) {
-    // The last CTA to leave resets the counters for the next launch and records
-    // that this call site now holds generation `gather_gen` (unless a wait failed).
-    int* st = args.g.state;
-    if (*abort_flag) atomicOr(st + GS_FAIL, 1);
-    __threadfence();
-    if (atomicAdd(st + GS_DONE, 1) == (int)gridDim.x - 1) {
-      __threadfence();
-      volatile int* vs = st;
-      for (int i = 0; i < kb_total; ++i) vs[i] = 0;
-      vs[GS_TICKET] = 0;
-      if (*gather_gen != 0 && vs[GS_FAIL] == 0) vs[GS_SITES + args.g.site] = *gather_gen;
-      vs[GS_FAIL] = 0;
-      vs[GS_DONE] = 0;
-      __threadfence();
-    }
-  }
+  if (GATHER && threadIdx.x == 0) gather_exit(args.g, kb_total, *gather_gen, *abort_flag != 0);
 }
 
 // -------------------------------------------------------------------------
@@ -557,8 +569,8 @@ struct Gemm2Cfg {
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
 };
 
-template <bool A_MN, bool B_MN>
-__global__ void __launch_bounds__(kThreads, 1)
+template <bool A_MN, bool B_MN, bool GATHER = false>
+__global__ void __launch_bounds__(GATHER ? kThreads + kGatherWarps * 32 : kThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmAux,
                     GemmArgs args) {
@@ -573,6 +585,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* done_bar = tempty_bar + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* gather_gen = abort_flag + 1;  // GATHER: generation to reach, 0 = nothing to pull
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -590,6 +603,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(done_bar, 1);
     *abort_flag = 0;
+    if (GATHER) *gather_gen = gather_generation(args.g);
     fence_barrier_init_cluster();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -607,6 +621,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int splits = args.splits;
   const int units = mt * nt * splits;
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const bool gathering = GATHER && *gather_gen != 0;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -615,6 +630,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      uint64_t ready_lo = 0, ready_hi = 0;  // GATHER: k-blocks known to be in place
       for (int u = pair; u < units && ok; u += npairs) {
         const int t = u / splits, sp = u % splits;
         int mi, ni;
@@ -622,6 +638,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int m0 = mi * 256 + (int)rank * 128, n0 = ni * 256 + (int)rank * 128;
         const int kb0 = (int)((long)kb_total * sp / splits), kb1 = (int)((long)kb_total * (sp + 1) / splits);
         for (int kb = kb0; kb < kb1; ++kb) {
+          if (GATHER && gathering && !gather_wait_kb(args.g, kb, ready_lo, ready_hi, abort_flag)) {
+            ok = false;
+            break;
+          }
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag)) { ok = false; break; }
           uint8_t* sA = smem + stage * Cfg::STAGE_BYTES;
           uint8_t* sB = sA + Cfg::A_BYTES;
@@ -680,6 +700,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (++ab == 2) { ab = 0; aphase ^= 1; }
       }
     }
+  } else if (GATHER && warp >= 2 + kEpiWarps) {
+    // -------------------------------------------------------------- gather warps (both CTAs)
+    if (gathering) gather_worker(args.g, K, N, kb_total, threadIdx.x - (2 + kEpiWarps) * 32);
   } else {
     // -------------------------------------------------------------- epilogue (both CTAs)
     const int ew = warp - 2;
@@ -741,6 +764,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
   }
+  if (GATHER && threadIdx.x == 0) gather_exit(args.g, kb_total, *gather_gen, *abort_flag != 0);
 }
 
 // Deterministic split-K reduction: out = alpha * sum_{s=0..S-1} ws[s] (+ out).
@@ -880,11 +904,11 @@ static int max_pair_clusters() {
   return n;
 }
 
-template <bool A_MN, bool B_MN>
+template <bool A_MN, bool B_MN, bool GATHER = false>
 static void launch_gemm2(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const CUtensorMap& tx,
                          const GemmArgs& a, cudaStream_t st) {
   static bool attr_set = false;
-  auto kern = gemm_tc2_kernel<A_MN, B_MN>;
+  auto kern = gemm_tc2_kernel<A_MN, B_MN, GATHER>;
   if (!attr_set) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Gemm2Cfg::SMEM_BYTES);
     attr_set = true;
@@ -893,7 +917,7 @@ static void launch_gemm2(const CUtensorMap& ta, const CUtensorMap& tb, const CUt
   const int pairs = std::min(units, max_pair_clusters());
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs, 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3(GATHER ? kThreads + kGatherWarps * 32 : kThreads, 1, 1);
   cfg.dynamicSmemBytes = Gemm2Cfg::SMEM_BYTES;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -1028,10 +1052,10 @@ static void gemm_impl(torch::Tensor a, bool a_trans, torch::Tensor b, bool b_tra
   choose_tiling((int)M, (int)N, (int)K, bn, splits, can_split);
   // 2-SM 256x256 pair tiles whenever the 1-SM choice is 128x256 and M spans a pair
   // (force_bn: 128 / 256 pick a 1-SM width, 512 the 2-SM path)
-  bool pair2 = (bn == 256 && M > 128 && !gather);
+  bool pair2 = (bn == 256 && M > 128);
   if (pair2) splits = choose_splits2((int)M, (int)N, (int)K, can_split);
   if (force_bn > 0) {
-    pair2 = (force_bn == 512) && !gather;
+    pair2 = (force_bn == 512);
     bn = pair2 ? 256 : (int)force_bn;
   }
   if (force_splits > 0) splits = (int)force_splits;
@@ -1070,7 +1094,8 @@ static void gemm_impl(torch::Tensor a, bool a_trans, torch::Tensor b, bool b_tra
   else if (a_trans && !b_trans) launch_gemm<BNV, true, true>(ta, tb, to, tx, run, st);   \
   else launch_gemm<BNV, true, false>(ta, tb, to, tx, run, st);
   if (gather) {
-    if (bn == 256) launch_gemm<256, false, true, true>(ta, tb, to, tx, run, st);
+    if (pair2) launch_gemm2<false, true, true>(ta, tb, to, tx, run, st);
+    else if (bn == 256) launch_gemm<256, false, true, true>(ta, tb, to, tx, run, st);
     else launch_gemm<128, false, true, true>(ta, tb, to, tx, run, st);
   } else if (pair2) {
     if (!a_trans && !b_trans) launch_gemm2<false, true>(ta, tb, to, tx, run, st);

@@ -25,7 +25,9 @@ does in two launches with a kernel boundary as the grid-wide sync:
 In the fused kernel a grid-wide cross-rank flag barrier separates 1 from 2 and
 each CTA updates exactly the slice of the partition it reduced.
 
-3. with ``gather_gemm`` (the default for bf16 models on 2+ GPUs) step 2 pulls
+3. with ``gather_gemm`` (bf16 models on 2+ GPUs; off by default because the bulk
+   gather in step 2 measured faster on B200, GPT-2-medium on 2 GPUs: 115.0 vs
+   116.8 ms per step) step 2 pulls
    only the parameters that are not Linear weights (embeddings, LayerNorm,
    biases) and publishes a new generation number; each Linear weight is pulled
    by the first forward GEMM that reads it (``gemm_gather``): gather warps inside
@@ -93,7 +95,7 @@ class GatherPlan:
 
 class ZeroAdamW:
     def __init__(self, model, pg, max_grad_norm: float | None = None, gather_master: bool | None = None,
-                 gather_gemm: bool = True, fuse_rs: bool = True, **adam):
+                 gather_gemm: bool = False, fuse_rs: bool = True, **adam):
         self.pg = pg
         self.model = model
         self.params = list(model.parameters())

@@ -58,9 +58,9 @@ def parse(argv=None):
     ap.add_argument("--algo", choices=["ring", "direct"], default="ring")
     ap.add_argument("--ar-method", choices=["auto", "oneshot", "twoshot"], default="auto")
     ap.add_argument("--device", default=None, help="cpu | cuda (default: cuda for bfloat16, else cpu)")
-    ap.add_argument("--no-gather-gemm", action="store_true",
-                    help="ZeRO on GPUs: all-gather every parameter in the optimizer kernel instead of letting the "
-                         "forward GEMMs pull their weights from the other ranks")
+    ap.add_argument("--gather-gemm", action="store_true",
+                    help="ZeRO on GPUs: let the forward GEMMs pull their weights from the other ranks (all-gather "
+                         "fused into the GEMM) instead of gathering every parameter in the optimizer kernel")
     ap.add_argument("--cuda-graph", action="store_true",
                     help="GPU: capture forward+backward of a step in a CUDA graph and replay it (removes the "
                          "per-kernel host launch cost; the gradient sync and the optimizer run eagerly)")
@@ -130,7 +130,7 @@ class Trainer:
         elif a.mode == "zero":
             from .parallel.zero import ZeroAdamW
             self.zero = ZeroAdamW(self.model, pg, max_grad_norm=a.clip, lr=a.lr, weight_decay=a.wd,
-                                  gather_gemm=not getattr(a, "no_gather_gemm", False))
+                                  gather_gemm=getattr(a, "gather_gemm", False))
         if self.zero is None:
             fp = self.model.flat
             if fp is not None and self.gpu:
