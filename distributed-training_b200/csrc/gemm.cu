@@ -149,6 +149,20 @@ __device__ __forceinline__ void slab_put_f32(uint8_t* slab, int lane, const floa
   for (int j = 0; j < 8; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
 }
 
+// Epilogues whose chunk is one 32x32 bf16 tile (2 KB) stage alternate chunks in the
+// two halves of the warp's 4 KB slab; fp32 and GELU (two outputs) chunks fill it.
+__device__ __forceinline__ bool epi_double_buffered(int epi) { return epi == EPI_BF16 || epi == EPI_DGELU; }
+
+// Before packing a chunk: lane 0 waits until the store that last used this (sub-)slab
+// has read it - with two halves that is every store but the most recent one.
+__device__ __forceinline__ void epi_slab_acquire(int lane, bool dbl) {
+  if (lane == 0) {
+    if (dbl) bulk_wait_read1();
+    else bulk_wait_read0();
+  }
+  __syncwarp();
+}
+
 // Epilogue for one 32x32 chunk held in registers (this lane = one row).  Writes the
 // staging slab and lets lane 0 issue the TMA store(s).
 __device__ __forceinline__ void epi_chunk(const GemmArgs& a, const CUtensorMap* tmOut, const CUtensorMap* tmAux,
@@ -494,6 +508,10 @@ __global__ void __launch_bounds__(GATHER ? kThreads + kGatherWarps * 32 : kThrea
     const int q = warp & 3;        // TMEM lane quarter this warp may access
     const int half = ew >> 2;      // which half of the tile's columns
     uint8_t* slab = epi_smem + ew * kEpiSlab;
+    // bf16 chunks (2 KB) alternate between the two halves of the slab, so the next
+    // chunk is packed while the previous one's TMA store is still reading
+    const bool dbl = epi_double_buffered(args.epi);
+    uint32_t ck = 0;
     int ab = 0;
     uint32_t aphase = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x) {
@@ -517,16 +535,16 @@ __global__ void __launch_bounds__(GATHER ? kThreads + kGatherWarps * 32 : kThrea
         // chunk c .. c+31
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r0[j]);
-        if (lane == 0) bulk_wait_read0();  // the slab's previous store has read its source
-        __syncwarp();
-        epi_chunk(args, &tmOut, &tmAux, slab, lane, row0, n0 + c, sp, v);
+        epi_slab_acquire(lane, dbl);  // the sub-slab's previous store has read its source
+        epi_chunk(args, &tmOut, &tmAux, slab + (dbl ? (ck & 1) * 2048 : 0), lane, row0, n0 + c, sp, v);
+        ++ck;
         // chunk c+32 .. c+63
         if (n0 + c + 32 < N) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r1[j]);
-          if (lane == 0) bulk_wait_read0();
-          __syncwarp();
-          epi_chunk(args, &tmOut, &tmAux, slab, lane, row0, n0 + c + 32, sp, v);
+          epi_slab_acquire(lane, dbl);
+          epi_chunk(args, &tmOut, &tmAux, slab + (dbl ? (ck & 1) * 2048 : 0), lane, row0, n0 + c + 32, sp, v);
+          ++ck;
         }
       }
       tc_fence_before();
@@ -710,6 +728,8 @@ __global__ void __launch_bounds__(GATHER ? kThreads + kGatherWarps * 32 : kThrea
     const int half = ew >> 2;
     uint8_t* slab = epi_smem + ew * kEpiSlab;
     const uint32_t lead_tempty0 = mapa_shared(&tempty_bar[0], 0);
+    const bool dbl = epi_double_buffered(args.epi);  // see the 1-SM epilogue
+    uint32_t ck = 0;
     int ab = 0;
     uint32_t aphase = 0;
     for (int u = pair; u < units; u += npairs) {
@@ -730,17 +750,19 @@ __global__ void __launch_bounds__(GATHER ? kThreads + kGatherWarps * 32 : kThrea
         tmem_ld32_issue(tbase + c + 32, r1);
         tmem_wait_ld();
         float v[32];
+        // chunk c .. c+31
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r0[j]);
-        if (lane == 0) bulk_wait_read0();
-        __syncwarp();
-        epi_chunk(args, &tmOut, &tmAux, slab, lane, row0, n0 + c, sp, v);
+        epi_slab_acquire(lane, dbl);  // the sub-slab's previous store has read its source
+        epi_chunk(args, &tmOut, &tmAux, slab + (dbl ? (ck & 1) * 2048 : 0), lane, row0, n0 + c, sp, v);
+        ++ck;
+        // chunk c+32 .. c+63
         if (n0 + c + 32 < N) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r1[j]);
-          if (lane == 0) bulk_wait_read0();
-          __syncwarp();
-          epi_chunk(args, &tmOut, &tmAux, slab, lane, row0, n0 + c + 32, sp, v);
+          epi_slab_acquire(lane, dbl);
+          epi_chunk(args, &tmOut, &tmAux, slab + (dbl ? (ck & 1) * 2048 : 0), lane, row0, n0 + c + 32, sp, v);
+          ++ck;
         }
       }
       tc_fence_before();
