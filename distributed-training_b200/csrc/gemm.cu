@@ -511,6 +511,7 @@ __global__ void __launch_bounds__(GATHER ? kThreads + kGatherWarps * 32 : kThrea
     // bf16 chunks (2 KB) alternate between the two halves of the slab, so the next
     // chunk is packed while the previous one's TMA store is still reading
     const bool dbl = epi_double_buffered(args.epi);
+    constexpr int kSub = 2048;
     uint32_t ck = 0;
     int ab = 0;
     uint32_t aphase = 0;
@@ -536,14 +537,14 @@ __global__ void __launch_bounds__(GATHER ? kThreads + kGatherWarps * 32 : kThrea
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r0[j]);
         epi_slab_acquire(lane, dbl);  // the sub-slab's previous store has read its source
-        epi_chunk(args, &tmOut, &tmAux, slab + (dbl ? (ck & 1) * 2048 : 0), lane, row0, n0 + c, sp, v);
+        epi_chunk(args, &tmOut, &tmAux, slab + (dbl ? (ck & 1) * kSub : 0), lane, row0, n0 + c, sp, v);
         ++ck;
         // chunk c+32 .. c+63
         if (n0 + c + 32 < N) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r1[j]);
           epi_slab_acquire(lane, dbl);
-          epi_chunk(args, &tmOut, &tmAux, slab + (dbl ? (ck & 1) * 2048 : 0), lane, row0, n0 + c + 32, sp, v);
+          epi_chunk(args, &tmOut, &tmAux, slab + (dbl ? (ck & 1) * kSub : 0), lane, row0, n0 + c + 32, sp, v);
           ++ck;
         }
       }
@@ -581,9 +582,9 @@ struct Gemm2Cfg {
   static constexpr int A_BYTES = kBM * kBK * 2;        // 16 KB: this CTA's 128 rows
   static constexpr int B_BYTES = 128 * kBK * 2;        // 16 KB: this CTA's 128 columns
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = 6;
+  static constexpr int STAGES = 5;
   static constexpr int TMEM_COLS = 512;                // two 256-column accumulators
-  static constexpr int EPI_BYTES = kEpiWarps * kEpiSlab;
+  static constexpr int EPI_BYTES = kEpiWarps * 2 * kEpiSlab;  // two 4 KB slabs per epilogue warp
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
 };
 
@@ -726,9 +727,12 @@ __global__ void __launch_bounds__(GATHER ? kThreads + kGatherWarps * 32 : kThrea
     const int ew = warp - 2;
     const int q = warp & 3;
     const int half = ew >> 2;
-    uint8_t* slab = epi_smem + ew * kEpiSlab;
+    // two full slabs per warp: every epilogue (fp32, GELU's two outputs) packs chunk
+    // i+1 while chunk i's TMA store is still reading
+    uint8_t* slab = epi_smem + ew * 2 * kEpiSlab;
     const uint32_t lead_tempty0 = mapa_shared(&tempty_bar[0], 0);
-    const bool dbl = epi_double_buffered(args.epi);  // see the 1-SM epilogue
+    const bool dbl = true;
+    constexpr int kSub = kEpiSlab;
     uint32_t ck = 0;
     int ab = 0;
     uint32_t aphase = 0;
@@ -754,14 +758,14 @@ __global__ void __launch_bounds__(GATHER ? kThreads + kGatherWarps * 32 : kThrea
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r0[j]);
         epi_slab_acquire(lane, dbl);  // the sub-slab's previous store has read its source
-        epi_chunk(args, &tmOut, &tmAux, slab + (dbl ? (ck & 1) * 2048 : 0), lane, row0, n0 + c, sp, v);
+        epi_chunk(args, &tmOut, &tmAux, slab + (dbl ? (ck & 1) * kSub : 0), lane, row0, n0 + c, sp, v);
         ++ck;
         // chunk c+32 .. c+63
         if (n0 + c + 32 < N) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r1[j]);
           epi_slab_acquire(lane, dbl);
-          epi_chunk(args, &tmOut, &tmAux, slab + (dbl ? (ck & 1) * 2048 : 0), lane, row0, n0 + c + 32, sp, v);
+          epi_chunk(args, &tmOut, &tmAux, slab + (dbl ? (ck & 1) * kSub : 0), lane, row0, n0 + c + 32, sp, v);
           ++ck;
         }
       }
