@@ -15,9 +15,11 @@ void gemm(torch::Tensor a, bool a_trans, torch::Tensor b, bool b_trans, torch::T
           c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> resid, c10::optional<torch::Tensor> aux,
           double alpha, bool accumulate, int64_t force_bn, int64_t force_splits,
           c10::optional<torch::Tensor> workspace);
-void gemm_gather(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t epi, c10::optional<torch::Tensor> bias,
-                 c10::optional<torch::Tensor> resid, c10::optional<torch::Tensor> aux, std::vector<int64_t> peers,
-                 int64_t rank, int64_t woff, int64_t nflat, torch::Tensor state, int64_t site);
+torch::Tensor gemm_gather(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t epi,
+                          c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> resid,
+                          c10::optional<torch::Tensor> aux, std::vector<int64_t> peers, int64_t rank, int64_t woff,
+                          int64_t nflat, torch::Tensor state, int64_t site);
+torch::Tensor gemm_lse(torch::Tensor a, torch::Tensor b, torch::Tensor out);
 std::vector<int64_t> gemm_tiling(int64_t M, int64_t N, int64_t K);
 // layernorm.cu
 std::vector<torch::Tensor> layernorm_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor b, double eps);
@@ -30,6 +32,7 @@ torch::Tensor embed_fwd(torch::Tensor idx, torch::Tensor tok, torch::Tensor pos,
 void embed_bwd(torch::Tensor sorted_ids, torch::Tensor perm, torch::Tensor dx, torch::Tensor dtok,
                torch::Tensor dpos, int64_t B, int64_t T, bool accumulate);
 std::vector<torch::Tensor> xent_fwd(torch::Tensor logits, torch::Tensor tgt);
+std::vector<torch::Tensor> xent_from_parts(torch::Tensor part, torch::Tensor logits, torch::Tensor tgt);
 void xent_bwd(torch::Tensor logits, torch::Tensor tgt, torch::Tensor lse, torch::Tensor gscale);
 // optim.cu
 void adamw_step(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, c10::optional<torch::Tensor> p16,
@@ -108,6 +111,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_gather", &gemm_gather, py::arg("a"), py::arg("b"), py::arg("out"), py::arg("epi"),
         py::arg("bias") = py::none(), py::arg("resid") = py::none(), py::arg("aux") = py::none(), py::arg("peers"),
         py::arg("rank"), py::arg("woff"), py::arg("nflat"), py::arg("state"), py::arg("site"));
+  m.def("gemm_lse", &gemm_lse);
+  m.def("xent_from_parts", &xent_from_parts);
   m.def("gemm_tiling", &gemm_tiling);
   m.def("layernorm_fwd", &layernorm_fwd);
   m.def("layernorm_bwd", &layernorm_bwd, py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("mean"),

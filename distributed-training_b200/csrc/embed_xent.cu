@@ -359,6 +359,61 @@ std::vector<torch::Tensor> xent_fwd(torch::Tensor logits, torch::Tensor tgt) {
   return {loss, lse};
 }
 
+// Cross-entropy forward from the LM-head GEMM's softmax partials (EPI_LSE in gemm.cu):
+// part[row, p] = (max, sum exp(x - max)) over column half-tile p of the bf16 logits.
+// One warp per row merges its partials in a fixed order (lane-strided, then a fixed
+// shuffle tree), so the result is deterministic; loss_row = lse - z[target].
+__global__ void __launch_bounds__(256)
+    xent_parts_kernel(const float2* __restrict__ part, int np, const bf16* __restrict__ logits, long ld,
+                      const int64_t* __restrict__ tgt, int V, long rows, float* __restrict__ lse_out,
+                      float* __restrict__ loss_out) {
+  const long row = (long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float2* pr = part + row * np;
+  float m = -INFINITY, s = 0.f;
+  for (int p = lane; p < np; p += 32) {
+    const float2 q = pr[p];
+    online_merge(m, s, q.x, q.y);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    online_merge(m, s, m2, s2);
+  }
+  if (lane == 0) {
+    const float lse = m + __logf(s);
+    lse_out[row] = lse;
+    const int64_t t = tgt[row];
+    loss_out[row] = (t >= 0 && t < V) ? lse - bf2f(logits[row * ld + t]) : 0.f;
+  }
+}
+
+// Returns (loss scalar fp32 [1], lse fp32 [rows]) from the head GEMM's partials.
+std::vector<torch::Tensor> xent_from_parts(torch::Tensor part, torch::Tensor logits, torch::Tensor tgt) {
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1 && logits.scalar_type() == at::kBFloat16,
+              "xent_from_parts: logits");
+  TORCH_CHECK(part.dim() == 3 && part.size(2) == 2 && part.scalar_type() == at::kFloat && part.is_contiguous() &&
+                  part.size(0) == logits.size(0),
+              "xent_from_parts: partials must be [rows, np, 2] fp32");
+  TORCH_CHECK(tgt.scalar_type() == at::kLong && tgt.numel() == logits.size(0), "xent_from_parts: targets");
+  c10::cuda::CUDAGuard guard(logits.device());
+  const long rows = logits.size(0);
+  auto lse = torch::empty({rows}, logits.options().dtype(at::kFloat));
+  auto lrow = torch::empty({rows}, logits.options().dtype(at::kFloat));
+  auto loss = torch::empty({}, logits.options().dtype(at::kFloat));
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  auto tg = tgt.contiguous();
+  xent_parts_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(
+      reinterpret_cast<const float2*>(part.data_ptr<float>()), (int)part.size(1),
+      reinterpret_cast<const bf16*>(logits.data_ptr()), logits.stride(0), tg.data_ptr<int64_t>(),
+      (int)logits.size(1), rows, lse.data_ptr<float>(), lrow.data_ptr<float>());
+  mean_kernel<<<1, 1024, 0, st>>>(lrow.data_ptr<float>(), rows, loss.data_ptr<float>());
+  count_launch(2);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {loss, lse};
+}
+
 void xent_bwd(torch::Tensor logits, torch::Tensor tgt, torch::Tensor lse, torch::Tensor gscale) {
   c10::cuda::CUDAGuard guard(logits.device());
   const long rows = logits.size(0);

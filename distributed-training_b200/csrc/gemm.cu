@@ -40,6 +40,8 @@ enum GemmEpi : int {
   EPI_DGELU = 2,    // out(bf16) = acc * gelu'(aux)
   EPI_F32 = 3,      // out(f32)  = alpha*acc [+ out if accumulate]
   EPI_PARTIAL = 4,  // ws[split](f32) = acc   (split-K partial, reduced by splitk_reduce)
+  EPI_LSE = 5,      // out(bf16) = acc, plus per (row, half-tile) softmax partials (max, sum exp) of the
+                    // bf16-rounded outputs -> lse_part (the LM head fused with the cross-entropy forward)
 };
 
 // All-gather fused into the GEMM (ZeRO-1 forward): B is a weight stored in a flat bf16
@@ -76,6 +78,8 @@ struct GemmArgs {
   long ldx;
   float alpha;
   int accumulate;
+  float2* lse_part;  // EPI_LSE: [M, lse_np] (max, sum of exp(x - max)) per row and column half-tile
+  int lse_np;
 };
 
 constexpr int kBM = 128;
@@ -151,7 +155,41 @@ __device__ __forceinline__ void slab_put_f32(uint8_t* slab, int lane, const floa
 
 // Epilogues whose chunk is one 32x32 bf16 tile (2 KB) stage alternate chunks in the
 // two halves of the warp's 4 KB slab; fp32 and GELU (two outputs) chunks fill it.
-__device__ __forceinline__ bool epi_double_buffered(int epi) { return epi == EPI_BF16 || epi == EPI_DGELU; }
+__device__ __forceinline__ bool epi_double_buffered(int epi) {
+  return epi == EPI_BF16 || epi == EPI_DGELU || epi == EPI_LSE;
+}
+
+__device__ __forceinline__ float ex2_fast(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// EPI_LSE: fold 32 outputs of this lane's row (columns col..col+31, those < N) into
+// the running (max m, sum s of exp(x - m)).  x is the bf16-rounded output, the value
+// the logits tensor holds.  One exp2 per element plus two per chunk.
+__device__ __forceinline__ void lse_fold(const float* v, int col, int N, float& m, float& s) {
+  constexpr float kLog2e = 1.4426950408889634f;
+  float x[32];
+  float cm = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    x[j] = (col + j < N) ? bf2f(f2bf(v[j])) : -INFINITY;
+    cm = fmaxf(cm, x[j]);
+  }
+  if (cm == -INFINITY) return;
+  const float nb = -cm * kLog2e;
+  float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+  for (int j = 0; j < 32; j += 2) {
+    s0 += ex2_fast(fmaf(x[j], kLog2e, nb));
+    s1 += ex2_fast(fmaf(x[j + 1], kLog2e, nb));
+  }
+  const float cs = s0 + s1;
+  if (m == -INFINITY) { m = cm; s = cs; }
+  else if (cm > m) { s = s * ex2_fast((m - cm) * kLog2e) + cs; m = cm; }
+  else { s += cs * ex2_fast((cm - m) * kLog2e); }
+}
 
 // Before packing a chunk: lane 0 waits until the store that last used this (sub-)slab
 // has read it - with two halves that is every store but the most recent one.
@@ -170,6 +208,7 @@ __device__ __forceinline__ void epi_chunk(const GemmArgs& a, const CUtensorMap* 
   const int row = row0 + lane;
   const bool row_ok = row < a.M;
   switch (a.epi) {
+    case EPI_LSE:
     case EPI_BF16: {
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] *= a.alpha;
@@ -525,6 +564,7 @@ __global__ void __launch_bounds__(GATHER ? kThreads + kGatherWarps * 32 : kThrea
       const int row0 = m0 + q * 32;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * BN);
       const int c_begin = half * (BN / 2), c_end = c_begin + BN / 2;
+      float lm = -INFINITY, ls = 0.f;  // EPI_LSE running softmax statistics of this lane's row
 #pragma unroll 1
       for (int c = c_begin; c < c_end; c += 64) {
         if (n0 + c >= N) break;  // warp-uniform
@@ -538,6 +578,7 @@ __global__ void __launch_bounds__(GATHER ? kThreads + kGatherWarps * 32 : kThrea
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r0[j]);
         epi_slab_acquire(lane, dbl);  // the sub-slab's previous store has read its source
         epi_chunk(args, &tmOut, &tmAux, slab + (dbl ? (ck & 1) * kSub : 0), lane, row0, n0 + c, sp, v);
+        if (args.epi == EPI_LSE) lse_fold(v, n0 + c, N, lm, ls);
         ++ck;
         // chunk c+32 .. c+63
         if (n0 + c + 32 < N) {
@@ -545,9 +586,12 @@ __global__ void __launch_bounds__(GATHER ? kThreads + kGatherWarps * 32 : kThrea
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r1[j]);
           epi_slab_acquire(lane, dbl);
           epi_chunk(args, &tmOut, &tmAux, slab + (dbl ? (ck & 1) * kSub : 0), lane, row0, n0 + c + 32, sp, v);
+          if (args.epi == EPI_LSE) lse_fold(v, n0 + c + 32, N, lm, ls);
           ++ck;
         }
       }
+      if (args.epi == EPI_LSE && row0 + lane < M) args.lse_part[(long)(row0 + lane) * args.lse_np + ni * 2 + half] =
+          make_float2(lm, ls);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty_bar[ab]);
@@ -746,6 +790,7 @@ __global__ void __launch_bounds__(GATHER ? kThreads + kGatherWarps * 32 : kThrea
       const int row0 = m0 + q * 32;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * 256);
       const int c_begin = half * 128, c_end = c_begin + 128;
+      float lm = -INFINITY, ls = 0.f;  // EPI_LSE running softmax statistics of this lane's row
 #pragma unroll 1
       for (int c = c_begin; c < c_end; c += 64) {
         if (n0 + c >= N) break;  // warp-uniform
@@ -759,6 +804,7 @@ __global__ void __launch_bounds__(GATHER ? kThreads + kGatherWarps * 32 : kThrea
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r0[j]);
         epi_slab_acquire(lane, dbl);  // the sub-slab's previous store has read its source
         epi_chunk(args, &tmOut, &tmAux, slab + (dbl ? (ck & 1) * kSub : 0), lane, row0, n0 + c, sp, v);
+        if (args.epi == EPI_LSE) lse_fold(v, n0 + c, N, lm, ls);
         ++ck;
         // chunk c+32 .. c+63
         if (n0 + c + 32 < N) {
@@ -766,9 +812,12 @@ __global__ void __launch_bounds__(GATHER ? kThreads + kGatherWarps * 32 : kThrea
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r1[j]);
           epi_slab_acquire(lane, dbl);
           epi_chunk(args, &tmOut, &tmAux, slab + (dbl ? (ck & 1) * kSub : 0), lane, row0, n0 + c + 32, sp, v);
+          if (args.epi == EPI_LSE) lse_fold(v, n0 + c + 32, N, lm, ls);
           ++ck;
         }
       }
+      if (args.epi == EPI_LSE && row0 + lane < M) args.lse_part[(long)(row0 + lane) * args.lse_np + ni * 2 + half] =
+          make_float2(lm, ls);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(lead_tempty0 + (uint32_t)(ab * sizeof(uint64_t)));
@@ -1007,10 +1056,12 @@ static void choose_tiling(int M, int N, int K, int& bn, int& splits, bool allow_
 
 // a: stored [M,K] (a_trans=false) or [K,M] (a_trans=true); b: stored [K,N] (b_trans=false) or [N,K] (b_trans=true).
 // `gather` (forward GEMMs of ZeRO-1 only): B's peer partitions are pulled in the kernel.
+// `lse_part` (EPI_LSE only): receives the [M, np, 2] softmax partials.
 static void gemm_impl(torch::Tensor a, bool a_trans, torch::Tensor b, bool b_trans, torch::Tensor out, int64_t epi,
                       c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> resid,
                       c10::optional<torch::Tensor> aux, double alpha, bool accumulate, int64_t force_bn,
-                      int64_t force_splits, c10::optional<torch::Tensor> workspace, const GatherArgs* gather) {
+                      int64_t force_splits, c10::optional<torch::Tensor> workspace, const GatherArgs* gather,
+                      torch::Tensor* lse_part = nullptr) {
   TORCH_CHECK(a.is_cuda() && b.is_cuda() && out.is_cuda(), "gemm: CUDA tensors expected");
   TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm: bf16 operands expected");
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && out.dim() == 2, "gemm: 2-D tensors expected");
@@ -1030,7 +1081,10 @@ static void gemm_impl(torch::Tensor a, bool a_trans, torch::Tensor b, bool b_tra
               "gemm: output columns / leading dimension must be multiples of 8 and 16-byte aligned");
   const bool f32_out = (epi == EPI_F32);
   TORCH_CHECK(out.scalar_type() == (f32_out ? at::kFloat : at::kBFloat16), "gemm: wrong output dtype for epilogue");
-  TORCH_CHECK(epi >= EPI_BF16 && epi <= EPI_F32, "gemm: unknown epilogue");
+  TORCH_CHECK((epi >= EPI_BF16 && epi <= EPI_F32) || (epi == EPI_LSE && lse_part), "gemm: unknown epilogue");
+  TORCH_CHECK(epi != EPI_LSE || (!a_trans && !(bias && bias->defined()) && !(resid && resid->defined()) &&
+                                 !accumulate && alpha == 1.0),
+              "gemm: the softmax-statistics epilogue is a plain forward X @ W");
   c10::cuda::CUDAGuard guard(a.device());
   bind_device_context(a.get_device());
 
@@ -1065,8 +1119,8 @@ static void gemm_impl(torch::Tensor a, bool a_trans, torch::Tensor b, bool b_tra
   TORCH_CHECK((epi != EPI_GELU && epi != EPI_DGELU) || auxt.defined(), "gemm: gelu epilogues need aux");
 
   if (gather) {
-    TORCH_CHECK(!a_trans && !b_trans && (epi == EPI_BF16 || epi == EPI_GELU) && !accumulate,
-                "gemm_gather: forward GEMMs (X @ W, bf16 / GELU epilogue) only");
+    TORCH_CHECK(!a_trans && !b_trans && (epi == EPI_BF16 || epi == EPI_GELU || epi == EPI_LSE) && !accumulate,
+                "gemm_gather: forward GEMMs (X @ W, bf16 / GELU / softmax-statistics epilogue) only");
     TORCH_CHECK(b.is_contiguous() && (K + kBK - 1) / kBK <= kGatherMaxKb, "gemm_gather: B must be contiguous, K <= 8192");
     args.g = *gather;
     args.g.local = reinterpret_cast<bf16*>(b.data_ptr());
@@ -1111,6 +1165,13 @@ static void gemm_impl(torch::Tensor a, bool a_trans, torch::Tensor b, bool b_tra
   } else {
     run.splits = 1;
     to = make_store_map(out.data_ptr(), f32_out, M, N, out.stride(0));
+  }
+  if (epi == EPI_LSE) {
+    const int tile_n = pair2 ? 256 : bn;
+    const int np = 2 * (int)((N + tile_n - 1) / tile_n);
+    *lse_part = torch::empty({M, np, 2}, a.options().dtype(at::kFloat));
+    run.lse_part = reinterpret_cast<float2*>(lse_part->data_ptr<float>());
+    run.lse_np = np;
   }
   tx = (epi == EPI_GELU) ? make_store_map(auxt.data_ptr(), false, M, N, auxt.stride(0)) : to;
 
@@ -1164,9 +1225,11 @@ void gemm(torch::Tensor a, bool a_trans, torch::Tensor b, bool b_trans, torch::T
 // the kernel first pulls the other ranks' partitions of W into `b`, k-block by
 // k-block, while the MMAs consume the k-blocks already in place; otherwise it is the
 // plain GEMM.  All calls that share `state` must run on one stream.
-void gemm_gather(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t epi, c10::optional<torch::Tensor> bias,
-                 c10::optional<torch::Tensor> resid, c10::optional<torch::Tensor> aux, std::vector<int64_t> peers,
-                 int64_t rank, int64_t woff, int64_t nflat, torch::Tensor state, int64_t site) {
+// Returns the softmax partials for epi == EPI_LSE (see gemm_lse), else an undefined tensor.
+torch::Tensor gemm_gather(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t epi,
+                          c10::optional<torch::Tensor> bias, c10::optional<torch::Tensor> resid,
+                          c10::optional<torch::Tensor> aux, std::vector<int64_t> peers, int64_t rank, int64_t woff,
+                          int64_t nflat, torch::Tensor state, int64_t site) {
   const int W = (int)peers.size();
   TORCH_CHECK(W >= 1 && W <= kGatherRanks && rank >= 0 && rank < W, "gemm_gather: 1..8 ranks");
   TORCH_CHECK(state.is_cuda() && state.scalar_type() == at::kInt && state.is_contiguous() &&
@@ -1182,7 +1245,20 @@ void gemm_gather(torch::Tensor a, torch::Tensor b, torch::Tensor out, int64_t ep
   g.world = W;
   g.site = (int)site;
   g.state = state.data_ptr<int>();
-  gemm_impl(a, false, b, false, out, epi, bias, resid, aux, 1.0, false, 0, 0, c10::nullopt, &g);
+  torch::Tensor part;
+  gemm_impl(a, false, b, false, out, epi, bias, resid, aux, 1.0, false, 0, 0, c10::nullopt, &g, &part);
+  return part;
+}
+
+// LM head fused with the cross-entropy forward's reduction: out = X @ W (bf16) and,
+// from the same epilogue, per row and column half-tile the (max, sum exp(x - max)) of
+// the bf16-rounded outputs.  Returns the partials [M, np, 2]; xent_from_parts turns
+// them into lse and the loss without reading the logits again.
+torch::Tensor gemm_lse(torch::Tensor a, torch::Tensor b, torch::Tensor out) {
+  torch::Tensor part;
+  gemm_impl(a, false, b, false, out, EPI_LSE, c10::nullopt, c10::nullopt, c10::nullopt, 1.0, false, 0, 0,
+            c10::nullopt, nullptr, &part);
+  return part;
 }
 
 // Returns the (BN, splits) the heuristic would pick, for tests and tuning.

@@ -22,6 +22,7 @@ Two execution paths, chosen by ``GPTConfig.dtype``:
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 
 import numpy as np
@@ -199,6 +200,12 @@ class GPT(nn.Module):
 
 
 # ---------------------------------------------------------------------- fused
+# The LM head's GEMM epilogue also computes the cross-entropy's per-row softmax
+# statistics (no second pass over the logits).  DTB_HEAD_XENT=separate selects the
+# plain GEMM followed by the streaming cross-entropy kernel instead.
+HEAD_XENT_FUSED = os.environ.get("DTB_HEAD_XENT", "fused") != "separate"
+
+
 def _K():
     from ..ops import kernels
     return kernels
@@ -322,8 +329,16 @@ class _HeadLossFn(torch.autograd.Function):
         N = B * T
         x2d = x.reshape(N, C)
         h, mu, rs = K.layernorm_fwd(x2d, W(gpt.ln.w), W(gpt.ln.b))
-        logits = _lin(fp, h, gpt.head.w)
-        loss, lse = K.xent_fwd(logits, targets)
+        if HEAD_XENT_FUSED:
+            # head GEMM + the cross-entropy's softmax statistics from the same epilogue
+            g = fp.gather
+            if g is not None and id(gpt.head.w) in g.sites:
+                logits, loss, lse = K.gemm_xent(h, W(gpt.head.w), targets, g, id(gpt.head.w))
+            else:
+                logits, loss, lse = K.gemm_xent(h, W(gpt.head.w), targets)
+        else:
+            logits = _lin(fp, h, gpt.head.w)
+            loss, lse = K.xent_fwd(logits, targets)
         ctx.save_for_backward(x2d, h, mu, rs, lse, targets)
         ctx.logits = logits
         ctx.gpt = gpt

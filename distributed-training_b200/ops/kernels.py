@@ -16,6 +16,7 @@ EPI_BF16 = 0    # out(bf16) = alpha*acc [+ bias] [+ resid]
 EPI_GELU = 1    # aux(bf16) = acc + bias ; out(bf16) = gelu(aux)
 EPI_DGELU = 2   # out(bf16) = acc * gelu'(aux)
 EPI_F32 = 3     # out(f32)  = alpha*acc [+ out]
+EPI_LSE = 5     # out(bf16) = acc, plus per-row softmax partials (LM head fused with the CE forward)
 
 
 def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, *, a_trans: bool = False,
@@ -46,6 +47,23 @@ def gemm_gather(a: torch.Tensor, b: torch.Tensor, plan, key, *, epi: int = EPI_B
     out = torch.empty(a.shape[0], b.shape[1], dtype=torch.bfloat16, device=a.device)
     lib().gemm_gather(a, b, out, epi, bias, resid, aux, peers, plan.rank, woff, plan.nflat, plan.state, site)
     return out
+
+
+def gemm_xent(a: torch.Tensor, b: torch.Tensor, targets: torch.Tensor, plan=None, key=None):
+    """LM head fused with the cross-entropy forward: ``logits = a @ b`` (bf16) whose
+    epilogue also emits per-row softmax partials, then one small kernel turns them into
+    ``lse`` and the mean loss - the logits are not read again.  With ``plan``/``key``
+    the weight is all-gathered inside the GEMM (``gemm_gather``).
+    Returns (logits, loss fp32 scalar, lse fp32 [rows])."""
+    logits = torch.empty(a.shape[0], b.shape[1], dtype=torch.bfloat16, device=a.device)
+    if plan is not None:
+        site, woff, peers = plan.sites[key]
+        part = lib().gemm_gather(a, b, logits, EPI_LSE, None, None, None, peers, plan.rank, woff, plan.nflat,
+                                 plan.state, site)
+    else:
+        part = lib().gemm_lse(a, b, logits)
+    loss, lse = lib().xent_from_parts(part, logits, targets.reshape(-1))
+    return logits, loss, lse
 
 
 def layernorm_fwd(x: torch.Tensor, w16: torch.Tensor, b16: torch.Tensor, eps: float = 1e-5):

@@ -214,6 +214,29 @@ def test_cross_entropy(rows, V):
     assert _rel(zz, zf.grad) < 2e-2
 
 
+@pytest.mark.parametrize("rows,V,K_", [(16384, 50304, 768), (300, 50304, 256), (256, 512, 128), (200, 128, 64),
+                                       (1000, 1000, 192)])
+def test_head_gemm_with_fused_cross_entropy_statistics(rows, V, K_):
+    """LM head GEMM whose epilogue emits the softmax partials (gemm_xent) vs the plain
+    GEMM followed by the streaming cross-entropy kernel and an fp32 torch reference."""
+    x = torch.randn(rows, K_, device="cuda").bfloat16()
+    w = (torch.randn(K_, V, device="cuda") * (2.0 / K_ ** 0.5)).bfloat16()
+    t = torch.randint(0, V, (rows,), device="cuda")
+    logits, loss, lse = K.gemm_xent(x, w, t)
+    plain = K.gemm(x, w)
+    torch.cuda.synchronize()
+    assert torch.equal(logits, plain), "the fused epilogue must store the same logits"
+    loss2, lse2 = K.xent_fwd(plain, t)
+    ref_lse = torch.logsumexp(plain.float(), -1)
+    ref = torch.nn.functional.cross_entropy(plain.float(), t)
+    assert (lse - ref_lse).abs().max().item() < 1e-4 * max(1.0, ref_lse.abs().max().item())
+    assert (lse - lse2).abs().max().item() < 1e-4 * max(1.0, ref_lse.abs().max().item())
+    assert abs(loss.item() - ref.item()) < 1e-4 * max(1.0, abs(ref.item()))
+    # deterministic: a second call gives the same bits
+    _, loss3, lse3 = K.gemm_xent(x, w, t)
+    assert torch.equal(lse3, lse) and torch.equal(loss3, loss)
+
+
 def test_adamw_and_norm():
     n = 100003
     p = torch.randn(n, device="cuda")
