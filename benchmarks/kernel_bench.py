@@ -1,6 +1,6 @@
 """Per-kernel timings of the sm_100a kernels on the GPT-2-small training shapes.
 
-    python benchmarks/kernel_bench.py [--only gemm,gather,attn,ln,xent,adamw] [--iters 20]
+    python benchmarks/kernel_bench.py [--only gemm,gather,headxent,attn,ln,xent,adamw] [--iters 20]
 
 Each kernel is timed with CUDA events on the current stream after warm-up, with
 a synchronize on both sides and a cold L2 (see ``timeit``); the median over
@@ -150,6 +150,16 @@ def main():
             del x, w, dy, gw
     if "gather" in only:
         gather_cases(a, rep, N, C, V)
+    if "headxent" in only:
+        # LM head + cross-entropy forward: fused (softmax partials from the GEMM epilogue)
+        # against the plain GEMM followed by the streaming cross-entropy kernel
+        h = torch.randn(N, C, device=dev).bfloat16()
+        w = (torch.randn(C, V, device=dev) * 0.05).bfloat16()
+        t = torch.randint(0, V, (N,), device=dev)
+        f = 2.0 * N * C * V
+        rep("head_gemm_xent_fused", timeit(lambda: K.gemm_xent(h, w, t), a.iters), f)
+        rep("head_gemm_then_xent", timeit(lambda: K.xent_fwd(K.gemm(h, w), t), a.iters), f)
+        del h, w, t
     if "attn" in only:
         D = C // H
         qkv = torch.randn(B * T, 3 * C, device=dev).bfloat16()
