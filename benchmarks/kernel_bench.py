@@ -113,6 +113,7 @@ def main():
     ap.add_argument("--gather-world", type=int, default=2,
                     help="ranks emulated on this GPU by the 'gather' case (fused all-gather -> GEMM)")
     ap.add_argument("--gather-shapes", default="qkv,fc,out,head")
+    ap.add_argument("--head-rows", type=int, default=16384, help="token rows of the 'headxent' case")
     a = ap.parse_args()
     pk_tf, pk_bw, tag = peaks()
     only = set(a.only.split(","))
@@ -153,10 +154,11 @@ def main():
     if "headxent" in only:
         # LM head + cross-entropy forward: fused (softmax partials from the GEMM epilogue)
         # against the plain GEMM followed by the streaming cross-entropy kernel
-        h = torch.randn(N, C, device=dev).bfloat16()
+        R = a.head_rows
+        h = torch.randn(R, C, device=dev).bfloat16()
         w = (torch.randn(C, V, device=dev) * 0.05).bfloat16()
-        t = torch.randint(0, V, (N,), device=dev)
-        f = 2.0 * N * C * V
+        t = torch.randint(0, V, (R,), device=dev)
+        f = 2.0 * R * C * V
         rep("head_gemm_xent_fused", timeit(lambda: K.gemm_xent(h, w, t), a.iters), f)
         rep("head_gemm_then_xent", timeit(lambda: K.xent_fwd(K.gemm(h, w), t), a.iters), f)
         del h, w, t
