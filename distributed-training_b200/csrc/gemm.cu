@@ -166,15 +166,15 @@ __device__ __forceinline__ float ex2_fast(float x) {
 }
 
 // EPI_LSE: fold 32 outputs of this lane's row (columns col..col+31, those < N) into
-// the running (max m, sum s of exp(x - m)).  x is the bf16-rounded output, the value
-// the logits tensor holds.  One exp2 per element plus two per chunk.
+// the running (max m, sum s of exp(x - m)).  v holds the bf16-rounded outputs (epi_chunk
+// rounds them), the values the logits tensor holds.  One exp2 per element plus two per chunk.
 __device__ __forceinline__ void lse_fold(const float* v, int col, int N, float& m, float& s) {
   constexpr float kLog2e = 1.4426950408889634f;
   float x[32];
   float cm = -INFINITY;
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
-    x[j] = (col + j < N) ? bf2f(f2bf(v[j])) : -INFINITY;
+    x[j] = (col + j < N) ? v[j] : -INFINITY;
     cm = fmaxf(cm, x[j]);
   }
   if (cm == -INFINITY) return;
@@ -208,7 +208,23 @@ __device__ __forceinline__ void epi_chunk(const GemmArgs& a, const CUtensorMap* 
   const int row = row0 + lane;
   const bool row_ok = row < a.M;
   switch (a.epi) {
-    case EPI_LSE:
+    case EPI_LSE: {
+      // pack to bf16 once; v keeps the rounded values (unpacked with shifts, not
+      // conversions) for the softmax statistics folded in by the caller
+      uint4* dst = reinterpret_cast<uint4*>(slab + lane * 64);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint32_t u[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          u[e] = pack_bf16x2(v[8 * j + 2 * e], v[8 * j + 2 * e + 1]);
+          v[8 * j + 2 * e] = __uint_as_float(u[e] << 16);
+          v[8 * j + 2 * e + 1] = __uint_as_float(u[e] & 0xffff0000u);
+        }
+        dst[j] = make_uint4(u[0], u[1], u[2], u[3]);
+      }
+      break;
+    }
     case EPI_BF16: {
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] *= a.alpha;
