@@ -1,6 +1,9 @@
 """Host-side bookkeeping of the ZeRO-1 in-GEMM all-gather (no GPU needed)."""
+import torch
+
 from dtrain_b200.models.gpt import GPT, GPTConfig
-from dtrain_b200.parallel.zero import keep_intervals
+from dtrain_b200.models.params import FlatParams
+from dtrain_b200.parallel.zero import GS_GEN, GS_SITES, GatherPlan, keep_intervals
 
 
 def test_keep_intervals_is_the_complement():
@@ -31,3 +34,22 @@ def test_gemm_weights_are_the_linear_weights_and_the_rest_is_kept():
             continue
         lo, hi = offs[id(p)]
         assert any(a <= lo and hi <= b for a, b in keep)
+
+
+def test_gather_plan_sites_and_generation_bookkeeping():
+    m = GPT(GPTConfig(vocab=65, ctx=16, dim=32, heads=2, layers=1))
+    fp = FlatParams(list(m.parameters()), "cpu", with_work=False)
+    ws = m.gemm_weights()
+    bases = [1 << 20, 3 << 20]  # every rank's base address of the bf16 working copy
+    plan = GatherPlan(fp, ws, bases, rank=1)
+    assert plan.rank == 1 and plan.nflat == fp.n
+    for s, w in enumerate(ws):
+        site, off, peers = plan.sites[id(w)]
+        assert site == s and off == fp.slot(fp.index[id(w)])[0]
+        assert peers == [b + 2 * off for b in bases]  # bf16: 2 bytes per element
+    keep = [tuple(r) for r in plan.keep.tolist()]
+    assert keep == keep_intervals(fp.n, [(o, o + w.numel()) for w in ws for o in [fp.slot(fp.index[id(w)])[0]]])
+    assert plan.state.dtype == torch.int32 and plan.state.numel() == GS_SITES + len(ws)
+    plan.state[GS_GEN] = 7
+    plan.mark_gathered()
+    assert plan.state[GS_SITES:].tolist() == [7] * len(ws)
