@@ -51,6 +51,10 @@ int64_t symm_open(torch::Tensor handle);
 void symm_close(int64_t peer_ptr);
 void symm_free(int64_t ptr);
 torch::Tensor tensor_from_ptr(int64_t ptr, std::vector<int64_t> sizes, c10::ScalarType dtype, int64_t device);
+// vmm.cpp
+std::tuple<int64_t, int64_t, int64_t> vmm_alloc(int64_t nbytes);
+int64_t vmm_import(int64_t fd, int64_t size);
+void vmm_free(int64_t va);
 int64_t comm_status();
 void comm_status_clear();
 int64_t allreduce(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> bufs,
@@ -136,6 +140,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_close", &symm_close);
   m.def("symm_free", &symm_free);
   m.def("tensor_from_ptr", &tensor_from_ptr);
+  m.def("vmm_alloc", &vmm_alloc);
+  m.def("vmm_import", &vmm_import);
+  m.def("vmm_free", &vmm_free);
   m.def("comm_status", &comm_status);
   m.def("comm_status_clear", &comm_status_clear);
   m.def("allreduce", &allreduce);

@@ -1,0 +1,192 @@
+// Peer memory through the CUDA virtual-memory-management API, shared by file descriptor.
+//
+// The default peer memory of NVLinkGroup is cudaMalloc + cudaIpc handles: an IPC
+// mapping is tied to the exporting process's allocation, so a rank that dies takes
+// the memory its peers are reading with it.  Here each rank creates a physical
+// allocation with cuMemCreate (shareable as a POSIX file descriptor), maps it into its
+// own address space, and passes the descriptor to its peers (over a Unix socket, in
+// Python); a peer imports the descriptor, which holds its own reference to the
+// physical memory, and maps it too.  The memory stays valid in every process that
+// mapped it until that process unmaps it, whatever happens to the exporter.
+//
+// Driver entry points are resolved at run time through cudaGetDriverEntryPoint, so the
+// extension needs no link against libcuda.
+#include <torch/extension.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <map>
+#include <mutex>
+#include <tuple>
+
+namespace dtb {
+
+namespace {
+
+struct VmmApi {
+  CUresult (*getGranularity)(size_t*, const CUmemAllocationProp*, CUmemAllocationGranularity_flags);
+  CUresult (*create)(CUmemGenericAllocationHandle*, size_t, const CUmemAllocationProp*, unsigned long long);
+  CUresult (*exportHandle)(void*, CUmemGenericAllocationHandle, CUmemAllocationHandleType, unsigned long long);
+  CUresult (*importHandle)(CUmemGenericAllocationHandle*, void*, CUmemAllocationHandleType);
+  CUresult (*reserve)(CUdeviceptr*, size_t, size_t, CUdeviceptr, unsigned long long);
+  CUresult (*map)(CUdeviceptr, size_t, size_t, CUmemGenericAllocationHandle, unsigned long long);
+  CUresult (*setAccess)(CUdeviceptr, size_t, const CUmemAccessDesc*, size_t);
+  CUresult (*unmap)(CUdeviceptr, size_t);
+  CUresult (*addressFree)(CUdeviceptr, size_t);
+  CUresult (*release)(CUmemGenericAllocationHandle);
+};
+
+template <typename F>
+void resolve(F& fn, const char* name) {
+  void* p = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  const cudaError_t e = cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q);
+  TORCH_CHECK(e == cudaSuccess && q == cudaDriverEntryPointSuccess && p, "vmm: driver entry point ", name,
+              " unavailable");
+  fn = reinterpret_cast<F>(p);
+}
+
+const VmmApi& api() {
+  static VmmApi a;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    resolve(a.getGranularity, "cuMemGetAllocationGranularity");
+    resolve(a.create, "cuMemCreate");
+    resolve(a.exportHandle, "cuMemExportToShareableHandle");
+    resolve(a.importHandle, "cuMemImportFromShareableHandle");
+    resolve(a.reserve, "cuMemAddressReserve");
+    resolve(a.map, "cuMemMap");
+    resolve(a.setAccess, "cuMemSetAccess");
+    resolve(a.unmap, "cuMemUnmap");
+    resolve(a.addressFree, "cuMemAddressFree");
+    resolve(a.release, "cuMemRelease");
+  });
+  return a;
+}
+
+#define DTB_CU(call, what)                                                      \
+  do {                                                                          \
+    const CUresult r_ = (call);                                                 \
+    TORCH_CHECK(r_ == CUDA_SUCCESS, "vmm: ", what, " failed with code ", (int)r_); \
+  } while (0)
+
+CUmemAllocationProp device_prop(int dev) {
+  CUmemAllocationProp prop = {};
+  prop.type = CU_MEM_ALLOCATION_TYPE_PINNED;
+  prop.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
+  prop.location.id = dev;
+  prop.requestedHandleTypes = CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR;
+  return prop;
+}
+
+struct Mapping {
+  CUmemGenericAllocationHandle handle;
+  size_t size;
+};
+std::mutex g_mu;
+std::map<int64_t, Mapping> g_maps;  // mapped base address -> handle and size
+
+// Reserve an address range for `handle` and map it read/write for device `dev`.
+int64_t map_handle(CUmemGenericAllocationHandle h, size_t size, size_t gran, int dev) {
+  const VmmApi& A = api();
+  CUdeviceptr va = 0;
+  DTB_CU(A.reserve(&va, size, gran, 0, 0), "cuMemAddressReserve");
+  CUresult r = A.map(va, size, 0, h, 0);
+  if (r != CUDA_SUCCESS) {
+    A.addressFree(va, size);
+    TORCH_CHECK(false, "vmm: cuMemMap failed with code ", (int)r);
+  }
+  CUmemAccessDesc acc = {};
+  acc.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
+  acc.location.id = dev;
+  acc.flags = CU_MEM_ACCESS_FLAGS_PROT_READWRITE;
+  r = A.setAccess(va, size, &acc, 1);
+  if (r != CUDA_SUCCESS) {
+    A.unmap(va, size);
+    A.addressFree(va, size);
+    TORCH_CHECK(false, "vmm: cuMemSetAccess failed with code ", (int)r);
+  }
+  std::lock_guard<std::mutex> g(g_mu);
+  g_maps[(int64_t)va] = {h, size};
+  return (int64_t)va;
+}
+
+size_t granularity(int dev) {
+  const CUmemAllocationProp prop = device_prop(dev);
+  size_t g = 0;
+  DTB_CU(api().getGranularity(&g, &prop, CU_MEM_ALLOC_GRANULARITY_RECOMMENDED), "cuMemGetAllocationGranularity");
+  return g ? g : ((size_t)2 << 20);
+}
+
+}  // namespace
+
+// Zero-filled device memory of at least `nbytes` on the current device, exportable as a
+// file descriptor.  Returns (address, descriptor, mapped size).  The caller owns the
+// descriptor (close it once every peer has received it).
+std::tuple<int64_t, int64_t, int64_t> vmm_alloc(int64_t nbytes) {
+  TORCH_CHECK(nbytes > 0, "vmm_alloc: size must be positive");
+  int dev = 0;
+  C10_CUDA_CHECK(cudaGetDevice(&dev));
+  cudaFree(nullptr);  // make sure the primary context exists and is current
+  const VmmApi& A = api();
+  const size_t gran = granularity(dev);
+  const size_t size = ((size_t)nbytes + gran - 1) / gran * gran;
+  const CUmemAllocationProp prop = device_prop(dev);
+  CUmemGenericAllocationHandle h;
+  DTB_CU(A.create(&h, size, &prop, 0), "cuMemCreate");
+  int64_t va = 0;
+  try {
+    va = map_handle(h, size, gran, dev);
+  } catch (...) {
+    A.release(h);
+    throw;
+  }
+  C10_CUDA_CHECK(cudaMemset(reinterpret_cast<void*>(va), 0, size));
+  C10_CUDA_CHECK(cudaDeviceSynchronize());
+  int fd = -1;
+  DTB_CU(A.exportHandle(&fd, h, CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR, 0), "cuMemExportToShareableHandle");
+  return {va, (int64_t)fd, (int64_t)size};
+}
+
+// Map a peer's allocation, received as a file descriptor, for the current device.  The
+// descriptor may be closed after this returns.  Returns the local address.
+int64_t vmm_import(int64_t fd, int64_t size) {
+  TORCH_CHECK(fd >= 0 && size > 0, "vmm_import: bad descriptor or size");
+  int dev = 0;
+  C10_CUDA_CHECK(cudaGetDevice(&dev));
+  cudaFree(nullptr);
+  const VmmApi& A = api();
+  const size_t gran = granularity(dev);
+  TORCH_CHECK((size_t)size % gran == 0, "vmm_import: size is not a multiple of the allocation granularity");
+  CUmemGenericAllocationHandle h;
+  DTB_CU(A.importHandle(&h, reinterpret_cast<void*>((uintptr_t)fd), CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR),
+         "cuMemImportFromShareableHandle");
+  try {
+    return map_handle(h, (size_t)size, gran, dev);
+  } catch (...) {
+    A.release(h);
+    throw;
+  }
+}
+
+// Unmap an address returned by vmm_alloc / vmm_import and drop this process's
+// reference to the physical memory (it is freed when the last process lets go).
+void vmm_free(int64_t va) {
+  Mapping m;
+  {
+    std::lock_guard<std::mutex> g(g_mu);
+    auto it = g_maps.find(va);
+    TORCH_CHECK(it != g_maps.end(), "vmm_free: unknown address");
+    m = it->second;
+    g_maps.erase(it);
+  }
+  C10_CUDA_CHECK(cudaDeviceSynchronize());
+  const VmmApi& A = api();
+  A.unmap((CUdeviceptr)va, m.size);
+  A.addressFree((CUdeviceptr)va, m.size);
+  A.release(m.handle);
+}
+
+}  // namespace dtb

@@ -22,7 +22,8 @@ SRC_DIR = PKG_DIR / "csrc"
 BUILD_DIR = PKG_DIR / "_build"
 NAME = "dtb_C"
 
-SOURCES = ["bindings.cpp", "gemm.cu", "layernorm.cu", "embed_xent.cu", "optim.cu", "attention.cu", "attention_tc.cu", "comm.cu"]
+SOURCES = ["bindings.cpp", "gemm.cu", "layernorm.cu", "embed_xent.cu", "optim.cu", "attention.cu", "attention_tc.cu", "comm.cu",
+           "vmm.cpp"]
 
 CUDA_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

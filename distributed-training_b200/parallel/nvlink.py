@@ -6,7 +6,11 @@ Same API as the host ``ProcessGroup`` (dtrain/comm.py:241-432): ``allreduce``,
 
 Memory model.  ``alloc(numel, dtype)`` is a collective: every rank allocates a
 buffer of the same size (cudaMalloc), exports an IPC handle, publishes it through
-the bootstrap ``exchange`` function and opens its peers' handles.  Collectives on
+the bootstrap ``exchange`` function and opens its peers' handles.  With
+``memory="vmm"`` (or ``DTB_PEER_MEMORY=vmm``) the buffer is a CUDA VMM allocation
+instead, exported as a file descriptor and passed to the peers over Unix sockets
+(``FdExchange``); each peer's import holds its own reference to the physical
+memory, so a rank that dies does not unmap memory that the others still read.  Collectives on
 tensors that live inside such a buffer run in place, reading and writing peer
 memory directly from the kernel (``csrc/comm.cu``); other CUDA tensors are staged
 through a symmetric scratch buffer.  DDP and ZeRO allocate their flat gradient,
@@ -23,6 +27,9 @@ non-zero status into ``CommError``.
 from __future__ import annotations
 
 import os
+import socket
+import struct
+import uuid
 
 import torch
 
@@ -40,25 +47,116 @@ _SIG_BYTES = 8192
 _ONESHOT_MAX_BYTES = 0
 
 
+class FdExchange:
+    """All-gather of file descriptors between the ranks of one node.
+
+    Each rank listens on an abstract Unix socket whose name goes through the bootstrap
+    ``exchange`` once.  ``all_gather(fd, size)`` connects to every peer and sends
+    ``(rank, tag, size)`` with the descriptor attached (SCM_RIGHTS), then accepts one
+    connection per peer.  Calls are collective and numbered; a message that belongs to
+    a later call (a fast peer already on the next allocation) is kept until then.
+    """
+
+    def __init__(self, rank: int, world: int, exchange, timeout: float = 60.0):
+        self.rank, self.world, self.timeout = int(rank), int(world), float(timeout)
+        self.name = f"\0dtb-fd-{uuid.uuid4().hex}-{self.rank}"
+        self.sock = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
+        self.sock.bind(self.name)
+        self.sock.listen(max(16, 2 * self.world))
+        self.sock.settimeout(self.timeout)
+        self.names = [n.decode() for n in exchange("fdx/sock", self.name.encode())]
+        self.calls = 0
+        self.pending: dict[tuple[int, int], tuple[int, int]] = {}
+
+    def all_gather(self, fd: int, size: int) -> list[tuple[int, int] | None]:
+        """Returns, per rank, (received descriptor, size) - None at this rank's index.
+        The caller owns the received descriptors."""
+        tag = self.calls
+        self.calls += 1
+        hdr = struct.pack("<iiq", self.rank, tag, int(size))
+        for p in range(self.world):
+            if p == self.rank:
+                continue
+            with socket.socket(socket.AF_UNIX, socket.SOCK_STREAM) as c:
+                c.settimeout(self.timeout)
+                c.connect(self.names[p])
+                socket.send_fds(c, [hdr], [int(fd)])
+        out: list[tuple[int, int] | None] = [None] * self.world
+        need = {p for p in range(self.world) if p != self.rank}
+        for p in list(need):
+            if (tag, p) in self.pending:
+                out[p] = self.pending.pop((tag, p))
+                need.discard(p)
+        while need:
+            try:
+                conn, _ = self.sock.accept()
+            except socket.timeout as e:
+                raise CommError(f"descriptor exchange: no message from ranks {sorted(need)}") from e
+            with conn:
+                conn.settimeout(self.timeout)
+                msg, fds, _, _ = socket.recv_fds(conn, struct.calcsize("<iiq"), 1)
+            if len(msg) != struct.calcsize("<iiq") or len(fds) != 1:
+                raise CommError("descriptor exchange: malformed message")
+            r, t, sz = struct.unpack("<iiq", msg)
+            if t == tag and r in need:
+                out[r] = (fds[0], sz)
+                need.discard(r)
+            elif t > tag:
+                self.pending[(t, r)] = (fds[0], sz)
+            else:
+                os.close(fds[0])
+                raise CommError(f"descriptor exchange: rank {r} sent call {t} during call {tag}")
+        return out
+
+    def close(self):
+        self.sock.close()
+        for fd, _ in self.pending.values():
+            os.close(fd)
+        self.pending.clear()
+
+
 class SymmetricBuffer:
     """One peer-mapped allocation: a local tensor view plus every rank's base pointer."""
 
     def __init__(self, group: "NVLinkGroup", nbytes: int):
         C = lib()
         self.nbytes = int(nbytes)
-        ptr, handle = C.symm_alloc(max(self.nbytes, 256))
-        self.ptr = int(ptr)
-        handles = group._exchange(f"symm/{group._nalloc}", bytes(handle.numpy().tobytes()))
-        group._nalloc += 1
+        self.vmm = group.memory == "vmm"
         self.ptrs = []
         self._opened = []
-        for r, h in enumerate(handles):
-            if r == group.rank:
-                self.ptrs.append(self.ptr)
-            else:
-                p = int(C.symm_open(torch.frombuffer(bytearray(h), dtype=torch.uint8)))
+        if self.vmm:
+            ptr, fd, size = C.vmm_alloc(max(self.nbytes, 256))
+            self.ptr = int(ptr)
+            try:
+                got = group._fdx.all_gather(fd, size)
+            finally:
+                os.close(fd)
+            group._nalloc += 1
+            for r, g in enumerate(got):
+                if r == group.rank:
+                    self.ptrs.append(self.ptr)
+                    continue
+                pfd, psize = g
+                try:
+                    if psize != size:
+                        raise CommError(f"vmm: rank {r} mapped {psize} bytes, this rank {size}")
+                    p = int(C.vmm_import(pfd, psize))
+                finally:
+                    os.close(pfd)
                 self.ptrs.append(p)
                 self._opened.append(p)
+        else:
+            ptr, handle = C.symm_alloc(max(self.nbytes, 256))
+            self.ptr = int(ptr)
+            handles = group._exchange(f"symm/{group._nalloc}", bytes(handle.numpy().tobytes()))
+            group._nalloc += 1
+            for r, h in enumerate(handles):
+                if r == group.rank:
+                    self.ptrs.append(self.ptr)
+                else:
+                    p = int(C.symm_open(torch.frombuffer(bytearray(h), dtype=torch.uint8)))
+                    self.ptrs.append(p)
+                    self._opened.append(p)
         self.device = group.device
 
     def tensor(self, numel: int, dtype: torch.dtype, byte_offset: int = 0) -> torch.Tensor:
@@ -76,10 +174,16 @@ class SymmetricBuffer:
     def free(self):
         C = lib()
         for p in self._opened:
-            C.symm_close(p)
+            if self.vmm:
+                C.vmm_free(p)
+            else:
+                C.symm_close(p)
         self._opened = []
         if self.ptr:
-            C.symm_free(self.ptr)
+            if self.vmm:
+                C.vmm_free(self.ptr)
+            else:
+                C.symm_free(self.ptr)
             self.ptr = 0
 
 
@@ -105,13 +209,15 @@ class NVLinkGroup:
     backend = "nvlink"
 
     def __init__(self, rank: int, world: int, device, exchange, timeout: float = 60.0, blocks: int = 0,
-                 comm_priority: int = 0):
+                 comm_priority: int = 0, memory: str | None = None):
         """``exchange(key, payload: bytes) -> list[bytes]`` is the bootstrap all-gather
         (over the rendezvous store or torch.distributed); it is used only at set-up.
         ``blocks`` caps the CTAs of one collective kernel (0: sized by the message);
         ``comm_priority`` is the CUDA priority of the stream that runs the asynchronous
         collectives (lower is more urgent: -1 lets their CTAs take SMs ahead of queued
-        compute work)."""
+        compute work); ``memory`` is "ipc" (cudaMalloc + IPC handles, the default) or
+        "vmm" (CUDA VMM allocations shared by file descriptor); the environment
+        variable DTB_PEER_MEMORY sets the default."""
         if world > int(lib().comm_max_ranks()):
             raise ValueError(f"NVLinkGroup supports up to {lib().comm_max_ranks()} ranks per node")
         self.rank, self.world = int(rank), int(world)
@@ -119,6 +225,10 @@ class NVLinkGroup:
         self.blocks = int(blocks)
         self._exchange_fn = exchange
         self._nalloc = 0
+        self.memory = (memory or os.environ.get("DTB_PEER_MEMORY", "ipc")).lower()
+        if self.memory not in ("ipc", "vmm"):
+            raise ValueError(f"unknown peer memory kind {self.memory!r} (ipc or vmm)")
+        self._fdx = FdExchange(self.rank, self.world, exchange, timeout) if self.memory == "vmm" else None
         self.seq = 0            # collectives issued
         self.buffers: list[SymmetricBuffer] = []
         self._eng = None
@@ -335,6 +445,9 @@ class NVLinkGroup:
         self.buffers = []
         if self._eng is not None:
             self._eng.forget_buffers()
+        if self._fdx is not None:
+            self._fdx.close()
+            self._fdx = None
 
 
 def store_exchange(store, rank: int, world: int, prefix: str = ""):
