@@ -49,13 +49,15 @@ def main():
     ap.add_argument("--out", default=None)
     ap.add_argument("--max-mb", type=int, default=1024)
     ap.add_argument("--blocks", type=int, default=0, help="CTAs per collective kernel (0 = size-based default)")
+    ap.add_argument("--memory", choices=["ipc", "vmm"], default="ipc",
+                    help="peer memory: cudaMalloc + IPC handles, or CUDA VMM allocations shared by file descriptor")
     a = ap.parse_args()
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
-    pg = NVLinkGroup(rank, world, dev, torch_exchange(), timeout=60.0, blocks=a.blocks)
+    pg = NVLinkGroup(rank, world, dev, torch_exchange(), timeout=60.0, blocks=a.blocks, memory=a.memory)
     maxb = a.max_mb << 20
     big = {dt: pg.alloc(maxb // torch.tensor([], dtype=dt).element_size(), dt) for dt in (torch.float32, torch.bfloat16)}
     ref = {dt: torch.empty(maxb // torch.tensor([], dtype=dt).element_size(), dtype=dt, device=dev)
