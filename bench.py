@@ -64,23 +64,36 @@ def _env_rank():
 
 
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks / throttle reasons while the timed region runs."""
+    """nvidia-smi sampling of SM clocks / throttle reasons every 50 ms.  Started before
+    the warm-up (nvidia-smi needs a moment to start); ``window()`` brackets the timed
+    region and only the samples whose timestamps fall inside it are summarised."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
+        self.t0 = self.t1 = None
 
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+
+    def window(self, t0: float, t1: float):
+        self.t0, self.t1 = t0, t1
+
+    @staticmethod
+    def _ts(field: str):
+        try:
+            return datetime.datetime.strptime(field.strip(), "%Y/%m/%d %H:%M:%S.%f").timestamp()
+        except ValueError:
+            return None
 
     def stop(self) -> dict:
         if self.proc is None:
@@ -91,15 +104,21 @@ class ClockSampler:
         except subprocess.TimeoutExpired:
             self.proc.kill()
             out, _ = self.proc.communicate()
-        rows = [r for r in csv.reader(io.StringIO(out)) if len(r) >= 9]
+        rows = [r for r in csv.reader(io.StringIO(out)) if len(r) >= 10]
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        sm = [float(r[1]) for r in rows]
-        smax = float(rows[0][2])
+        where = "whole run"
+        if self.t0 is not None:
+            inside = [r for r in rows if (t := self._ts(r[0])) is not None and self.t0 <= t <= self.t1]
+            if inside:
+                rows, where = inside, "timed region"
+        sm = [float(r[2]) for r in rows]
+        smax = float(rows[0][3])
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.strip().lower() == "active"})
+        reasons = sorted({n for r in rows for n, v in zip(names, r[6:10]) if v.strip().lower() == "active"})
+        pw = [float(r[4]) for r in rows if r[4].strip() not in ("", "[N/A]")]
         return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": smax, "reasons": reasons, "samples": len(rows),
-                "power_w_max": max(float(r[3]) for r in rows if r[3].strip() not in ("", "[N/A]"))}
+                "samples_from": where, "power_w_max": max(pw) if pw else None}
 
 
 def _timed(fn, steps: int, world: int):
@@ -159,17 +178,21 @@ def run_ours(a, rank, world, local):
     def device_step(i):  # inputs already resident: the kernel-side number
         tr.step([[mb] for mb in dev_batches[i % nb]], return_loss=False)
 
+    sampler = ClockSampler(local) if local == 0 else None
+    if sampler:
+        sampler.start()
     for i in range(a.warmup):
         device_step(i)
     torch.cuda.synchronize()
     pg.check()
-    sampler = ClockSampler(local) if local == 0 else None
-    if sampler:
-        sampler.start()
     l0, r0 = K.launch_count(), tr.graph_replays
+    t0 = time.time()
     ms = _timed(lambda i: device_step(a.warmup + i), a.steps, world)
+    t1 = time.time()
     # eager launches counted on the host, plus the kernels each graph replay runs
     launches = K.launch_count() - l0 + (tr.graph_replays - r0) * tr.graph_launches
+    if sampler:
+        sampler.window(t0, t1)
     clocks = sampler.stop() if sampler else None
     pg.check()
 
@@ -267,12 +290,16 @@ def run_reference(a, rank, world, local):
         opt.step()
         return float(total.item()) if read_loss else None
 
-    for i in range(a.warmup):
-        step(dev_tokens[i], False)
     sampler = ClockSampler(local) if local == 0 else None
     if sampler:
         sampler.start()
+    for i in range(a.warmup):
+        step(dev_tokens[i], False)
+    t0 = time.time()
     ms = _timed(lambda i: step(dev_tokens[a.warmup + i], False), a.steps, world)
+    t1 = time.time()
+    if sampler:
+        sampler.window(t0, t1)
     clocks = sampler.stop() if sampler else None
     ms_e2e = _timed(lambda i: step([p.to(dev, non_blocking=True) for p in pinned[a.warmup + i]], True),
                     a.steps, world)
