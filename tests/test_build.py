@@ -21,3 +21,10 @@ def test_shared_libstdcxx_link_input_is_found():
     import torch  # noqa: F401  (loads the C++ runtime into this process)
     inputs = _ext._shared_libstdcxx()
     assert inputs and ("libstdc++.so" in os.path.basename(inputs[0]) or inputs[0].startswith("-l:"))
+
+
+def test_every_native_source_is_built():
+    """build() compiles every .cu / .cpp file of csrc/ (a new kernel file must not be left out)."""
+    on_disk = sorted(f for f in os.listdir(_ext.SRC_DIR) if f.endswith((".cu", ".cpp")))
+    assert sorted(_ext.SOURCES) == on_disk
+    assert "arch=compute_100a,code=sm_100a" in " ".join(_ext.CUDA_FLAGS)
