@@ -34,6 +34,9 @@ from .utils import checkpoint
 from .utils.data import CharData, SyntheticData, load_text, lr_at, rank_batch
 
 
+_PRECISION = {"fp64": "float64", "fp32": "float32", "bf16": "bfloat16"}
+
+
 def parse(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--mode", choices=["single", "ddp", "zero"], default="single")
@@ -45,6 +48,8 @@ def parse(argv=None):
     ap.add_argument("--heads", type=int, default=4)
     ap.add_argument("--layers", type=int, default=4)
     ap.add_argument("--dtype", default="float32", help="float64 | float32 | bfloat16 (bf16 compute, fp32 masters)")
+    ap.add_argument("--precision", choices=sorted(_PRECISION), default=None,
+                    help="short form of --dtype: fp64 | fp32 | bf16")
     ap.add_argument("--lr", type=float, default=1e-3)
     ap.add_argument("--warmup", type=int, default=0, help="linear warm-up steps, then cosine decay to lr/10")
     ap.add_argument("--wd", type=float, default=0.1)
@@ -72,7 +77,10 @@ def parse(argv=None):
     ap.add_argument("--fail-rank", type=int, default=1)
     ap.add_argument("--log", default=None)
     ap.add_argument("--save-params", default=None, help="write final parameters (.npz) from rank 0")
-    return ap.parse_args(argv)
+    a = ap.parse_args(argv)
+    if a.precision is not None:
+        a.dtype = _PRECISION[a.precision]
+    return a
 
 
 def _default_device(a) -> torch.device:
