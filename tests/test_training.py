@@ -160,3 +160,10 @@ def test_checkpoints_interchange_with_the_reference(tmp_path, corpus, mode):
                            extra=["--steps", "6", "--ckpt-dir", str(ck2), "--resume"])
     assert "resumed from step 3" in r.stderr
     assert_close(res_ours, full, 1e-12)
+
+
+def test_precision_flag_is_a_short_form_of_dtype():
+    from dtrain_b200 import train as T
+    assert T.parse(["--precision", "bf16"]).dtype == "bfloat16"
+    assert T.parse(["--precision", "fp64"]).dtype == "float64"
+    assert T.parse(["--dtype", "float32"]).dtype == "float32"

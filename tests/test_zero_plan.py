@@ -53,10 +53,3 @@ def test_gather_plan_sites_and_generation_bookkeeping():
     plan.state[GS_GEN] = 7
     plan.mark_gathered()
     assert plan.state[GS_SITES:].tolist() == [7] * len(ws)
-
-
-def test_precision_flag_is_a_short_form_of_dtype():
-    from dtrain_b200 import train as T
-    assert T.parse(["--precision", "bf16"]).dtype == "bfloat16"
-    assert T.parse(["--precision", "fp64"]).dtype == "float64"
-    assert T.parse(["--dtype", "float32"]).dtype == "float32"
