@@ -5,6 +5,9 @@ collectives:
 
     python benchmarks/allreduce_bench.py --world 4 --out results.json
 
+``--impl reference`` (or ``both``) times the reference's own host ProcessGroup
+from its installed copy in baseline/_ref on the same machine.
+
 Starts ``--world`` processes on this machine (rendezvous store + TCP mesh over
 loopback), then times the ``ring`` and ``direct`` all-reduce of float32 zeros
 from 1 KiB to 64 MiB: the median of the timed calls after three warm-ups,
@@ -34,9 +37,15 @@ def _reps(nbytes: int) -> int:
     return max(5, min(200, (64 << 20) // max(nbytes, 1) // 4))
 
 
-def _rank_main(rank: int, world: int, addr: str, algos, q):
-    from dtrain_b200.parallel.comm import ProcessGroup
+def _rank_main(rank: int, world: int, addr: str, algos, q, impl: str = "ours"):
+    if impl == "reference":
+        # the reference's own host ProcessGroup, from its installed copy
+        sys.path.insert(0, os.path.join(ROOT, "baseline", "_ref"))
+        from dtrain.comm import ProcessGroup
+    else:
+        from dtrain_b200.parallel.comm import ProcessGroup
     pg = ProcessGroup(rank, world, addr, timeout=120)
+    tag = "reference" if impl == "reference" else "dtrain_b200"
     rows = []
     for algo in algos:
         for nbytes in SIZES:
@@ -50,19 +59,19 @@ def _rank_main(rank: int, world: int, addr: str, algos, q):
                 pg.allreduce(x, algo)
                 ts.append(time.perf_counter() - t0)
             sec = float(np.median(ts))
-            rows.append({"impl": f"dtrain-{algo}", "world": world, "bytes": nbytes, "seconds": sec,
+            rows.append({"impl": f"{tag}-{algo}", "world": world, "bytes": nbytes, "seconds": sec,
                          "latency_us": sec * 1e6, "bus_GBps": 2 * (world - 1) / world * nbytes / sec / 1e9})
     pg.close()
     if rank == 0:
         q.put(rows)
 
 
-def run(world: int, algos=("ring", "direct")) -> list:
+def run(world: int, algos=("ring", "direct"), impl: str = "ours") -> list:
     from dtrain_b200.utils.store import StoreServer
     srv = StoreServer()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank_main, args=(r, world, srv.address, algos, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, srv.address, algos, q, impl)) for r in range(world)]
     for p in procs:
         p.start()
     try:
@@ -81,9 +90,12 @@ def main(argv=None):
     ap.add_argument("--world", type=int, default=4)
     ap.add_argument("--algos", default="ring,direct")
     ap.add_argument("--out", default=None)
+    ap.add_argument("--impl", choices=["ours", "reference", "both"], default="ours",
+                    help="this stack's host ProcessGroup, the reference's (baseline/_ref), or both in turn")
     a = ap.parse_args(argv)
     os.environ.setdefault("OMP_NUM_THREADS", "1")
-    rows = run(a.world, tuple(a.algos.split(",")))
+    impls = ["ours", "reference"] if a.impl == "both" else [a.impl]
+    rows = [r for impl in impls for r in run(a.world, tuple(a.algos.split(",")), impl)]
     for r in rows:
         print(json.dumps(r))
     if a.out:
