@@ -71,6 +71,9 @@ def parse(argv=None):
                          "per-kernel host launch cost; the gradient sync and the optimizer run eagerly)")
     ap.add_argument("--ckpt-dir", default=None)
     ap.add_argument("--ckpt-every", type=int, default=0)
+    ap.add_argument("--async-ckpt", action="store_true",
+                    help="write checkpoint shards in a background thread; each checkpoint is committed "
+                         "(barrier, manifest, LATEST) at the next checkpoint or at the end of the run")
     ap.add_argument("--resume", action="store_true", help="resume from the latest checkpoint if any")
     ap.add_argument("--stop-after", type=int, default=-1, help="stop cleanly after this many steps (preemption)")
     ap.add_argument("--fail-at-step", type=int, default=-1, help="fault injection: crash at this step")
@@ -434,6 +437,7 @@ def main(argv=None):
     log = open(a.log, "a") if (a.log and rank == 0) else None
     restarts = int(os.environ.get("DTRAIN_RESTART_COUNT", "0"))
     tokens_per_step = a.batch * a.ctx * a.accum * max(world, a.emulate_world)
+    saver = checkpoint.AsyncSaver() if (a.async_ckpt and a.ckpt_dir and a.ckpt_every) else None
     vworlds = a.emulate_world if a.mode == "single" else 1
     # GPU jobs that log also record the device time of each step (every rank takes
     # part in the max, so the decision depends only on the shared flags)
@@ -476,9 +480,15 @@ def main(argv=None):
             log.write(json.dumps(rec) + "\n")
             log.flush()
         if a.ckpt_dir and a.ckpt_every and (step + 1) % a.ckpt_every == 0:
-            checkpoint.save(a.ckpt_dir, step + 1, rank, world, tr.state(), tr.barrier)
+            if saver is not None:
+                saver.commit(tr.barrier)
+                saver.start(a.ckpt_dir, step + 1, rank, world, tr.state())
+            else:
+                checkpoint.save(a.ckpt_dir, step + 1, rank, world, tr.state(), tr.barrier)
         if a.stop_after >= 0 and step + 1 >= a.stop_after:
             break
+    if saver is not None:
+        saver.commit(tr.barrier)
 
     if a.save_params:
         if tr.zero is not None:

@@ -69,13 +69,20 @@ def _to_numpy(v):
     return np.asarray(v)
 
 
-def save(root: str, step: int, rank: int, world: int, state: dict, barrier) -> str:
-    name = f"step_{step:06d}"
-    d = os.path.join(root, name)
+def _write_shard(root: str, step: int, rank: int, host_state: dict) -> str:
+    d = os.path.join(root, f"step_{step:06d}")
     os.makedirs(d, exist_ok=True)
     payload = io.BytesIO()
-    np.savez(payload, **{k: _to_numpy(v) for k, v in state.items()})
+    np.savez(payload, **host_state)
     _write_atomic(os.path.join(d, f"rank{rank}.npz"), payload.getvalue())
+    return d
+
+
+def _commit(root: str, step: int, rank: int, world: int, barrier) -> str:
+    """Every rank's shard is on disk once all ranks reach the first barrier; rank 0 then
+    hashes the shards into the manifest and moves LATEST (dtrain/checkpoint.py:52-68)."""
+    name = f"step_{step:06d}"
+    d = os.path.join(root, name)
     barrier()
     if rank == 0:
         manifest = {"step": step, "world": world,
@@ -86,6 +93,57 @@ def save(root: str, step: int, rank: int, world: int, state: dict, barrier) -> s
         _sync_dir(root)
     barrier()
     return d
+
+
+def save(root: str, step: int, rank: int, world: int, state: dict, barrier) -> str:
+    _write_shard(root, step, rank, {k: _to_numpy(v) for k, v in state.items()})
+    return _commit(root, step, rank, world, barrier)
+
+
+class AsyncSaver:
+    """Checkpoints whose shard files are written by a background thread.
+
+    ``start`` copies the state to host memory on the calling thread (the training
+    state may change right after) and writes ``rank{r}.npz`` in the background while
+    training continues.  ``commit`` - called by the training thread at the next
+    checkpoint and at the end of the run, in the same order on every rank - waits for
+    the file and runs the same barrier / manifest / LATEST protocol as ``save``, so
+    the collectives stay on the training thread.  A checkpoint is visible to
+    ``latest``/``load`` only once committed: a crash before the commit resumes from
+    the previous one.
+    """
+
+    def __init__(self):
+        self._thread = None
+        self._pending = None
+        self._error: BaseException | None = None
+
+    def start(self, root: str, step: int, rank: int, world: int, state: dict):
+        import threading
+        if self._pending is not None:
+            raise RuntimeError("commit the previous checkpoint first")
+        host = {k: _to_numpy(v) for k, v in state.items()}
+        self._error = None
+
+        def work():
+            try:
+                _write_shard(root, step, rank, host)
+            except BaseException as e:  # noqa: BLE001 - re-raised by commit()
+                self._error = e
+
+        self._pending = (root, step, rank, world)
+        self._thread = threading.Thread(target=work, name="dtb-ckpt-writer", daemon=True)
+        self._thread.start()
+
+    def commit(self, barrier) -> str | None:
+        if self._pending is None:
+            return None
+        self._thread.join()
+        root, step, rank, world = self._pending
+        self._pending = self._thread = None
+        if self._error is not None:
+            raise self._error
+        return _commit(root, step, rank, world, barrier)
 
 
 def latest(root: str) -> str | None:

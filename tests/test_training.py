@@ -167,3 +167,25 @@ def test_precision_flag_is_a_short_form_of_dtype():
     assert T.parse(["--precision", "bf16"]).dtype == "bfloat16"
     assert T.parse(["--precision", "fp64"]).dtype == "float64"
     assert T.parse(["--dtype", "float32"]).dtype == "float32"
+
+
+@pytest.mark.parametrize("mode", ["ddp", "zero"])
+def test_async_checkpoints_match_synchronous_ones(tmp_path, corpus, mode):
+    """--async-ckpt writes the same shard files (same bytes) and commits them in the same
+    layout; resuming from one reproduces the uninterrupted run exactly."""
+    full, _, _ = train(tmp_path, f"{mode}-full", corpus, mode, 2, extra=["--steps", "8"])
+    sync_ck, async_ck = tmp_path / f"sync-{mode}", tmp_path / f"async-{mode}"
+    train(tmp_path, f"{mode}-sync", corpus, mode, 2,
+          extra=["--steps", "8", "--stop-after", "4", "--ckpt-dir", str(sync_ck), "--ckpt-every", "2"])
+    train(tmp_path, f"{mode}-async", corpus, mode, 2,
+          extra=["--steps", "8", "--stop-after", "4", "--ckpt-dir", str(async_ck), "--ckpt-every", "2",
+                 "--async-ckpt"])
+    for step in ("step_000002", "step_000004"):
+        for f in ("rank0.npz", "rank1.npz", "manifest.json"):
+            assert (sync_ck / step / f).read_bytes() == (async_ck / step / f).read_bytes(), (step, f)
+    assert (async_ck / "LATEST").read_text() == "step_000004"
+    resumed, _, r = train(tmp_path, f"{mode}-res", corpus, mode, 2,
+                          extra=["--steps", "8", "--ckpt-dir", str(async_ck), "--ckpt-every", "2", "--resume",
+                                 "--async-ckpt"])
+    assert "resumed from step 4" in r.stderr
+    assert_close(resumed, full, 0.0)
