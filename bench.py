@@ -121,6 +121,21 @@ class ClockSampler:
                 "samples_from": where, "power_w_max": max(pw) if pw else None}
 
 
+def _model_rate(M: dict, tokens_per_step: float, ms_per_step: float) -> dict:
+    """Model FLOP rate of a step against the measured bf16 GEMM peak (MEASURED_PEAKS.json
+    when present, else the pool's fallback), per GPU."""
+    from dtrain_b200.models.gpt import GPTConfig, train_flops_per_token
+    flops = train_flops_per_token(GPTConfig(**M)) * tokens_per_step
+    peak, tag = 1590.0, "of fallback"
+    p = os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            peak, tag = float(json.load(f)["bf16_tflops"]), "of measured"
+    tf = flops / (ms_per_step / 1e3) / 1e12
+    return {"model_tflops_per_step": flops / 1e12, "model_tflops_per_s": tf,
+            "frac_of_bf16_peak": f"{tf / peak:.3f} {tag} {peak:.0f} TFLOP/s burst"}
+
+
 def _timed(fn, steps: int, world: int):
     """CUDA-event time of ``steps`` calls of fn, barrier + synchronize on both sides; max over ranks (ms)."""
     import torch.distributed as dist
@@ -229,6 +244,7 @@ def run_ours(a, rank, world, local):
                 "ms_per_step": ms_e2e / a.steps, "final_loss": losses[-1] if losses else None},
         "gpu_launches": int(launches),
         "gpu_launches_per_step": launches / max(1, a.steps),
+        "per_gpu": _model_rate(M, seq * accum * M["ctx"], ms / a.steps),
         "clocks": clocks,
     }
     tr._graph = None  # release the captured graph before the groups go away
@@ -319,6 +335,7 @@ def run_reference(a, rank, world, local):
                 "h2d_bytes_per_step": seq * accum * (M["ctx"] + 1) * 8, "d2h_bytes_per_step": 4,
                 "ms_per_step": ms_e2e / a.steps},
         "gpu_launches": 0,
+        "per_gpu": _model_rate(M, seq * accum * M["ctx"], ms / a.steps),
         "clocks": clocks,
     }
     if world > 1:

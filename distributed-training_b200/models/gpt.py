@@ -47,6 +47,15 @@ class GPTConfig:
         return self.dtype in ("bfloat16", "bf16")
 
 
+def train_flops_per_token(c: GPTConfig) -> float:
+    """Model FLOPs of one training token (forward + backward, no recomputation): 6 per
+    GEMM weight (Linear and head) plus causal attention's 6 * layers * ctx * dim
+    (QK^T and PV, 4*ctx*dim per token forward over the full square, halved by the mask,
+    times three for forward + backward)."""
+    gemm = c.layers * (c.dim * 3 * c.dim + c.dim * c.dim + 2 * c.dim * 4 * c.dim) + c.dim * c.vocab
+    return 6.0 * gemm + 6.0 * c.layers * c.ctx * c.dim
+
+
 def _np_dtype(cfg: GPTConfig):
     return np.float32 if cfg.fused else np.dtype(cfg.dtype)
 

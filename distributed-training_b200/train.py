@@ -28,7 +28,7 @@ import time
 import numpy as np
 import torch
 
-from .models.gpt import GPT, GPTConfig
+from .models.gpt import GPT, GPTConfig, train_flops_per_token
 from .ops.optim import AdamW, clip_scale
 from .utils import checkpoint
 from .utils.data import CharData, SyntheticData, load_text, lr_at, rank_batch
@@ -438,6 +438,7 @@ def main(argv=None):
     restarts = int(os.environ.get("DTRAIN_RESTART_COUNT", "0"))
     tokens_per_step = a.batch * a.ctx * a.accum * max(world, a.emulate_world)
     saver = checkpoint.AsyncSaver() if (a.async_ckpt and a.ckpt_dir and a.ckpt_every) else None
+    flops_per_token = train_flops_per_token(cfg)
     vworlds = a.emulate_world if a.mode == "single" else 1
     # GPU jobs that log also record the device time of each step (every rank takes
     # part in the max, so the decision depends only on the shared flags)
@@ -477,6 +478,7 @@ def main(argv=None):
             if dev_ms is not None:  # device-timed (CUDA events on the training stream), max over ranks
                 rec["step_ms_max_over_ranks"] = dev_ms
                 rec["tokens_per_s_device"] = tokens_per_step / (dev_ms / 1e3)
+                rec["model_tflops_per_s_per_gpu"] = flops_per_token * tokens_per_step / world / (dev_ms / 1e3) / 1e12
             log.write(json.dumps(rec) + "\n")
             log.flush()
         if a.ckpt_dir and a.ckpt_every and (step + 1) % a.ckpt_every == 0:

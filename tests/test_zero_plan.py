@@ -53,3 +53,11 @@ def test_gather_plan_sites_and_generation_bookkeeping():
     plan.state[GS_GEN] = 7
     plan.mark_gathered()
     assert plan.state[GS_SITES:].tolist() == [7] * len(ws)
+
+
+def test_train_flops_per_token_counts_gemm_weights_and_causal_attention():
+    from dtrain_b200.models.gpt import train_flops_per_token
+    c = GPTConfig(vocab=50304, ctx=1024, dim=768, heads=12, layers=12)
+    gemm = 12 * (768 * 2304 + 768 * 768 + 2 * 768 * 3072) + 768 * 50304  # 123.57 M weights
+    assert gemm == 123_568_128
+    assert train_flops_per_token(c) == 6.0 * gemm + 6.0 * 12 * 1024 * 768
