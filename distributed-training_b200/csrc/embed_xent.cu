@@ -359,7 +359,8 @@ std::vector<torch::Tensor> xent_fwd(torch::Tensor logits, torch::Tensor tgt) {
   return {loss, lse};
 }
 
-// Cross-entropy forward from the LM-head GEMM's softmax partials (EPI_LSE in gemm.cu):
+// Cross-entropy forward (dtrain/autograd.py:250-266: mean over rows of lse - z[target])
+// from the LM-head GEMM's softmax partials (EPI_LSE in gemm.cu):
 // part[row, p] = (max, sum exp(x - max)) over column half-tile p of the bf16 logits.
 // One warp per row merges its partials in a fixed order (lane-strided, then a fixed
 // shuffle tree), so the result is deterministic; loss_row = lse - z[target].

@@ -165,7 +165,8 @@ __device__ __forceinline__ float ex2_fast(float x) {
   return y;
 }
 
-// EPI_LSE: fold 32 outputs of this lane's row (columns col..col+31, those < N) into
+// EPI_LSE (the head GEMM carrying the cross-entropy forward's row statistics,
+// dtrain/autograd.py:250-266): fold 32 outputs of this lane's row (columns col..col+31, those < N) into
 // the running (max m, sum s of exp(x - m)).  v holds the bf16-rounded outputs (epi_chunk
 // rounds them), the values the logits tensor holds.  One exp2 per element plus two per chunk.
 __device__ __forceinline__ void lse_fold(const float* v, int col, int N, float& m, float& s) {

@@ -48,7 +48,8 @@ _ONESHOT_MAX_BYTES = 0
 
 
 class FdExchange:
-    """All-gather of file descriptors between the ranks of one node.
+    """All-gather of file descriptors between the ranks of one node (no counterpart in
+    the reference, whose peers share nothing but TCP connections, dtrain/comm.py:132-217).
 
     Each rank listens on an abstract Unix socket whose name goes through the bootstrap
     ``exchange`` once.  ``all_gather(fd, size)`` connects to every peer and sends
