@@ -1,142 +1,140 @@
-"""End-to-end distributed training through the launcher (real processes, fp64 CPU ranks).
+"""Training jobs end to end: CLI, launcher, real processes, fp64 CPU ranks.
 
-Same checks as the reference's integration tests, plus equality with the
-reference's own training run and checkpoint-format compatibility with it.
+Pinned behaviours (the reference's integration tests, tests/test_training.py there):
+data-parallel and ZeRO-1 jobs reproduce a single process that emulates the same
+global batch; bucket size, overlap and summation order leave the result unchanged;
+gradient accumulation equals the larger batch; stop/resume and crash/restart/resume
+are bit-identical to an uninterrupted run; an injected crash with no restart left
+surfaces exit code 17; a corrupted shard is refused.  Added here: equality with the
+reference's own training run, checkpoint interchange with it in both directions,
+asynchronous checkpoints, and the launcher's per-attempt exit records.
 """
 import json
-import os
-import subprocess
-import sys
 
-import numpy as np
 import pytest
+from harness import HAVE_REF, max_param_diff, run_job
 
-PY = sys.executable
-ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-REF = os.path.join(ROOT, "baseline", "_ref")
-TINY = ["--dim", "16", "--heads", "2", "--layers", "2", "--ctx", "16", "--batch", "2", "--dtype", "float64",
-        "--lr", "3e-3", "--warmup", "2"]
+MODEL = ["--dim", "24", "--heads", "2", "--layers", "2", "--ctx", "12", "--batch", "3", "--dtype", "float64",
+         "--lr", "2e-3", "--warmup", "2"]
+STEPS = 5
 
 
 @pytest.fixture(scope="module")
-def corpus(tmp_path_factory):
-    rng = np.random.default_rng(0)
-    words = ["the", "king", "and", "queen", "of", "rome", "said", "to", "thee", "now"]
-    p = tmp_path_factory.mktemp("data") / "corpus.txt"
-    p.write_text(" ".join(rng.choice(words, 4000)) + "\n")
-    return str(p)
+def jobs(tmp_path_factory, corpus):
+    """Runs each distinct (mode, world, flags) job once per module."""
+    workdir = tmp_path_factory.mktemp("jobs")
+    cache = {}
+
+    def get(mode, world, *flags, steps=STEPS):
+        key = (mode, world, flags, steps)
+        if key not in cache:
+            name = f"{mode}{world}-{len(cache)}"
+            job = run_job(workdir, mode, world, ["--data", corpus, "--steps", str(steps), *MODEL, *flags], name=name)
+            assert job.code == 0, job.stderr[-3000:]
+            cache[key] = job
+        return cache[key]
+
+    return get
 
 
-def train(tmp, name, corpus, mode, nproc=1, extra=(), restarts=0, check=True, pkg="dtrain_b200"):
-    out = tmp / f"{name}.npz"
-    log = tmp / f"{name}.jsonl"
-    args = ["-m", f"{pkg}.train", "--mode", mode, "--data", corpus, "--save-params", str(out), "--log", str(log),
-            *TINY, *extra]
-    if mode == "single":
-        cmd = [PY, *args]
-    else:
-        cmd = [PY, "-m", f"{pkg}.launch", "--nproc", str(nproc), "--max-restarts", str(restarts), "--timeout", "30",
-               "--", PY, *args]
-    env = dict(os.environ, OMP_NUM_THREADS="1", OPENBLAS_NUM_THREADS="1",
-               PYTHONPATH=(REF if pkg == "dtrain" else ROOT) + os.pathsep + os.environ.get("PYTHONPATH", ""))
-    r = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=600, cwd=ROOT)
-    if check:
-        assert r.returncode == 0, r.stderr[-3000:]
-    params = dict(np.load(out)) if out.exists() else None
-    logs = [json.loads(line) for line in open(log)] if log.exists() else []
-    return params, logs, r
+# (description, job A, job B, max |param difference|)
+EQUIVALENT = [
+    ("ddp on 4 ranks == one process emulating 4 ranks", ("ddp", 4), ("single", 1, "--emulate-world", "4"), 1e-10),
+    ("zero on 4 ranks == ddp on 4 ranks", ("zero", 4), ("ddp", 4), 1e-10),
+    ("1 KiB buckets overlapped == one 100 MiB bucket after backward",
+     ("ddp", 3, "--bucket-mb", "0.001"), ("ddp", 3, "--no-overlap", "--bucket-mb", "100"), 1e-12),
+    ("ring order == direct order", ("ddp", 3), ("ddp", 3, "--algo", "direct"), 1e-12),
+    ("2 micro-steps on 2 ranks == one process emulating 2 ranks with 2 micro-steps",
+     ("ddp", 2, "--accum", "2"), ("single", 1, "--emulate-world", "2", "--accum", "2"), 1e-10),
+]
 
 
-def assert_close(a, b, tol):
-    assert a.keys() == b.keys()
-    worst = max(float(np.max(np.abs(a[k] - b[k]))) for k in a)
-    assert worst <= tol, f"max abs param difference {worst:g} > {tol:g}"
+@pytest.mark.parametrize("case", EQUIVALENT, ids=[c[0] for c in EQUIVALENT])
+def test_equivalent_jobs_train_the_same_model(jobs, case):
+    _, a, b, tol = case
+    ja, jb = jobs(*a), jobs(*b)
+    assert max_param_diff(ja.params, jb.params) <= tol
+    la = [r["loss"] for r in ja.log if "loss" in r]
+    lb = [r["loss"] for r in jb.log if "loss" in r]
+    assert len(la) == len(lb) == STEPS
+    assert max(abs(x - y) for x, y in zip(la, lb)) <= 1e-10
 
 
-STEPS = ["--steps", "6"]
-needs_ref = pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "dtrain")), reason="reference not installed")
-
-
-def test_ddp_matches_single_process(tmp_path, corpus):
-    ref, ref_log, _ = train(tmp_path, "single", corpus, "single", extra=[*STEPS, "--emulate-world", "4"])
-    ddp, ddp_log, _ = train(tmp_path, "ddp", corpus, "ddp", 4, extra=STEPS)
-    assert_close(ddp, ref, 1e-10)
-    for a, b in zip(ref_log, ddp_log):
-        assert abs(a["loss"] - b["loss"]) < 1e-10
-
-
-def test_zero_matches_ddp_and_shards_state(tmp_path, corpus):
-    ddp, _, _ = train(tmp_path, "ddp", corpus, "ddp", 4, extra=STEPS)
-    zero, zlog, _ = train(tmp_path, "zero", corpus, "zero", 4, extra=STEPS)
-    assert_close(zero, ddp, 1e-10)
-    nparams = sum(v.size for v in ddp.values())
-    state = [x for x in zlog if "optimizer_state_bytes_per_rank" in x][0]["optimizer_state_bytes_per_rank"]
-    assert state == 2 * 8 * -(-nparams // 4)  # rank 0: m and v (float64) for ceil(n/4) elements
-
-
-def test_overlap_bucket_size_and_algorithm_do_not_change_results(tmp_path, corpus):
-    a, _, _ = train(tmp_path, "a", corpus, "ddp", 3, extra=[*STEPS, "--bucket-mb", "0.001"])
-    b, _, _ = train(tmp_path, "b", corpus, "ddp", 3, extra=[*STEPS, "--no-overlap", "--bucket-mb", "100"])
-    c, _, _ = train(tmp_path, "c", corpus, "ddp", 3, extra=[*STEPS, "--algo", "direct"])
-    assert_close(a, b, 1e-12)
-    assert_close(a, c, 1e-12)
-
-
-def test_gradient_accumulation_matches_larger_batch(tmp_path, corpus):
-    ref, _, _ = train(tmp_path, "ref", corpus, "single", extra=[*STEPS, "--emulate-world", "2", "--accum", "2"])
-    ddp, _, _ = train(tmp_path, "acc", corpus, "ddp", 2, extra=[*STEPS, "--accum", "2"])
-    assert_close(ddp, ref, 1e-10)
+def test_zero_keeps_one_shard_of_optimizer_state_per_rank(jobs):
+    ddp, zero = jobs("ddp", 4), jobs("zero", 4)
+    n = sum(v.size for v in ddp.params.values())
+    rec = [r for r in zero.log if "optimizer_state_bytes_per_rank" in r]
+    assert rec and rec[0]["optimizer_state_bytes_per_rank"] == 2 * 8 * -(-n // 4)  # rank 0: fp64 m and v
 
 
 @pytest.mark.parametrize("mode", ["ddp", "zero"])
-def test_checkpoint_resume_is_exact(tmp_path, corpus, mode):
-    full, _, _ = train(tmp_path, f"{mode}-full", corpus, mode, 2, extra=["--steps", "8"])
-    ck = tmp_path / f"ck-{mode}"
-    train(tmp_path, f"{mode}-part", corpus, mode, 2,
-          extra=["--steps", "8", "--stop-after", "4", "--ckpt-dir", str(ck), "--ckpt-every", "2"])
-    resumed, _, r = train(tmp_path, f"{mode}-res", corpus, mode, 2,
-                          extra=["--steps", "8", "--ckpt-dir", str(ck), "--ckpt-every", "2", "--resume"])
-    assert "resumed from step 4" in r.stderr
-    assert_close(resumed, full, 0.0)
+def test_preempted_job_resumes_bit_identically(tmp_path, corpus, mode):
+    common = ["--data", corpus, "--steps", "7", *MODEL]
+    whole = run_job(tmp_path, mode, 2, common, name="whole")
+    ck = str(tmp_path / "ck")
+    first = run_job(tmp_path, mode, 2, [*common, "--stop-after", "4", "--ckpt-dir", ck, "--ckpt-every", "2"],
+                    name="first")
+    second = run_job(tmp_path, mode, 2, [*common, "--ckpt-dir", ck, "--ckpt-every", "2", "--resume"], name="second")
+    assert whole.code == first.code == second.code == 0, second.stderr[-2000:]
+    assert "resumed from step 4" in second.stderr
+    assert max_param_diff(second.params, whole.params) == 0.0
 
 
 @pytest.mark.parametrize("mode", ["ddp", "zero"])
-def test_worker_crash_restart_resume_matches_failure_free_run(tmp_path, corpus, mode):
-    clean, _, _ = train(tmp_path, f"{mode}-clean", corpus, mode, 3, extra=["--steps", "9"])
-    ck = tmp_path / f"ck-fail-{mode}"
-    crashed, _, r = train(tmp_path, f"{mode}-crash", corpus, mode, 3, restarts=2,
-                          extra=["--steps", "9", "--ckpt-dir", str(ck), "--ckpt-every", "3", "--resume",
-                                 "--fail-at-step", "5", "--fail-rank", "1"])
-    assert "injected failure at step 5" in r.stderr
-    assert "restarting" in r.stderr and "resumed from step 3" in r.stderr
-    assert_close(crashed, clean, 0.0)
+def test_crash_restart_resume_is_bit_identical(tmp_path, corpus, mode):
+    common = ["--data", corpus, "--steps", "8", *MODEL]
+    clean = run_job(tmp_path, mode, 3, common, name="clean")
+    ck = str(tmp_path / "ck")
+    exits = str(tmp_path / "exits.jsonl")
+    crashed = run_job(tmp_path, mode, 3, [*common, "--ckpt-dir", ck, "--ckpt-every", "2", "--resume",
+                                          "--fail-at-step", "5", "--fail-rank", "2"],
+                      name="crashed", restarts=1, launcher_flags=["--exit-log", exits])
+    assert clean.code == crashed.code == 0, crashed.stderr[-3000:]
+    assert "injected failure at step 5" in crashed.stderr
+    assert "exited with" in crashed.stderr and "restarting" in crashed.stderr
+    assert "resumed from step 4" in crashed.stderr
+    assert max_param_diff(crashed.params, clean.params) == 0.0
+    recs = [json.loads(line) for line in open(exits)]
+    first = {r["rank"]: r for r in recs if r["attempt"] == 0}
+    assert set(first) == {0, 1, 2}
+    assert (first[2]["code"], first[2]["cause"]) == (17, "failed")  # the injected crash
+    # the survivors either noticed the dead peer themselves or were stopped by the launcher
+    assert all(first[r]["cause"] in ("failed", "stopped") and first[r]["code"] != 0 for r in (0, 1))
+    assert sorted((r["rank"], r["code"], r["cause"]) for r in recs if r["attempt"] == 1) == [
+        (0, 0, "ok"), (1, 0, "ok"), (2, 0, "ok")]
 
 
-def test_no_restarts_left_propagates_failure(tmp_path, corpus):
-    _, _, r = train(tmp_path, "fail", corpus, "ddp", 2, restarts=0, check=False,
-                    extra=["--steps", "4", "--fail-at-step", "1", "--fail-rank", "0"])
-    assert r.returncode == 17
+def test_failure_without_restarts_returns_the_workers_code(tmp_path, corpus):
+    job = run_job(tmp_path, "ddp", 2, ["--data", corpus, "--steps", "4", *MODEL, "--fail-at-step", "2",
+                                       "--fail-rank", "1"], name="fail")
+    assert job.code == 17
+    assert "injected failure at step 2" in job.stderr
 
 
-def test_corrupt_checkpoint_is_rejected(tmp_path, corpus):
-    ck = tmp_path / "ck-bad"
-    train(tmp_path, "w", corpus, "ddp", 2, extra=["--steps", "2", "--ckpt-dir", str(ck), "--ckpt-every", "2"])
-    shard = ck / "step_000002" / "rank1.npz"
-    b = bytearray(shard.read_bytes())
-    b[len(b) // 2] ^= 0xFF
-    shard.write_bytes(bytes(b))
-    _, _, r = train(tmp_path, "r", corpus, "ddp", 2, check=False,
-                    extra=["--steps", "4", "--ckpt-dir", str(ck), "--resume"])
-    assert r.returncode != 0 and "checksum mismatch" in r.stderr
+def test_corrupted_shard_is_refused(tmp_path, corpus):
+    ck = tmp_path / "ck"
+    common = ["--data", corpus, *MODEL, "--ckpt-dir", str(ck)]
+    assert run_job(tmp_path, "ddp", 2, [*common, "--steps", "2", "--ckpt-every", "2"], name="w").code == 0
+    shard = ck / "step_000002" / "rank0.npz"
+    data = bytearray(shard.read_bytes())
+    data[-len(data) // 3] ^= 0x5A
+    shard.write_bytes(bytes(data))
+    job = run_job(tmp_path, "ddp", 2, [*common, "--steps", "4", "--resume"], name="r")
+    assert job.code != 0 and "checksum mismatch" in job.stderr
+
+
+needs_ref = pytest.mark.skipif(not HAVE_REF, reason="reference not installed in baseline/_ref")
 
 
 @needs_ref
 @pytest.mark.parametrize("mode", ["ddp", "zero"])
 def test_matches_the_reference_training_run(tmp_path, corpus, mode):
-    ours, our_log, _ = train(tmp_path, f"ours-{mode}", corpus, mode, 2, extra=STEPS)
-    ref, ref_log, _ = train(tmp_path, f"ref-{mode}", corpus, mode, 2, extra=STEPS, pkg="dtrain")
-    assert_close(ours, ref, 1e-10)
-    for a, b in zip(our_log, ref_log):
+    flags = ["--data", corpus, "--steps", str(STEPS), *MODEL]
+    ours = run_job(tmp_path, mode, 2, flags, name="ours")
+    ref = run_job(tmp_path, mode, 2, flags, name="ref", package="dtrain")
+    assert ours.code == ref.code == 0
+    assert max_param_diff(ours.params, ref.params) <= 1e-10
+    for a, b in zip(ours.log, ref.log):
         if "loss" in a:
             assert abs(a["loss"] - b["loss"]) < 1e-10
 
@@ -144,22 +142,17 @@ def test_matches_the_reference_training_run(tmp_path, corpus, mode):
 @needs_ref
 @pytest.mark.parametrize("mode", ["ddp", "zero"])
 def test_checkpoints_interchange_with_the_reference(tmp_path, corpus, mode):
-    """Our checkpoint resumes in the reference and the reference's resumes here, bit-exactly."""
-    full, _, _ = train(tmp_path, f"full-{mode}", corpus, mode, 2, extra=["--steps", "6"])
-    ck = tmp_path / f"ck-x-{mode}"
-    train(tmp_path, f"part-{mode}", corpus, mode, 2,
-          extra=["--steps", "6", "--stop-after", "3", "--ckpt-dir", str(ck), "--ckpt-every", "3"])
-    res_ref, _, r = train(tmp_path, f"res-ref-{mode}", corpus, mode, 2, pkg="dtrain",
-                          extra=["--steps", "6", "--ckpt-dir", str(ck), "--resume"])
-    assert "resumed from step 3" in r.stderr
-    assert_close(res_ref, full, 1e-12)
-    ck2 = tmp_path / f"ck-y-{mode}"
-    train(tmp_path, f"part2-{mode}", corpus, mode, 2, pkg="dtrain",
-          extra=["--steps", "6", "--stop-after", "3", "--ckpt-dir", str(ck2), "--ckpt-every", "3"])
-    res_ours, _, r = train(tmp_path, f"res-ours-{mode}", corpus, mode, 2,
-                           extra=["--steps", "6", "--ckpt-dir", str(ck2), "--resume"])
-    assert "resumed from step 3" in r.stderr
-    assert_close(res_ours, full, 1e-12)
+    """A checkpoint written here resumes in the reference, and one written by the
+    reference resumes here, both reproducing the uninterrupted run."""
+    common = ["--data", corpus, "--steps", "6", *MODEL]
+    full = run_job(tmp_path, mode, 2, common, name="full")
+    for writer, reader in (("dtrain_b200", "dtrain"), ("dtrain", "dtrain_b200")):
+        ck = str(tmp_path / f"ck-{writer}")
+        run_job(tmp_path, mode, 2, [*common, "--stop-after", "3", "--ckpt-dir", ck, "--ckpt-every", "3"],
+                name=f"w-{writer}", package=writer)
+        res = run_job(tmp_path, mode, 2, [*common, "--ckpt-dir", ck, "--resume"], name=f"r-{reader}", package=reader)
+        assert res.code == 0 and "resumed from step 3" in res.stderr, res.stderr[-2000:]
+        assert max_param_diff(res.params, full.params) <= 1e-12
 
 
 def test_precision_flag_is_a_short_form_of_dtype():
@@ -173,19 +166,18 @@ def test_precision_flag_is_a_short_form_of_dtype():
 def test_async_checkpoints_match_synchronous_ones(tmp_path, corpus, mode):
     """--async-ckpt writes the same shard files (same bytes) and commits them in the same
     layout; resuming from one reproduces the uninterrupted run exactly."""
-    full, _, _ = train(tmp_path, f"{mode}-full", corpus, mode, 2, extra=["--steps", "8"])
-    sync_ck, async_ck = tmp_path / f"sync-{mode}", tmp_path / f"async-{mode}"
-    train(tmp_path, f"{mode}-sync", corpus, mode, 2,
-          extra=["--steps", "8", "--stop-after", "4", "--ckpt-dir", str(sync_ck), "--ckpt-every", "2"])
-    train(tmp_path, f"{mode}-async", corpus, mode, 2,
-          extra=["--steps", "8", "--stop-after", "4", "--ckpt-dir", str(async_ck), "--ckpt-every", "2",
-                 "--async-ckpt"])
+    common = ["--data", corpus, "--steps", "8", *MODEL]
+    full = run_job(tmp_path, mode, 2, common, name="full")
+    sync_ck, async_ck = tmp_path / "sync", tmp_path / "async"
+    run_job(tmp_path, mode, 2, [*common, "--stop-after", "4", "--ckpt-dir", str(sync_ck), "--ckpt-every", "2"],
+            name="sync")
+    run_job(tmp_path, mode, 2, [*common, "--stop-after", "4", "--ckpt-dir", str(async_ck), "--ckpt-every", "2",
+                                "--async-ckpt"], name="async")
     for step in ("step_000002", "step_000004"):
         for f in ("rank0.npz", "rank1.npz", "manifest.json"):
             assert (sync_ck / step / f).read_bytes() == (async_ck / step / f).read_bytes(), (step, f)
     assert (async_ck / "LATEST").read_text() == "step_000004"
-    resumed, _, r = train(tmp_path, f"{mode}-res", corpus, mode, 2,
-                          extra=["--steps", "8", "--ckpt-dir", str(async_ck), "--ckpt-every", "2", "--resume",
-                                 "--async-ckpt"])
-    assert "resumed from step 4" in r.stderr
-    assert_close(resumed, full, 0.0)
+    res = run_job(tmp_path, mode, 2, [*common, "--ckpt-dir", str(async_ck), "--ckpt-every", "2", "--resume",
+                                      "--async-ckpt"], name="res")
+    assert "resumed from step 4" in res.stderr
+    assert max_param_diff(res.params, full.params) == 0.0
