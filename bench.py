@@ -1,13 +1,21 @@
 """Flagship benchmark: GPT-2-small-shape DDP training throughput on N B200s.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--bucket-mb 1]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--bucket-mb 25]
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \
         --master-port P bench.py --gpus N --steps K --warmup W
 
 Config (GPT-2-small DDP): 12 layers, d_model 768, 12 heads,
 context 1024, vocab 50304, 16 sequences per GPU of iid uniform random tokens,
 bf16 compute with fp32 grads and master weights, AdamW with global-norm clip
-1.0, 1 MiB gradient buckets, random init.  Weak scaling: per-GPU work is fixed.
+1.0, 25 MiB gradient buckets (``--bucket-mb 1`` for the config's other size),
+random init.  Weak scaling: per-GPU work is fixed.
+
+Gradient sync (N > 1): each bucket's all-reduce is launched from the grad-ready
+hooks while backward runs, inside the CUDA graph that replays forward + backward;
+the same kernels publish the gradient's sum of squares for the clip.  After the
+timed runs the line reports ``checks``: whether every rank holds bit-identical
+masters and gradients, and whether bucket-by-bucket and flat all-reduces of one
+local gradient agree bit for bit.
 
 Timing: W untimed warm-up steps, then K steps bracketed by a barrier and
 torch.cuda.synchronize() on both sides, timed with CUDA events on the training
@@ -136,6 +144,59 @@ def _model_rate(M: dict, tokens_per_step: float, ms_per_step: float) -> dict:
             "frac_of_bf16_peak": f"{tf / peak:.3f} {tag} {peak:.0f} TFLOP/s burst"}
 
 
+def _hash64(t: torch.Tensor) -> int:
+    """A 64-bit fingerprint of a tensor's bits (position-weighted wrapping sum of its
+    32-bit words, computed on the device; equal bits give equal fingerprints)."""
+    w = t.reshape(-1).view(torch.int32).long()
+    idx = torch.arange(w.numel(), device=w.device, dtype=torch.int64)
+    coef = (idx * 2654435761 + 40503) % 2147483647 * 2 + 1
+    return int((w * coef).sum().item()) & ((1 << 64) - 1)
+
+
+def _all_rows(pg, row: list[int]) -> list[list[int]]:
+    """Every rank's row of 64-bit integers, exchanged through the NVLink group: each
+    value travels as four exact 16-bit pieces in fp32 in this rank's slot of a
+    rank-order all-reduce (a sum with zeros everywhere else)."""
+    k = len(row)
+    buf = torch.zeros(pg.world, 4 * k, dtype=torch.float32, device=pg.device)
+    buf[pg.rank] = torch.tensor([float((v >> (16 * j)) & 0xFFFF) for v in row for j in range(4)],
+                                device=pg.device)
+    pg.allreduce(buf.reshape(-1), "direct", method="twoshot")
+    pg.check()
+    out = buf.long().cpu().tolist()
+    return [[sum(r[4 * i + j] << (16 * j) for j in range(4)) for i in range(k)] for r in out]
+
+
+def _consistency(tr, pg, batch) -> dict:
+    """Cross-rank checks after the timed runs (ranks in lockstep):
+    ranks_bit_identical - every rank's fp32 masters and averaged gradient of the last
+    step have the same bits; bucketed_equals_flat - one more backward without sync,
+    then its local gradient all-reduced bucket by bucket (the lean kernels the
+    overlapped step uses) and, from the same input, as one flat all-reduce, both in
+    rank order: the two results have the same bits on every rank."""
+    fp = tr.model.flat
+    rows = _all_rows(pg, [_hash64(fp.master), _hash64(fp.grad)])
+    ident = all(r == rows[0] for r in rows)
+    ddp = tr.ddp
+    tr.model.zero_grad()
+    x, y = batch
+    with ddp.no_sync():
+        _, loss = tr.model(x, y)
+        loss.backward()
+    raw = fp.grad.clone()
+    for b in ddp.buckets:
+        pg.allreduce(fp.grad[b.lo:b.hi], "direct", scale=1.0 / pg.world, method="twoshot", blocks=b.blocks,
+                     lean=b.lean)
+    bucketed = fp.grad.clone()
+    fp.grad.copy_(raw)
+    pg.allreduce(fp.grad, "direct", scale=1.0 / pg.world, method="twoshot")
+    same = bool(torch.equal(bucketed, fp.grad))
+    votes = _all_rows(pg, [int(same)])
+    pg.synchronize()
+    return {"ranks_bit_identical": ident, "bucketed_equals_flat": all(v[0] == 1 for v in votes),
+            "fingerprints_rank0": {"master": hex(rows[0][0]), "grad": hex(rows[0][1])}}
+
+
 def _timed(fn, steps: int, world: int):
     """CUDA-event time of ``steps`` calls of fn, barrier + synchronize on both sides; max over ranks (ms)."""
     import torch.distributed as dist
@@ -156,6 +217,27 @@ def _timed(fn, steps: int, world: int):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     return ms
+
+
+def _grad_sync(tr, C, a, world) -> dict | str:
+    """What the gradient synchronisation of the measured step actually ran."""
+    if C["mode"] == "zero":
+        if world == 1:
+            return "one GPU: no collective (AdamW + norm kernels)"
+        return ("one kernel: reduce-scatter + clip + AdamW (non-GEMM params gathered there); Linear weights "
+                "all-gathered inside the forward GEMMs" if a.gather_gemm else
+                "one kernel: reduce-scatter + clip + AdamW + all-gather")
+    if world == 1:
+        return "one GPU: no collective (gradient norm kernel + AdamW)"
+    d = tr.ddp
+    if not d.overlap:
+        return {"buckets": "unused", "method": "one two-shot all-reduce of the flat gradient after backward",
+                "order": a.algo, "grad_norm": "fused into the all-reduce"}
+    lean = sum(1 for b in d.buckets if b.lean)
+    return {"buckets": len(d.buckets), "bucket_mb": a.bucket_mb,
+            "method": "two-shot per bucket, launched from the grad-ready hooks during backward",
+            "lean_buckets": lean, "full_width_buckets": len(d.buckets) - lean, "order": a.algo,
+            "grad_norm": "fused into the all-reduce"}
 
 
 # ------------------------------------------------------------------ our arm
@@ -181,10 +263,12 @@ def run_ours(a, rank, world, local):
                     "--dim", str(M["dim"]), "--heads", str(M["heads"]), "--layers", str(M["layers"]),
                     "--lr", "6e-4", "--clip", "1.0", "--bucket-mb", str(a.bucket_mb), "--data", "synthetic",
                     "--vocab", str(M["vocab"]), "--algo", a.algo, "--accum", str(accum)]
-                   + ([] if a.overlap else ["--no-overlap"]) + (["--cuda-graph"] if a.cuda_graph else [])
+                   + (["--no-overlap"] if a.no_overlap else []) + (["--cuda-graph"] if a.cuda_graph else [])
                    + (["--gather-gemm"] if a.gather_gemm else []))
     cfg = GPTConfig(dtype="bfloat16", **M)
     tr = T.Trainer(args, cfg, dev, pg)
+    if a.trace and tr.ddp is not None:
+        tr.ddp.enable_trace()
     data = SyntheticData(M["vocab"])
     nb = a.warmup + a.steps
     host = [[data.rank_batch(s, mi, seq, M["ctx"], 0, rank, world) for mi in range(accum)] for s in range(nb)]
@@ -204,6 +288,7 @@ def run_ours(a, rank, world, local):
     t0 = time.time()
     ms = _timed(lambda i: device_step(a.warmup + i), a.steps, world)
     t1 = time.time()
+    trace = tr.ddp.trace_report() if (a.trace and tr.ddp is not None) else None
     # eager launches counted on the host, plus the kernels each graph replay runs
     launches = K.launch_count() - l0 + (tr.graph_replays - r0) * tr.graph_launches
     if sampler:
@@ -220,6 +305,7 @@ def run_ours(a, rank, world, local):
 
     ms_e2e = _timed(e2e_step, a.steps, world)
     pg.check()
+    checks = _consistency(tr, pg, dev_batches[0][0]) if (world > 1 and tr.ddp is not None) else None
     tokens = seq * accum * M["ctx"] * world
     res = {
         "metric": METRIC, "value": tokens * a.steps / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
@@ -228,20 +314,17 @@ def run_ours(a, rank, world, local):
         "data": "synthetic (iid uniform token ids, random-init weights)",
         "config": {"model": C["name"], "global_batch": seq * accum * world,
                    "seq_len": M["ctx"], "parallelism": f"{'dp' if C['mode'] == 'ddp' else 'zero1-dp'}{world}",
-                   "grad_accum": accum, "bucket_mb": a.bucket_mb if C["mode"] == "ddp" else None,
-                   "grad_sync": ("per-bucket all-reduce overlapped with backward"
-                                 if (tr.ddp is not None and tr.ddp.overlap) else
-                                 "one all-reduce of the flat gradient after backward") if C["mode"] == "ddp" else
-                   ("one kernel: reduce-scatter + clip + AdamW (non-GEMM params gathered there); Linear weights "
-                    "all-gathered inside the forward GEMMs" if a.gather_gemm else
-                    "one kernel: reduce-scatter + clip + AdamW + all-gather"),
-                   "optimizer": "AdamW, clip 1.0", "allreduce_order": a.algo,
-                   "cuda_graph": ("forward+backward captured once and replayed; gradient sync and optimizer "
-                                  "eager" if a.cuda_graph else False),
+                   "grad_accum": accum, "grad_sync": _grad_sync(tr, C, a, world),
+                   "optimizer": "AdamW, clip 1.0",
+                   "cuda_graph": (("forward+backward" + (" + bucket all-reduces + gradient norm"
+                                                         if tr.sync_in_graph and world > 1 else ""))
+                                  + " captured once and replayed; optimizer eager" if a.cuda_graph else False),
                    "l2": "no flush: weights/activations/logits per step >> 126 MB L2"},
         "e2e": {"value": tokens * a.steps / (ms_e2e / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": 2 * seq * accum * M["ctx"] * 8, "d2h_bytes_per_step": 4,
                 "ms_per_step": ms_e2e / a.steps, "final_loss": losses[-1] if losses else None},
+        "checks": checks,
+        **({"trace_last_step": trace} if trace is not None else {}),
         "gpu_launches": int(launches),
         "gpu_launches_per_step": launches / max(1, a.steps),
         "per_gpu": _model_rate(M, seq * accum * M["ctx"], ms / a.steps),
@@ -349,7 +432,9 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--bucket-mb", type=float, default=1.0)
+    ap.add_argument("--bucket-mb", type=float, default=25.0,
+                    help="DDP gradient bucket size in MiB, both arms (BASELINE config 3 names 1 and 25; 25 is torch "
+                         "DDP's default and measured faster here: fewer per-bucket cross-GPU barriers)")
     ap.add_argument("--algo", choices=["ring", "direct"], default="ring")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="gpt2-small-ddp")
     ap.add_argument("--comm-blocks", type=int, default=0, help="CTAs per collective kernel (0: by size)")
@@ -360,9 +445,12 @@ def main():
     ap.add_argument("--gather-gemm", action="store_true",
                     help="ZeRO: all-gather the Linear weights inside the forward GEMMs instead of in the optimizer "
                          "kernel (measured 1.6%% slower on 2 GPUs, GPT-2-medium)")
-    ap.add_argument("--overlap", action="store_true",
-                    help="all-reduce each gradient bucket during backward (default: one all-reduce of the flat "
-                         "gradient after backward, measured faster on B200)")
+    ap.add_argument("--trace", action="store_true",
+                    help="DDP: record device timestamps of the buckets' ready points and all-reduces (adds ~3 tiny "
+                         "kernels per bucket) and print the last timed step's timeline")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="one all-reduce of the flat gradient after backward instead of per-bucket all-reduces "
+                         "launched from the grad-ready hooks during backward")
     a = ap.parse_args()
     if a.warmup < 3:
         a.warmup = 3

@@ -164,7 +164,7 @@ struct Bars {
 
 // 320 threads, one CTA per SM.  10 warps put 3 warps on some schedulers, so the
 // per-scheduler register file caps a thread at 168 registers.
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __maxnreg__(DTB_CORESIDENT_MAXNREG_ATTN)
     fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, bf16* __restrict__ out, float* __restrict__ lse2, int T,
                   int H, float sl2) {
   extern __shared__ uint8_t smem_raw[];
@@ -501,7 +501,7 @@ __device__ __forceinline__ void put_row128(uint8_t* A, int r, const uint32_t* pk
 }
 
 template <bool DKDV>
-__global__ void __launch_bounds__(BW_THREADS, 1)
+__global__ void __maxnreg__(DTB_CORESIDENT_MAXNREG_ATTN)
     bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_constant__ CUtensorMap tmDO,
                   const float* __restrict__ lse2, float* __restrict__ delta, const bf16* __restrict__ out,
                   const bf16* __restrict__ dout, bf16* __restrict__ dqkv, int T, int H, float sl2, float scale) {

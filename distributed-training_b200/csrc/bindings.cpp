@@ -57,28 +57,32 @@ int64_t vmm_import(int64_t fd, int64_t size);
 void vmm_free(int64_t va);
 int64_t comm_status();
 void comm_status_clear();
-int64_t allreduce(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> bufs,
-                  int64_t byte_offset, int64_t n, int64_t in_dtype, int64_t out_ptr, int64_t out_dtype, int64_t algo,
-                  int64_t order, double scale, double timeout_s, int64_t blocks);
-int64_t reduce_scatter(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> bufs,
-                       int64_t byte_offset, int64_t n, int64_t dtype, int64_t out_ptr, int64_t order, double scale,
-                       int64_t sq_part_ptr, double timeout_s, int64_t blocks);
-int64_t all_gather(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> bufs,
-                   int64_t byte_offset, int64_t n, int64_t dtype, double timeout_s, int64_t blocks);
-int64_t broadcast(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> bufs,
-                  int64_t byte_offset, int64_t nbytes, int64_t root, int64_t cast_src, int64_t out16, int64_t n16,
-                  double timeout_s, int64_t blocks);
-int64_t device_barrier(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, double timeout_s);
-int64_t zero_rs_adamw(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> grads,
+int64_t allreduce(std::vector<int64_t> sigs, int64_t rank, std::vector<int64_t> bufs, int64_t byte_offset, int64_t n,
+                  int64_t in_dtype, int64_t out_ptr, int64_t out_dtype, int64_t algo, int64_t order, double scale,
+                  double timeout_s, int64_t blocks, bool lean, std::vector<int64_t> sq_pads, int64_t sq_base,
+                  int64_t sq_stride);
+int64_t collective_blocks(int64_t nbytes, int64_t want, bool lean);
+void stamp(torch::Tensor buf, int64_t slot);
+void sq_total(torch::Tensor pad, torch::Tensor out, int64_t world, int64_t stride, int64_t lo, int64_t hi);
+int64_t reduce_scatter(std::vector<int64_t> sigs, int64_t rank, std::vector<int64_t> bufs, int64_t byte_offset,
+                       int64_t n, int64_t dtype, int64_t out_ptr, int64_t order, double scale, int64_t sq_part_ptr,
+                       double timeout_s, int64_t blocks);
+int64_t all_gather(std::vector<int64_t> sigs, int64_t rank, std::vector<int64_t> bufs, int64_t byte_offset, int64_t n,
+                   int64_t dtype, double timeout_s, int64_t blocks);
+int64_t broadcast(std::vector<int64_t> sigs, int64_t rank, std::vector<int64_t> bufs, int64_t byte_offset,
+                  int64_t nbytes, int64_t root, int64_t cast_src, int64_t out16, int64_t n16, double timeout_s,
+                  int64_t blocks);
+int64_t device_barrier(std::vector<int64_t> sigs, int64_t rank, double timeout_s);
+int64_t zero_rs_adamw(std::vector<int64_t> sigs, int64_t rank, std::vector<int64_t> grads,
                       std::vector<int64_t> sq_parts, torch::Tensor master, torch::Tensor m, torch::Tensor v,
                       std::vector<int64_t> work16, std::vector<int64_t> master32, int64_t n, double lr, double b1,
                       double b2, double eps, double wd, int64_t t, double scale, double max_norm,
                       c10::optional<torch::Tensor> sq_out, bool gather_master, double timeout_s, int64_t blocks,
                       c10::optional<torch::Tensor> keep, c10::optional<torch::Tensor> gen_word);
-int64_t zero_adamw_allgather(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> sq_parts,
-                             int64_t nparts, torch::Tensor master, torch::Tensor grad, torch::Tensor m,
-                             torch::Tensor v, std::vector<int64_t> work16, std::vector<int64_t> master32, int64_t n,
-                             double lr, double b1, double b2, double eps, double wd, int64_t t, double max_norm,
+int64_t zero_adamw_allgather(std::vector<int64_t> sigs, int64_t rank, std::vector<int64_t> sq_parts, int64_t nparts,
+                             torch::Tensor master, torch::Tensor grad, torch::Tensor m, torch::Tensor v,
+                             std::vector<int64_t> work16, std::vector<int64_t> master32, int64_t n, double lr,
+                             double b1, double b2, double eps, double wd, int64_t t, double max_norm,
                              c10::optional<torch::Tensor> sq_out, bool gather_master, double timeout_s,
                              int64_t blocks, c10::optional<torch::Tensor> keep, c10::optional<torch::Tensor> gen_word);
 int64_t comm_max_blocks();
@@ -146,6 +150,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("comm_status", &comm_status);
   m.def("comm_status_clear", &comm_status_clear);
   m.def("allreduce", &allreduce);
+  m.def("collective_blocks", &collective_blocks);
+  m.def("sq_total", &sq_total);
+  m.def("stamp", &stamp);
   m.def("reduce_scatter", &reduce_scatter);
   m.def("all_gather", &all_gather);
   m.def("broadcast", &broadcast);
@@ -159,12 +166,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("forget_buffers", &CommEngine::forget_buffers)
       .def("contains", &CommEngine::contains)
       .def("peer_ptrs", &CommEngine::peer_ptrs)
-      .def("allreduce_inplace", &CommEngine::allreduce_inplace)
+      .def("allreduce_inplace", &CommEngine::allreduce_inplace, py::arg("t"), py::arg("order"), py::arg("scale"),
+           py::arg("blocks") = 0, py::arg("lean") = false, py::arg("sq_pad") = py::none(), py::arg("sq_base") = 0,
+           py::arg("sq_stride") = 0)
       .def("reduce_scatter", &CommEngine::reduce_scatter)
       .def("all_gather", &CommEngine::all_gather)
       .def("barrier", &CommEngine::barrier)
-      .def("advance", &CommEngine::advance)
-      .def_property_readonly("epoch", &CommEngine::epoch)
+      .def("note_issued", &CommEngine::note_issued)
+      .def_property_readonly("issued", &CommEngine::issued)
+      .def("device_epoch", &CommEngine::device_epoch)
       .def_property("timeout", &CommEngine::timeout, &CommEngine::set_timeout)
       .def_property_readonly("blocks", &CommEngine::blocks);
   m.def("comm_max_ranks", &comm_max_ranks);

@@ -21,6 +21,18 @@
 // barriers are enough.  Each wait gives up after `timeout_ns` (%globaltimer),
 // writes kStatusPeerTimeout into a host-mapped status word and makes the kernel
 // return: a dead peer produces an error on the host, not a hung GPU.
+//
+// Epochs live on the device: a counter in each rank's own signal pad holds the
+// last epoch its collectives used; a kernel reads it once at entry and its last
+// CTA to finish advances it.  Nothing about a collective's launch therefore
+// changes from call to call, so collectives can be captured in a CUDA graph
+// (e.g. the DDP bucket all-reduces inside the captured backward) and replayed.
+//
+// Lean variants (128 threads, <= 56 registers, < 768 B of static shared memory)
+// run beside the GEMM and attention kernels: those are capped at 144 / 152
+// registers a thread (common.cuh) and use up to ~226 KB of shared memory per SM,
+// which leaves room for exactly such a CTA, so a bucket all-reduce launched during
+// backward does not wait for (or take) whole SMs.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -31,18 +43,20 @@
 namespace dtb {
 
 constexpr int kMaxRanks = 8;
-constexpr int kMaxCommBlocks = 128;
+constexpr int kMaxCommBlocks = 160;
 constexpr int kCommThreads = 512;
+constexpr int kLeanThreads = 128;
 
-int64_t allreduce(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> bufs,
-                  int64_t byte_offset, int64_t n, int64_t in_dtype, int64_t out_ptr, int64_t out_dtype, int64_t algo,
-                  int64_t order, double scale, double timeout_s, int64_t blocks);
-int64_t reduce_scatter(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> bufs,
+int64_t allreduce(std::vector<int64_t> sigs, int64_t rank, std::vector<int64_t> bufs, int64_t byte_offset, int64_t n,
+                  int64_t in_dtype, int64_t out_ptr, int64_t out_dtype, int64_t algo, int64_t order, double scale,
+                  double timeout_s, int64_t blocks, bool lean, std::vector<int64_t> sq_pads, int64_t sq_base,
+                  int64_t sq_stride);
+int64_t reduce_scatter(std::vector<int64_t> sigs, int64_t rank, std::vector<int64_t> bufs,
                        int64_t byte_offset, int64_t n, int64_t dtype, int64_t out_ptr, int64_t order, double scale,
                        int64_t sq_part_ptr, double timeout_s, int64_t blocks);
-int64_t all_gather(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> bufs,
+int64_t all_gather(std::vector<int64_t> sigs, int64_t rank, std::vector<int64_t> bufs,
                    int64_t byte_offset, int64_t n, int64_t dtype, double timeout_s, int64_t blocks);
-int64_t device_barrier(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, double timeout_s);
+int64_t device_barrier(std::vector<int64_t> sigs, int64_t rank, double timeout_s);
 
 enum : int { ORDER_RANK = 0, ORDER_CYCLIC = 1 };
 enum : int { DT_F32 = 0, DT_BF16 = 1 };
@@ -55,18 +69,69 @@ struct Sigs {
 };
 
 struct CommCtx {
-  Sigs sig;           // every rank's signal pad [kMaxCommBlocks][kMaxRanks] + descriptor ring
+  Sigs sig;           // every rank's signal pad [kMaxCommBlocks][kMaxRanks] + descriptor ring + counters
+  const Sigs* sp;     // device: a shared-memory copy of `sig` (set by collective_begin)
   int rank, world;
-  uint32_t epoch;     // first epoch this launch may use
+  uint32_t epoch;     // first epoch of this launch: set on the device by collective_begin()
   uint32_t tag;       // descriptor of this collective (kind, element count, dtype)
   uint64_t timeout_ns;
   int* host_status;   // host-mapped status word (device pointer)
 };
 
+// Sums of squares of a collective's reduced values, published to every rank:
+// CTA b of rank r writes its slice's fp64 sum to p[q][r * stride + base + b] on
+// every rank q, so each rank ends up with all ranks' partials in its own pad.
+struct SqOut {
+  double* p[kMaxRanks];  // every rank's pad (nullptr: not requested)
+  int base, stride;
+};
+
 // After the flags, each rank's signal pad holds a ring of kDescSlots 64-bit
-// descriptors (epoch << 32 | tag) of its own recent collectives.
+// descriptors (epoch << 32 | tag) of its own recent collectives, then two 32-bit
+// counters: the last epoch used and the CTAs of the running collective that exited.
 constexpr int kFlagWords = kMaxCommBlocks * kMaxRanks;
 constexpr int kDescSlots = 16;
+constexpr int kCtrWord = kFlagWords + 2 * kDescSlots;
+constexpr int kSigBytesUsed = (kCtrWord + 2) * 4;
+static_assert(kSigBytesUsed <= 8192, "signal pad layout exceeds the 8 KB pad");
+
+// Copies pointer arrays from kernel parameters into shared memory with static
+// indices.  The kernels index them with ranks computed at run time; doing that on
+// the parameters would make every thread keep a local-memory copy of the struct.
+#define DTB_SHARED_COPY(T, name, src)                                      \
+  __shared__ T name;                                                      \
+  if (threadIdx.x == 0) {                                                 \
+    _Pragma("unroll") for (int i_ = 0; i_ < kMaxRanks; ++i_) name.p[i_] = (src).p[i_]; \
+  }
+
+// Reads the epoch counter (one value for the whole CTA): this launch uses epochs
+// last+1 ... last+used.  Also publishes the shared copies the kernel made before
+// calling it (its barriers order them).
+__device__ __forceinline__ void collective_begin(CommCtx& c) {
+  DTB_SHARED_COPY(Sigs, s_sig, c.sig)
+  __shared__ uint32_t s_last;
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = __ldcg(s_sig.p[c.rank] + kCtrWord);  // L2: written by the last launch
+  __syncthreads();
+  c.sp = &s_sig;
+  c.epoch = s_last + 1u;
+}
+
+// Every CTA calls this once on its way out (also after a timeout); the last one
+// resets the exit count and advances the epoch counter by `used`.  All CTAs have
+// read the counter before any of them can be the last to exit.
+__device__ __forceinline__ void collective_end(const CommCtx& c, uint32_t used) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t* w = c.sp->p[c.rank] + kCtrWord;
+    __threadfence();
+    if (atomicAdd(w + 1, 1u) == gridDim.x - 1u) {
+      atomicExch(w + 1, 0u);
+      atomicExch(w, c.epoch - 1u + used);
+      __threadfence();
+    }
+  }
+}
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -76,6 +141,16 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+
+// Polling load: relaxed at system scope, so it reads the coherent value without
+// the L1 invalidation an acquire implies on every poll (a co-resident kernel keeps
+// its L1 contents); the waiter issues one acquire fence once the flag has arrived.
+__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_acquire_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 
 __device__ __forceinline__ uint64_t ld_acquire_sys64(const uint64_t* p) {
   uint64_t v;
@@ -92,13 +167,18 @@ __device__ bool cta_barrier(const CommCtx& c, uint32_t epoch) {
   if (threadIdx.x < c.world) {
     const int p = threadIdx.x;
     __threadfence_system();
-    st_release_sys(c.sig.p[p] + blockIdx.x * kMaxRanks + c.rank, epoch);
-    const uint32_t* mine = c.sig.p[c.rank] + blockIdx.x * kMaxRanks + p;
+    st_release_sys(c.sp->p[p] + blockIdx.x * kMaxRanks + c.rank, epoch);
+    const uint32_t* mine = c.sp->p[c.rank] + blockIdx.x * kMaxRanks + p;
     uint64_t t0 = 0;
     for (uint32_t i = 0;; ++i) {
-      const uint32_t v = ld_acquire_sys(mine);
-      if ((int)(v - epoch) >= 0) break;
-      if ((i & 63u) == 0u) {
+      const uint32_t v = ld_relaxed_sys(mine);
+      if ((int)(v - epoch) >= 0) {
+        fence_acquire_sys();
+        break;
+      }
+      // after a short spin, poll politely: the CTA may share its SM with a GEMM
+      if (i >= 16u) __nanosleep(i < 256u ? 128 : 512);
+      if ((i & 31u) == 0u) {
         const uint64_t now = globaltimer_ns();
         if (t0 == 0) t0 = now;
         else if (now - t0 > c.timeout_ns) {
@@ -124,7 +204,7 @@ __device__ bool cta_barrier(const CommCtx& c, uint32_t epoch) {
 __device__ bool cta_enter(const CommCtx& c) {
   const uint64_t mine = ((uint64_t)c.epoch << 32) | c.tag;
   if (blockIdx.x == 0 && threadIdx.x == 0) {
-    uint64_t* ring = reinterpret_cast<uint64_t*>(c.sig.p[c.rank] + kFlagWords);
+    uint64_t* ring = reinterpret_cast<uint64_t*>(c.sp->p[c.rank] + kFlagWords);
     *reinterpret_cast<volatile uint64_t*>(ring + (c.epoch % kDescSlots)) = mine;
     __threadfence_system();
   }
@@ -134,7 +214,7 @@ __device__ bool cta_enter(const CommCtx& c) {
   if (threadIdx.x == 0) mismatch = 0;
   __syncthreads();
   if (threadIdx.x < c.world && threadIdx.x != c.rank) {
-    const uint64_t* ring = reinterpret_cast<const uint64_t*>(c.sig.p[threadIdx.x] + kFlagWords);
+    const uint64_t* ring = reinterpret_cast<const uint64_t*>(c.sp->p[threadIdx.x] + kFlagWords);
     if (ld_acquire_sys64(ring + (c.epoch % kDescSlots)) != mine) {
       atomicExch(&mismatch, 1);
       atomicCAS(c.host_status, 0, kStatusSeqMismatch);
@@ -271,7 +351,7 @@ __device__ __forceinline__ void store8<bf16>(bf16* out, const float* v) {
 // If sq != nullptr, also accumulate sum of squares of the written values (fp64).
 // All ranks' buffers share one byte offset from 256-byte aligned bases, so they
 // have the same 16-byte phase; the vector loop runs when `out` shares it too.
-template <typename TI, typename TO, int WT = 0>
+template <typename TI, typename TO, int WT = 0, bool LEAN = false>
 __device__ __forceinline__ void reduce_range(const Peers& in, TO* out, long a, long b, int W, int first, float scale,
                                              double* sq) {
   double s = 0.0;
@@ -289,10 +369,11 @@ __device__ __forceinline__ void reduce_range(const Peers& in, TO* out, long a, l
       out[i] = v;
       s += (double)v * v;
     }
-    // two float4 per thread per iteration: 2*WT loads in flight
+    // two float4 per thread per iteration: 2*WT loads in flight (one in the lean
+    // variant, which has a quarter of the registers)
     const long step = (long)blockDim.x * 4;
     long i = head + threadIdx.x * 4;
-    for (; i + step < ve; i += 2 * step) {
+    for (; !LEAN && i + step < ve; i += 2 * step) {
       float4 v0 = reduce_vec4<WT>(in, i, W, first);
       float4 v1 = reduce_vec4<WT>(in, i + step, W, first);
       v0.x *= scale; v0.y *= scale; v0.z *= scale; v0.w *= scale;
@@ -334,10 +415,11 @@ __device__ __forceinline__ void reduce_range(const Peers& in, TO* out, long a, l
       stf<TO>(out + i, v);
       s += (double)v * v;
     }
-    // two vectors per thread per iteration: 2*WT 16-byte loads in flight
+    // two vectors per thread per iteration: 2*WT 16-byte loads in flight (one
+    // vector in the lean variant)
     const long step = (long)blockDim.x * 8;
     long i = head + threadIdx.x * 8;
-    for (; i + step < ve; i += 2 * step) {
+    for (; !LEAN && i + step < ve; i += 2 * step) {
       float v0[8], v1[8];
       reduce_vec8_bf16<WT>(in, i, W, first, v0);
       reduce_vec8_bf16<WT>(in, i + step, W, first, v1);
@@ -412,8 +494,7 @@ __device__ __forceinline__ void copy_range(const T* src, T* dst, long a, long b)
 // One-shot all-reduce: every rank reduces the whole buffer from all peers (order
 // ORDER_RANK or ORDER_CYCLIC over the same chunking as the two-shot) into `out`.
 template <typename TI, typename TO, int WT>
-__global__ void __launch_bounds__(kCommThreads)
-    allreduce_oneshot_kernel(CommCtx c, Peers in, TO* out, long n, int order, float scale) {
+__device__ __forceinline__ void allreduce_oneshot_body(CommCtx c, const Peers& in, TO* out, long n, int order, float scale) {
   if (!cta_enter(c)) return;
   for (int ch = 0; ch < c.world; ++ch) {
     long lo, hi, a, b;
@@ -423,21 +504,54 @@ __global__ void __launch_bounds__(kCommThreads)
   }
   cta_barrier(c, c.epoch + 1);
 }
+template <typename TI, typename TO, int WT>
+__global__ void __launch_bounds__(kCommThreads)
+    allreduce_oneshot_kernel(CommCtx c, Peers in, TO* out, long n, int order, float scale) {
+  DTB_SHARED_COPY(Peers, s_in, in)
+  collective_begin(c);
+  allreduce_oneshot_body<TI, TO, WT>(c, s_in, out, n, order, scale);
+  collective_end(c, 2);
+}
+
+// Fixed-order block sum of a per-thread fp64 value; thread q < W then stores it
+// into rank q's pad at [rank * stride + base + blockIdx.x].  The cta_barrier that
+// follows has the same thread q release its flag to rank q, which orders the store
+// before the peer passes that barrier.
+template <int NT>
+__device__ __forceinline__ void publish_sq(const CommCtx& c, const SqOut& sq, double s) {
+  __shared__ double red[NT / 32];
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x < c.world) {
+    double t = 0.0;
+#pragma unroll
+    for (int w = 0; w < NT / 32; ++w) t += red[w];
+    sq.p[threadIdx.x][(long)c.rank * sq.stride + sq.base + blockIdx.x] = t;
+  }
+}
 
 // Two-shot all-reduce: reduce-scatter into the owner's buffer (in place), then
 // all-gather of the reduced chunks.  `out` is this rank's destination (may be the
 // local input buffer).  in.p[rank] must be this rank's input; in-place is safe
 // because the owner only writes its own chunk, which peers do not read until the
-// middle barrier.
-template <typename T, int WT>
-__global__ void __launch_bounds__(kCommThreads)
-    allreduce_twoshot_kernel(CommCtx c, Peers in, T* out, long n, int order, float scale) {
+// middle barrier.  With `sq` the owner also publishes the sum of squares of the
+// scaled values it reduced (the DDP gradient norm comes out of the all-reduce, not
+// out of a second pass over the gradient).  LEAN: 128-thread CTAs that fit beside
+// a GEMM or attention CTA on one SM (used for buckets reduced during backward).
+template <typename T, int WT, bool LEAN>
+__device__ __forceinline__ void allreduce_twoshot_body(CommCtx c, const Peers& in, T* out, long n, int order, float scale,
+                                                       const SqOut& sq) {
   if (!cta_enter(c)) return;
   long lo, hi, a, b;
   chunk_bounds(n, c.world, c.rank, lo, hi);
   cta_slice(lo, hi, a, b);
   T* mine = reinterpret_cast<T*>(in.p[c.rank]);
-  reduce_range<T, T, WT>(in, mine, a, b, c.world, order == ORDER_CYCLIC ? c.rank : 0, scale, nullptr);
+  const bool want_sq = sq.p[0] != nullptr;
+  double s = 0.0;
+  reduce_range<T, T, WT, LEAN>(in, mine, a, b, c.world, order == ORDER_CYCLIC ? c.rank : 0, scale,
+                               want_sq ? &s : nullptr);
+  if (want_sq) publish_sq<LEAN ? kLeanThreads : kCommThreads>(c, sq, s);
   if (!cta_barrier(c, c.epoch + 1)) return;
   for (int k = 0; k < c.world; ++k) {
     const int p = (c.rank + k) % c.world;
@@ -451,14 +565,45 @@ __global__ void __launch_bounds__(kCommThreads)
   }
   cta_barrier(c, c.epoch + 2);
 }
+template <typename T, int WT, bool LEAN>
+__global__ void __maxnreg__(LEAN ? DTB_LEAN_COMM_MAXNREG : 128)
+    allreduce_twoshot_kernel(CommCtx c, Peers in, T* out, long n, int order, float scale, SqOut sq) {
+  DTB_SHARED_COPY(Peers, s_in, in)
+  DTB_SHARED_COPY(SqOut, s_sq, sq)
+  if (threadIdx.x == 0) {
+    s_sq.base = sq.base;
+    s_sq.stride = sq.stride;
+  }
+  collective_begin(c);
+  allreduce_twoshot_body<T, WT, LEAN>(c, s_in, out, n, order, scale, s_sq);
+  collective_end(c, 3);
+}
+
+// Sum of fp64 partials pad[r * stride + s] over ranks r < world and slots
+// lo <= s < hi, in a fixed order (thread t sums the linear indices t, t+1024, ...
+// of that range in order, then a fixed shuffle tree): the same bits on every rank.
+__global__ void __launch_bounds__(1024)
+    sq_total_kernel(const double* pad, int world, long stride, long lo, long hi, double* out) {
+  __shared__ double red[32];
+  const long len = hi - lo, n = (long)world * len;
+  double s = 0.0;
+  for (long i = threadIdx.x; i < n; i += blockDim.x) s += __ldcg(pad + (i / len) * stride + lo + i % len);
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int w = 0; w < 32; ++w) t += red[w];
+    out[0] = t;
+  }
+}
 
 // Reduce-scatter: chunk `rank` summed in cyclic order from `rank` (bit-equal to
 // dtrain's ring reduce-scatter with rotation, comm.py:310-316,342-362), scaled,
 // written to `out` (this rank's buffer index space).  With sq_part, each CTA also
 // writes the fp64 sum of squares of its slice to sq_part[blockIdx.x].
 template <typename TI, typename TO, int WT>
-__global__ void __launch_bounds__(kCommThreads)
-    reduce_scatter_kernel(CommCtx c, Peers in, TO* out, long n, int order, float scale, double* sq_part) {
+__device__ __forceinline__ void reduce_scatter_body(CommCtx c, const Peers& in, TO* out, long n, int order, float scale, double* sq_part) {
   __shared__ double red[kCommThreads / 32];
   if (!cta_enter(c)) return;
   long lo, hi, a, b;
@@ -480,10 +625,18 @@ __global__ void __launch_bounds__(kCommThreads)
   }
   cta_barrier(c, c.epoch + 1);
 }
+template <typename TI, typename TO, int WT>
+__global__ void __launch_bounds__(kCommThreads)
+    reduce_scatter_kernel(CommCtx c, Peers in, TO* out, long n, int order, float scale, double* sq_part) {
+  DTB_SHARED_COPY(Peers, s_in, in)
+  collective_begin(c);
+  reduce_scatter_body<TI, TO, WT>(c, s_in, out, n, order, scale, sq_part);
+  collective_end(c, 2);
+}
 
 // All-gather in place: every rank copies chunk p from rank p into `out`.
 template <typename T>
-__global__ void __launch_bounds__(kCommThreads) all_gather_kernel(CommCtx c, Peers in, T* out, long n) {
+__device__ __forceinline__ void all_gather_body(CommCtx c, const Peers& in, T* out, long n) {
   if (!cta_enter(c)) return;
   for (int k = 1; k < c.world; ++k) {
     const int p = (c.rank + k) % c.world;
@@ -494,11 +647,18 @@ __global__ void __launch_bounds__(kCommThreads) all_gather_kernel(CommCtx c, Pee
   }
   cta_barrier(c, c.epoch + 1);
 }
+template <typename T>
+__global__ void __launch_bounds__(kCommThreads)
+    all_gather_kernel(CommCtx c, Peers in, T* out, long n) {
+  DTB_SHARED_COPY(Peers, s_in, in)
+  collective_begin(c);
+  all_gather_body<T>(c, s_in, out, n);
+  collective_end(c, 2);
+}
 
 // Broadcast from `root`: non-root ranks pull root's buffer into `out` (with an
 // optional fp32 -> bf16 cast into out16 on every rank, root included).
-__global__ void __launch_bounds__(kCommThreads)
-    broadcast_kernel(CommCtx c, Peers in, void* out, long nbytes, int root, const float* cast_src, bf16* out16,
+__device__ __forceinline__ void broadcast_body(CommCtx c, const Peers& in, void* out, long nbytes, int root, const float* cast_src, bf16* out16,
                      long n16) {
   if (!cta_enter(c)) return;
   if (c.rank != root && out) {
@@ -513,8 +673,20 @@ __global__ void __launch_bounds__(kCommThreads)
     for (long i = a + threadIdx.x; i < b; i += blockDim.x) out16[i] = f2bf(cast_src[i]);
   }
 }
+__global__ void __launch_bounds__(kCommThreads)
+    broadcast_kernel(CommCtx c, Peers in, void* out, long nbytes, int root, const float* cast_src, bf16* out16,
+                     long n16) {
+  DTB_SHARED_COPY(Peers, s_in, in)
+  collective_begin(c);
+  broadcast_body(c, s_in, out, nbytes, root, cast_src, out16, n16);
+  collective_end(c, 2);
+}
 
-__global__ void barrier_kernel(CommCtx c) { cta_enter(c); }
+__global__ void barrier_kernel(CommCtx c) {
+  collective_begin(c);
+  cta_enter(c);
+  collective_end(c, 1);
+}
 
 // ZeRO-1 update, fused with the global-norm exchange and the parameter all-gather.
 // Phase 1: every CTA sums all ranks' per-CTA squared-norm partials (written by
@@ -528,9 +700,8 @@ __global__ void barrier_kernel(CommCtx c) { cta_enter(c); }
 //          the forward GEMMs that gather them tile by tile (gemm.cu, gemm_gather),
 //          which start pulling once `gen_out` (written here) moves past the
 //          generation they last gathered.
-__global__ void __launch_bounds__(kCommThreads)
-    zero_adamw_allgather_kernel(CommCtx c, Sigs sq_parts, int nparts, float* master, const float* grad,
-                                float* m, float* v, Peers work16, Peers master32, long n, AdamConsts ak,
+__device__ __forceinline__ void zero_adamw_allgather_body(CommCtx c, const Sigs& sq_parts, int nparts, float* master, const float* grad,
+                                float* m, float* v, const Peers& work16, const Peers& master32, long n, AdamConsts ak,
                                 float max_norm, double* sq_out, int gather_master, const long* keep, int nkeep,
                                 int* gen_out) {
   __shared__ float s_clip;
@@ -585,6 +756,18 @@ __global__ void __launch_bounds__(kCommThreads)
   }
   cta_barrier(c, c.epoch + 2);
 }
+__global__ void __launch_bounds__(kCommThreads)
+    zero_adamw_allgather_kernel(CommCtx c, Sigs sq_parts, int nparts, float* master, const float* grad,
+                                float* m, float* v, Peers work16, Peers master32, long n, AdamConsts ak,
+                                float max_norm, double* sq_out, int gather_master, const long* keep, int nkeep,
+                                int* gen_out) {
+  DTB_SHARED_COPY(Sigs, s_sq_parts, sq_parts)
+  DTB_SHARED_COPY(Peers, s_work16, work16)
+  DTB_SHARED_COPY(Peers, s_master32, master32)
+  collective_begin(c);
+  zero_adamw_allgather_body(c, s_sq_parts, nparts, master, grad, m, v, s_work16, s_master32, n, ak, max_norm, sq_out, gather_master, keep, nkeep, gen_out);
+  collective_end(c, 3);
+}
 
 // Grid-wide barrier across ranks: returns once every CTA of every rank has arrived
 // at `epoch`.  CTA b of rank r publishes slot [b][r] in every rank's signal pad
@@ -598,14 +781,18 @@ __device__ bool grid_barrier(const CommCtx& c, uint32_t epoch) {
   __syncthreads();
   if (threadIdx.x < c.world) {
     __threadfence_system();
-    st_release_sys(c.sig.p[threadIdx.x] + blockIdx.x * kMaxRanks + c.rank, epoch);
+    st_release_sys(c.sp->p[threadIdx.x] + blockIdx.x * kMaxRanks + c.rank, epoch);
   }
   const int slots = (int)gridDim.x * c.world;
   for (int t = threadIdx.x; t < slots; t += blockDim.x) {
-    const uint32_t* f = c.sig.p[c.rank] + (t / c.world) * kMaxRanks + (t % c.world);
+    const uint32_t* f = c.sp->p[c.rank] + (t / c.world) * kMaxRanks + (t % c.world);
     uint64_t t0 = 0;
     for (uint32_t i = 0;; ++i) {
-      if ((int)(ld_acquire_sys(f) - epoch) >= 0) break;
+      if ((int)(ld_relaxed_sys(f) - epoch) >= 0) {
+        fence_acquire_sys();
+        break;
+      }
+      if (i >= 16u) __nanosleep(128);
       if ((i & 63u) == 0u) {
         if (*reinterpret_cast<volatile int*>(&failed)) break;
         const uint64_t now = globaltimer_ns();
@@ -638,9 +825,8 @@ __device__ bool grid_barrier(const CommCtx& c, uint32_t epoch) {
 //          optionally of the fp32 masters; a last barrier keeps this rank's
 //          partition unchanged until every peer has pulled it.
 template <int WT>
-__global__ void __launch_bounds__(kCommThreads)
-    zero_rs_adamw_kernel(CommCtx c, Peers grads, Sigs sq_parts, float* master, float* m, float* v, Peers work16,
-                         Peers master32, long n, AdamConsts ak, float scale, float max_norm, double* sq_out,
+__device__ __forceinline__ void zero_rs_adamw_body(CommCtx c, const Peers& grads, const Sigs& sq_parts, float* master, float* m, float* v, const Peers& work16,
+                         const Peers& master32, long n, AdamConsts ak, float scale, float max_norm, double* sq_out,
                          int gather_master, const long* keep, int nkeep, int* gen_out) {
   __shared__ double red[kCommThreads / 32];
   __shared__ float s_clip;
@@ -707,6 +893,19 @@ __global__ void __launch_bounds__(kCommThreads)
   }
   cta_barrier(c, c.epoch + 3);
 }
+template <int WT>
+__global__ void __launch_bounds__(kCommThreads)
+    zero_rs_adamw_kernel(CommCtx c, Peers grads, Sigs sq_parts, float* master, float* m, float* v, Peers work16,
+                         Peers master32, long n, AdamConsts ak, float scale, float max_norm, double* sq_out,
+                         int gather_master, const long* keep, int nkeep, int* gen_out) {
+  DTB_SHARED_COPY(Peers, s_grads, grads)
+  DTB_SHARED_COPY(Sigs, s_sq_parts, sq_parts)
+  DTB_SHARED_COPY(Peers, s_work16, work16)
+  DTB_SHARED_COPY(Peers, s_master32, master32)
+  collective_begin(c);
+  zero_rs_adamw_body<WT>(c, s_grads, s_sq_parts, master, m, v, s_work16, s_master32, n, ak, scale, max_norm, sq_out, gather_master, keep, nkeep, gen_out);
+  collective_end(c, 4);
+}
 
 // ---------------------------------------------------------------- host side
 // Symmetric allocation: cudaMalloc + IPC export.  Returns (ptr, handle bytes).
@@ -766,8 +965,7 @@ static uint32_t op_tag(uint32_t kind, int64_t n, int64_t dtype) {
   return (uint32_t)(h ^ (h >> 32));
 }
 
-static CommCtx make_ctx(const std::vector<int64_t>& sigs, int64_t rank, int64_t epoch, double timeout_s,
-                        uint32_t tag) {
+static CommCtx make_ctx(const std::vector<int64_t>& sigs, int64_t rank, double timeout_s, uint32_t tag) {
   ensure_status();
   CommCtx c{};
   const int W = (int)sigs.size();
@@ -776,7 +974,7 @@ static CommCtx make_ctx(const std::vector<int64_t>& sigs, int64_t rank, int64_t 
   for (int i = 0; i < W; ++i) c.sig.p[i] = reinterpret_cast<uint32_t*>(sigs[i]);
   c.rank = (int)rank;
   c.world = W;
-  c.epoch = (uint32_t)epoch;
+  c.epoch = 0;  // read from the rank's epoch counter by collective_begin()
   c.tag = tag;
   c.timeout_ns = (uint64_t)(timeout_s * 1e9);
   c.host_status = g_dev_status;
@@ -789,24 +987,82 @@ static Peers make_peers(const std::vector<int64_t>& ptrs, int64_t byte_offset) {
   return p;
 }
 
-static int comm_blocks(long bytes, int64_t want) {
-  if (want > 0) return (int)std::min<int64_t>(want, kMaxCommBlocks);
-  const long per = 64 * 1024;  // ~64 KB per CTA before adding more CTAs
-  return (int)std::max<long>(1, std::min<long>(kMaxCommBlocks / 2, (bytes + per - 1) / per));
+// A lean kernel's CTAs must be able to share an SM with a GEMM CTA that uses
+// ~226 KB of shared memory.  An SM's L1/shared split is set for the CTAs it runs,
+// and a kernel with almost no shared memory would by default get a small shared
+// carve-out - a GEMM CTA then cannot join that SM until the comm CTA leaves.  So
+// lean kernels ask for the maximum shared carve-out (once per kernel).
+template <typename K>
+static void prefer_max_shared(K* kern) {
+  static bool done = false;
+  if (!done) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                        (int)cudaSharedmemCarveoutMaxShared));
+    done = true;
+  }
 }
 
-// Every collective returns the number of epochs it consumed; the caller adds it
-// to its epoch counter (identically on every rank).
-int64_t allreduce(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> bufs,
-                  int64_t byte_offset, int64_t n, int64_t in_dtype, int64_t out_ptr, int64_t out_dtype, int64_t algo,
-                  int64_t order, double scale, double timeout_s, int64_t blocks) {
-  CommCtx c = make_ctx(sigs, rank, epoch, timeout_s, op_tag(1 + (uint32_t)algo, n, in_dtype * 8 + out_dtype));
+// Device-side timestamps for tracing a step: one thread writes %globaltimer (ns,
+// the same clock on every SM) into buf[slot] when the stream reaches it.
+__global__ void stamp_kernel(int64_t* slot) { *slot = (int64_t)globaltimer_ns(); }
+
+void stamp(torch::Tensor buf, int64_t slot) {
+  TORCH_CHECK(buf.is_cuda() && buf.scalar_type() == at::kLong && slot >= 0 && slot < buf.numel(),
+              "stamp: int64 CUDA buffer and a slot inside it");
+  stamp_kernel<<<1, 1, 0, at::cuda::getCurrentCUDAStream()>>>(buf.data_ptr<int64_t>() + slot);
+  count_launch();
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// CTAs of a full-width collective: ~64 KB per CTA, at most 64 CTAs, unless the
+// caller asks for a count.
+static int comm_blocks(long bytes, int64_t want) {
+  if (want > 0) return (int)std::min<int64_t>(want, kMaxCommBlocks);
+  const long per = 64 * 1024;
+  return (int)std::max<long>(1, std::min<long>(64, (bytes + per - 1) / per));
+}
+
+// CTAs of a lean collective (one 128-thread CTA beside each SM's resident
+// kernel): ~16 KB per CTA, at most one per SM.
+static int lean_blocks(long bytes, int64_t want) {
+  if (want > 0) return (int)std::min<int64_t>(want, kMaxCommBlocks);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const long per = 16 * 1024;
+  return (int)std::max<long>(1, std::min<long>(std::min(sms, kMaxCommBlocks), (bytes + per - 1) / per));
+}
+
+int64_t collective_blocks(int64_t nbytes, int64_t want, bool lean) {
+  return lean ? lean_blocks(nbytes, want) : comm_blocks(nbytes, want);
+}
+
+static SqOut make_sq(const std::vector<int64_t>& pads, int64_t base, int64_t stride, int W, int nb) {
+  SqOut s{};
+  if (pads.empty()) return s;
+  TORCH_CHECK((int)pads.size() == W, "allreduce: one sum-of-squares pad per rank expected");
+  TORCH_CHECK(base >= 0 && stride > 0 && base + nb <= stride, "allreduce: sum-of-squares slots [", base, ", ",
+              base + nb, ") exceed the per-rank stride ", stride);
+  for (int i = 0; i < W; ++i) s.p[i] = reinterpret_cast<double*>(pads[i]);
+  s.base = (int)base;
+  s.stride = (int)stride;
+  return s;
+}
+
+// Every collective launches one kernel on the current stream and returns its CTA
+// count.  Flag epochs come from the device counter (see collective_begin).
+int64_t allreduce(std::vector<int64_t> sigs, int64_t rank, std::vector<int64_t> bufs, int64_t byte_offset, int64_t n,
+                  int64_t in_dtype, int64_t out_ptr, int64_t out_dtype, int64_t algo, int64_t order, double scale,
+                  double timeout_s, int64_t blocks, bool lean, std::vector<int64_t> sq_pads, int64_t sq_base,
+                  int64_t sq_stride) {
+  CommCtx c = make_ctx(sigs, rank, timeout_s, op_tag(1 + (uint32_t)algo, n, in_dtype * 8 + out_dtype));
   Peers in = make_peers(bufs, byte_offset);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   const long esz = in_dtype == DT_F32 ? 4 : 2;
-  const int nb = comm_blocks(n * esz, blocks);
+  const int nb = lean ? lean_blocks(n * esz, blocks) : comm_blocks(n * esz, blocks);
   if (algo == 0) {  // one-shot, out-of-place
     TORCH_CHECK(out_ptr != 0, "allreduce one-shot needs an output buffer");
+    TORCH_CHECK(!lean && sq_pads.empty(), "allreduce one-shot: no lean variant and no sum of squares");
     const int od = (int)order;
     const float sc = (float)scale;
     if (in_dtype == DT_F32 && out_dtype == DT_F32) {
@@ -825,30 +1081,61 @@ int64_t allreduce(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::v
       TORCH_CHECK(false, "allreduce: unsupported dtype pair");
     count_launch();
     C10_CUDA_KERNEL_LAUNCH_CHECK();
-    return 2;
+    return nb;
   }
   TORCH_CHECK(in_dtype == out_dtype, "allreduce two-shot: in/out dtypes must match");
   void* out = out_ptr ? reinterpret_cast<void*>(out_ptr) : in.p[rank];
+  const SqOut sq = make_sq(sq_pads, sq_base, sq_stride, c.world, nb);
+  const int od = (int)order;
+  const float sc = (float)scale;
+  const int nt = lean ? kLeanThreads : kCommThreads;
+#define DTB_TWOSHOT(T, WTV, LN)                                                           \
+  do {                                                                                    \
+    if (LN) prefer_max_shared(allreduce_twoshot_kernel<T, WTV, LN>);                      \
+    allreduce_twoshot_kernel<T, WTV, LN><<<nb, nt, 0, st>>>(c, in, reinterpret_cast<T*>(out), n, od, sc, sq); \
+  } while (0)
   if (in_dtype == DT_F32) {
-    auto* o = reinterpret_cast<float*>(out);
-    switch (c.world) {
-      case 2: allreduce_twoshot_kernel<float, 2><<<nb, kCommThreads, 0, st>>>(c, in, o, n, (int)order, (float)scale); break;
-      case 4: allreduce_twoshot_kernel<float, 4><<<nb, kCommThreads, 0, st>>>(c, in, o, n, (int)order, (float)scale); break;
-      case 8: allreduce_twoshot_kernel<float, 8><<<nb, kCommThreads, 0, st>>>(c, in, o, n, (int)order, (float)scale); break;
-      default: allreduce_twoshot_kernel<float, 0><<<nb, kCommThreads, 0, st>>>(c, in, o, n, (int)order, (float)scale);
+    if (lean) {
+      switch (c.world) {
+        case 2: DTB_TWOSHOT(float, 2, true); break;
+        case 4: DTB_TWOSHOT(float, 4, true); break;
+        case 8: DTB_TWOSHOT(float, 8, true); break;
+        default: DTB_TWOSHOT(float, 0, true);
+      }
+    } else {
+      switch (c.world) {
+        case 2: DTB_TWOSHOT(float, 2, false); break;
+        case 4: DTB_TWOSHOT(float, 4, false); break;
+        case 8: DTB_TWOSHOT(float, 8, false); break;
+        default: DTB_TWOSHOT(float, 0, false);
+      }
     }
+  } else if (lean) {
+    DTB_TWOSHOT(bf16, 0, true);
   } else {
-    allreduce_twoshot_kernel<bf16, 0><<<nb, kCommThreads, 0, st>>>(c, in, reinterpret_cast<bf16*>(out), n, (int)order, (float)scale);
+    DTB_TWOSHOT(bf16, 0, false);
   }
+#undef DTB_TWOSHOT
   count_launch();
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  return 3;
+  return nb;
 }
 
-int64_t reduce_scatter(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> bufs,
+void sq_total(torch::Tensor pad, torch::Tensor out, int64_t world, int64_t stride, int64_t lo, int64_t hi) {
+  TORCH_CHECK(pad.is_cuda() && pad.scalar_type() == at::kDouble && pad.is_contiguous(), "sq_total: fp64 CUDA pad");
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kDouble && out.numel() >= 1, "sq_total: fp64 CUDA out");
+  TORCH_CHECK(world >= 1 && 0 <= lo && lo < hi && hi <= stride && world * stride <= pad.numel(),
+              "sq_total: slots [", lo, ", ", hi, ") x ", world, " ranks do not fit a pad of ", pad.numel());
+  sq_total_kernel<<<1, 1024, 0, at::cuda::getCurrentCUDAStream()>>>(pad.data_ptr<double>(), (int)world, stride, lo,
+                                                                     hi, out.data_ptr<double>());
+  count_launch();
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+int64_t reduce_scatter(std::vector<int64_t> sigs, int64_t rank, std::vector<int64_t> bufs,
                        int64_t byte_offset, int64_t n, int64_t dtype, int64_t out_ptr, int64_t order, double scale,
                        int64_t sq_part_ptr, double timeout_s, int64_t blocks) {
-  CommCtx c = make_ctx(sigs, rank, epoch, timeout_s, op_tag(4, n, dtype));
+  CommCtx c = make_ctx(sigs, rank, timeout_s, op_tag(4, n, dtype));
   Peers in = make_peers(bufs, byte_offset);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   const int nb = comm_blocks(n * (dtype == DT_F32 ? 4 : 2), blocks);
@@ -869,12 +1156,12 @@ int64_t reduce_scatter(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, s
   }
   count_launch();
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  return 2;
+  return nb;
 }
 
-int64_t all_gather(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> bufs,
+int64_t all_gather(std::vector<int64_t> sigs, int64_t rank, std::vector<int64_t> bufs,
                    int64_t byte_offset, int64_t n, int64_t dtype, double timeout_s, int64_t blocks) {
-  CommCtx c = make_ctx(sigs, rank, epoch, timeout_s, op_tag(5, n, dtype));
+  CommCtx c = make_ctx(sigs, rank, timeout_s, op_tag(5, n, dtype));
   Peers in = make_peers(bufs, byte_offset);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   const int nb = comm_blocks(n * (dtype == DT_F32 ? 4 : 2), blocks);
@@ -884,13 +1171,13 @@ int64_t all_gather(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::
     all_gather_kernel<bf16><<<nb, kCommThreads, 0, st>>>(c, in, reinterpret_cast<bf16*>(in.p[rank]), n);
   count_launch();
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  return 2;
+  return nb;
 }
 
-int64_t broadcast(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> bufs,
+int64_t broadcast(std::vector<int64_t> sigs, int64_t rank, std::vector<int64_t> bufs,
                   int64_t byte_offset, int64_t nbytes, int64_t root, int64_t cast_src, int64_t out16, int64_t n16,
                   double timeout_s, int64_t blocks) {
-  CommCtx c = make_ctx(sigs, rank, epoch, timeout_s, op_tag(6, nbytes, root));
+  CommCtx c = make_ctx(sigs, rank, timeout_s, op_tag(6, nbytes, root));
   Peers in = make_peers(bufs, byte_offset);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   const int nb = comm_blocks(nbytes, blocks);
@@ -899,25 +1186,26 @@ int64_t broadcast(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::v
                                                 reinterpret_cast<bf16*>(out16), n16);
   count_launch();
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  return 2;
+  return nb;
 }
 
-int64_t device_barrier(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, double timeout_s) {
-  CommCtx c = make_ctx(sigs, rank, epoch, timeout_s, op_tag(7, 0, 0));
-  barrier_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(c);
+int64_t device_barrier(std::vector<int64_t> sigs, int64_t rank, double timeout_s) {
+  CommCtx c = make_ctx(sigs, rank, timeout_s, op_tag(7, 0, 0));
+  const int nb = 1;
+  barrier_kernel<<<nb, 32, 0, at::cuda::getCurrentCUDAStream()>>>(c);
   count_launch();
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  return 1;
+  return nb;
 }
 
-int64_t zero_adamw_allgather(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> sq_parts,
+int64_t zero_adamw_allgather(std::vector<int64_t> sigs, int64_t rank, std::vector<int64_t> sq_parts,
                              int64_t nparts, torch::Tensor master, torch::Tensor grad, torch::Tensor m,
                              torch::Tensor v, std::vector<int64_t> work16, std::vector<int64_t> master32, int64_t n,
                              double lr, double b1, double b2, double eps, double wd, int64_t t, double max_norm,
                              c10::optional<torch::Tensor> sq_out, bool gather_master, double timeout_s,
                              int64_t blocks, c10::optional<torch::Tensor> keep, c10::optional<torch::Tensor> gen_word) {
   const int64_t nkeep_tag = (keep && keep->defined()) ? keep->size(0) + 1 : 0;
-  CommCtx c = make_ctx(sigs, rank, epoch, timeout_s, op_tag(8, n, (gather_master ? 1 : 0) + 2 * nkeep_tag));
+  CommCtx c = make_ctx(sigs, rank, timeout_s, op_tag(8, n, (gather_master ? 1 : 0) + 2 * nkeep_tag));
   Sigs sp{};
   for (size_t i = 0; i < sq_parts.size(); ++i) sp.p[i] = reinterpret_cast<uint32_t*>(sq_parts[i]);
   Peers w16 = make_peers(work16, 0), m32 = make_peers(master32, 0);
@@ -943,20 +1231,20 @@ int64_t zero_adamw_allgather(std::vector<int64_t> sigs, int64_t rank, int64_t ep
       w16, m32, n, ak, (float)max_norm, sqo, gather_master ? 1 : 0, kp, nkeep, gw);
   count_launch();
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  return 3;
+  return nb;
 }
 
 // One-kernel ZeRO-1 step (zero_rs_adamw_kernel).  `grads` are every rank's
 // addresses of the flat fp32 gradient, `sq_parts` every rank's fp64 pad of at least
-// `blocks` (or 64) slots.  Returns the epochs consumed.
-int64_t zero_rs_adamw(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, std::vector<int64_t> grads,
+// `blocks` (or 64) slots.  Returns the CTA count.
+int64_t zero_rs_adamw(std::vector<int64_t> sigs, int64_t rank, std::vector<int64_t> grads,
                       std::vector<int64_t> sq_parts, torch::Tensor master, torch::Tensor m, torch::Tensor v,
                       std::vector<int64_t> work16, std::vector<int64_t> master32, int64_t n, double lr, double b1,
                       double b2, double eps, double wd, int64_t t, double scale, double max_norm,
                       c10::optional<torch::Tensor> sq_out, bool gather_master, double timeout_s, int64_t blocks,
                       c10::optional<torch::Tensor> keep, c10::optional<torch::Tensor> gen_word) {
   const int64_t nkeep_tag = (keep && keep->defined()) ? keep->size(0) + 1 : 0;
-  CommCtx c = make_ctx(sigs, rank, epoch, timeout_s, op_tag(9, n, (gather_master ? 1 : 0) + 2 * nkeep_tag));
+  CommCtx c = make_ctx(sigs, rank, timeout_s, op_tag(9, n, (gather_master ? 1 : 0) + 2 * nkeep_tag));
   TORCH_CHECK(grads.size() == sigs.size() && sq_parts.size() == sigs.size(), "zero_rs_adamw: one pointer per rank");
   Sigs sp{};
   for (size_t i = 0; i < sq_parts.size(); ++i) sp.p[i] = reinterpret_cast<uint32_t*>(sq_parts[i]);
@@ -996,12 +1284,12 @@ int64_t zero_rs_adamw(std::vector<int64_t> sigs, int64_t rank, int64_t epoch, st
 #undef DTB_ZRA
   count_launch();
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  return 4;
+  return nb;
 }
 
 // Native per-group state so a collective on a peer-mapped tensor costs one call
 // from Python: the registered buffers (every rank's base pointer), the signal
-// pads, the flag epoch counter and the timeout live here.
+// pads and the timeout live here (the flag epoch counter lives on the device).
 CommEngine::CommEngine(int64_t rank, int64_t world, std::vector<int64_t> sigs, double timeout_s, int64_t blocks)
     : rank_(rank), world_(world), sigs_(std::move(sigs)), timeout_(timeout_s), blocks_(blocks) {}
 
@@ -1042,19 +1330,35 @@ static int64_t dt_code(const torch::Tensor& t) {
   return DT_BF16;
 }
 
-void CommEngine::allreduce_inplace(torch::Tensor t, int64_t order, double scale) {
+int64_t CommEngine::allreduce_inplace(torch::Tensor t, int64_t order, double scale, int64_t blocks, bool lean,
+                                      c10::optional<torch::Tensor> sq_pad, int64_t sq_base, int64_t sq_stride) {
   int64_t id, off;
   TORCH_CHECK(t.is_contiguous() && locate(t, id, off), "allreduce_inplace: tensor is not in a registered buffer");
-  epoch_ += dtb::allreduce(sigs_, rank_, epoch_, bufs_[id], off, t.numel(), dt_code(t), 0, dt_code(t), 1, order,
-                           scale, timeout_, blocks_);
+  std::vector<int64_t> pads;
+  if (sq_pad && sq_pad->defined()) {
+    TORCH_CHECK(sq_pad->scalar_type() == at::kDouble, "allreduce_inplace: the sum-of-squares pad must be fp64");
+    pads = peer_ptrs(*sq_pad);
+    TORCH_CHECK(sq_pad->numel() >= world_ * sq_stride, "allreduce_inplace: sum-of-squares pad too small");
+  }
+  ++issued_;
+  return dtb::allreduce(sigs_, rank_, bufs_[id], off, t.numel(), dt_code(t), 0, dt_code(t), 1, order, scale, timeout_,
+                        blocks > 0 ? blocks : blocks_, lean, pads, sq_base, sq_stride);
+}
+
+int64_t CommEngine::device_epoch() const {
+  uint32_t v = 0;
+  C10_CUDA_CHECK(cudaMemcpy(&v, reinterpret_cast<const uint32_t*>(sigs_[rank_]) + kCtrWord, sizeof(v),
+                            cudaMemcpyDeviceToHost));
+  return (int64_t)v;
 }
 
 torch::Tensor CommEngine::reduce_scatter(torch::Tensor flat, int64_t order, double scale, int64_t sq_part_ptr,
                                          int64_t blocks) {
   int64_t id, off;
   TORCH_CHECK(flat.is_contiguous() && locate(flat, id, off), "reduce_scatter: tensor is not in a registered buffer");
-  epoch_ += dtb::reduce_scatter(sigs_, rank_, epoch_, bufs_[id], off, flat.numel(), dt_code(flat), 0, order, scale,
-                                sq_part_ptr, timeout_, blocks > 0 ? blocks : blocks_);
+  ++issued_;
+  dtb::reduce_scatter(sigs_, rank_, bufs_[id], off, flat.numel(), dt_code(flat), 0, order, scale, sq_part_ptr, timeout_,
+                      blocks > 0 ? blocks : blocks_);
   const int64_t n = flat.numel(), base = n / world_, extra = n % world_;
   const int64_t lo = rank_ * base + std::min(rank_, extra);
   return flat.narrow(0, lo, base + (rank_ < extra ? 1 : 0));
@@ -1063,10 +1367,14 @@ torch::Tensor CommEngine::reduce_scatter(torch::Tensor flat, int64_t order, doub
 void CommEngine::all_gather(torch::Tensor flat) {
   int64_t id, off;
   TORCH_CHECK(flat.is_contiguous() && locate(flat, id, off), "all_gather: tensor is not in a registered buffer");
-  epoch_ += dtb::all_gather(sigs_, rank_, epoch_, bufs_[id], off, flat.numel(), dt_code(flat), timeout_, blocks_);
+  ++issued_;
+  dtb::all_gather(sigs_, rank_, bufs_[id], off, flat.numel(), dt_code(flat), timeout_, blocks_);
 }
 
-void CommEngine::barrier() { epoch_ += dtb::device_barrier(sigs_, rank_, epoch_, timeout_); }
+void CommEngine::barrier() {
+  ++issued_;
+  dtb::device_barrier(sigs_, rank_, timeout_);
+}
 
 std::vector<int64_t> CommEngine::peer_ptrs(torch::Tensor t) const {
   int64_t id, off;

@@ -18,15 +18,23 @@ class CommEngine {
   bool contains(torch::Tensor t) const;
   std::vector<int64_t> peer_ptrs(torch::Tensor t) const;
 
-  // In-place two-shot all-reduce of a tensor inside a registered buffer.
-  void allreduce_inplace(torch::Tensor t, int64_t order, double scale);
+  // In-place two-shot all-reduce of a tensor inside a registered buffer; returns the
+  // CTA count.  `blocks` 0 sizes the grid by the message; `lean` selects the
+  // 128-thread CTAs that run beside a GEMM; with `sq_pad` (an fp64 registered
+  // buffer of world * sq_stride slots) CTA b also publishes the sum of squares of
+  // its reduced slice into slot [rank * sq_stride + sq_base + b] of every rank's pad.
+  int64_t allreduce_inplace(torch::Tensor t, int64_t order, double scale, int64_t blocks, bool lean,
+                            c10::optional<torch::Tensor> sq_pad, int64_t sq_base, int64_t sq_stride);
   // Returns this rank's partition of `flat` (holding the reduced values).
   torch::Tensor reduce_scatter(torch::Tensor flat, int64_t order, double scale, int64_t sq_part_ptr, int64_t blocks);
   void all_gather(torch::Tensor flat);
   void barrier();
 
-  int64_t epoch() const { return epoch_; }
-  void advance(int64_t n) { epoch_ += n; }
+  // Collectives issued through this engine (host count; graph replays not included).
+  int64_t issued() const { return issued_; }
+  void note_issued() { ++issued_; }
+  // The rank's device epoch counter (synchronous read: for tests and diagnostics).
+  int64_t device_epoch() const;
   double timeout() const { return timeout_; }
   void set_timeout(double t) { timeout_ = t; }
   int64_t blocks() const { return blocks_; }
@@ -38,7 +46,7 @@ class CommEngine {
   std::vector<int64_t> sigs_;
   double timeout_;
   int64_t blocks_;
-  int64_t epoch_ = 1;
+  int64_t issued_ = 0;
   std::vector<std::vector<int64_t>> bufs_;
   std::vector<int64_t> sizes_;
 };

@@ -52,6 +52,18 @@ __device__ __forceinline__ void set_status(int code) {
   atomicCAS(&g_dtb_status, 0, code);
 }
 
+// Register caps that let a lean collective CTA (4 warps, csrc/comm.cu) share an SM
+// with the 320-thread tensor-core kernels.  An SM's register file is four 16K-
+// register banks, one per warp scheduler, and warp w of a CTA lives in bank w % 4,
+// so a 10-warp CTA puts three warps in two of the banks and the lean CTA needs one
+// warp's worth of registers in every bank.  168 registers a thread (the most that
+// three warps of a bank can hold) leave nothing; the GEMM at 144 keeps
+// 16384 - 3*144*32 = 2560 free and the attention kernels (which spill below 152)
+// at 152 keep 1792 = one 56-register lean warp.
+#define DTB_CORESIDENT_MAXNREG 144
+#define DTB_CORESIDENT_MAXNREG_ATTN 152
+#define DTB_LEAN_COMM_MAXNREG 56
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

@@ -430,7 +430,7 @@ __device__ __forceinline__ void gather_exit(const GatherArgs& g, int kb_total, i
 }
 
 template <int BN, bool A_MN, bool B_MN, bool GATHER = false>
-__global__ void __launch_bounds__(GATHER ? kThreads + kGatherWarps * 32 : kThreads, 1)
+__global__ void __maxnreg__(DTB_CORESIDENT_MAXNREG)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmAux,
                    GemmArgs args) {
@@ -650,7 +650,7 @@ struct Gemm2Cfg {
 };
 
 template <bool A_MN, bool B_MN, bool GATHER = false>
-__global__ void __launch_bounds__(GATHER ? kThreads + kGatherWarps * 32 : kThreads, 1)
+__global__ void __maxnreg__(DTB_CORESIDENT_MAXNREG)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmAux,
                     GemmArgs args) {

@@ -147,6 +147,11 @@ class GPT(nn.Module):
             ws += [b.qkv.w, b.proj.w, b.fc.w, b.out.w]
         return ws + [self.head.w]
 
+    def late_grad_params(self):
+        """Parameters whose gradients the last backward kernel (the embedding
+        backward) produces: DDP reduces their buckets after backward has finished."""
+        return [self.tok, self.pos]
+
     def named_parameters_list(self):
         return list(self.named_parameters())
 

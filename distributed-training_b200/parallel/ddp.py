@@ -20,8 +20,19 @@ of the flat gradient that the backward kernels already wrote.  The bucket
 all-reduce is one kernel (``csrc/comm.cu``) on the comm stream that reads the
 peers' slices over NVLink, sums them in the fixed order, multiplies by 1/W and
 writes the result in place - the reference's copy-in, all-reduce, scale and
-copy-out (dtrain/ddp.py:73-110) collapse into that kernel.  ``finish()`` only
-makes the compute stream wait for the comm stream; no host synchronisation.
+copy-out (dtrain/ddp.py:73-110) collapse into that kernel.  The same kernel
+publishes the sum of squares of what it reduced, so the gradient norm for
+clipping (dtrain/train.py:155-158) costs no second pass: ``finish()`` makes the
+compute stream wait for the comm stream and sums those partials in a fixed order
+into ``sq_norm``; no host synchronisation.
+
+Buckets reduced while backward is still running use lean 128-thread CTAs, which
+fit beside the GEMM and attention CTAs on each SM instead of holding SMs those
+persistent kernels need; buckets whose gradients come from the last backward
+kernel (the embeddings, ``model.late_grad_params()``) have the GPU to themselves
+and use full-width CTAs.  The launches are the same every step (the flag epochs
+live on the device), so the whole forward + backward + bucket all-reduces can be
+captured in one CUDA graph (``Trainer --cuda-graph``).
 
 Host path (``pg`` is a TCP ``ProcessGroup``): the reference algorithm on host
 buffers, used by CPU ranks and the float64 oracle tests.
@@ -29,10 +40,15 @@ buffers, used by CPU ranks and the float64 oracle tests.
 from __future__ import annotations
 
 import contextlib
+import os
 import time
 
 import numpy as np
 import torch
+
+# Upper bound on the CTAs of a bucket all-reduce that runs during backward
+# (0: one per SM at most, sized by the bucket).
+LEAN_BLOCKS = int(os.environ.get("DTB_DDP_LEAN_BLOCKS", "0"))
 
 
 class _Bucket:
@@ -43,6 +59,9 @@ class _Bucket:
         self.lo, self.hi = lo, hi          # flat-gradient range (GPU path)
         self.buf = None                    # host buffer (TCP path)
         self.offsets = []
+        # GPU launch plan: CTA count, lean or full-width CTAs, first sum-of-squares slot
+        self.blocks, self.lean, self.sq_base = 0, False, 0
+        self.index = 0
 
 
 class DDP:
@@ -51,6 +70,8 @@ class DDP:
         self.model, self.pg, self.overlap, self.algo, self.method = model, pg, overlap, algo, method
         self.params = list(model.parameters())
         self.gpu = getattr(pg, "backend", "tcp") == "nvlink"
+        # one GPU: the flat buffer already holds the averaged gradient, nothing to launch
+        self._single_gpu = self.gpu and pg.world == 1
         self.comm_wait_s = 0.0
         self._sync = True
         if self.gpu:
@@ -71,8 +92,12 @@ class DDP:
             self.buckets.append(self._make_bucket(cur))
         self._where = {}
         for bi, b in enumerate(self.buckets):
+            b.index = bi
             for pi, p in enumerate(b.params):
                 self._where[id(p)] = (bi, pi)
+        self._trace = None
+        if self.gpu:
+            self._plan_gpu()
         self._hooks = [p.register_post_accumulate_grad_hook(self._on_grad) for p in self.params]
 
     # -------------------------------------------------------------- set-up
@@ -85,6 +110,32 @@ class DDP:
         # rank 0's parameters everywhere, with the bf16 working copy re-derived
         pg.broadcast(flat.master, root=0, cast_to=flat.work)
         self.flat = flat
+
+    def _plan_gpu(self):
+        """Per-bucket launch plan and the sum-of-squares pad: bucket b's CTAs own
+        slots [b.sq_base, b.sq_base + b.blocks) of every rank's row; the single flat
+        all-reduce of the no-overlap path owns the slots after the last bucket's."""
+        pg = self.pg
+        late = getattr(self.model, "late_grad_params", None)
+        late_ids = {id(p) for p in late()} if callable(late) else {id(self.params[0])}
+        cur = 0
+        for b in self.buckets:
+            nbytes = (b.hi - b.lo) * self.flat.grad.element_size()
+            b.lean = self.overlap and not any(id(p) in late_ids for p in b.params)
+            b.blocks = pg.collective_blocks(nbytes, lean=b.lean)
+            if b.lean and LEAN_BLOCKS > 0:
+                b.blocks = min(b.blocks, LEAN_BLOCKS)
+            b.sq_base = cur
+            cur += b.blocks
+        self._sq_lo_buckets, self._sq_hi_buckets = 0, cur
+        self._flat_blocks = pg.collective_blocks(self.flat.n * self.flat.grad.element_size(), lean=False)
+        self._sq_lo_flat, self._sq_hi_flat = cur, cur + self._flat_blocks
+        self._sq_stride = cur + self._flat_blocks
+        # the two-shot kernel publishes the sums of squares; one-shot (method="oneshot") does not
+        self.fused_norm = pg.world > 1 and self.method != "oneshot"
+        self._sq_pad = pg.alloc(pg.world * self._sq_stride, torch.float64) if self.fused_norm else None
+        # global sum of squares of the averaged gradient, written by finish()
+        self.sq_norm = torch.zeros(1, dtype=torch.float64, device=pg.device)
 
     def _make_bucket(self, params) -> _Bucket:
         if self.gpu:
@@ -109,13 +160,60 @@ class DDP:
         finally:
             self._sync = prev
 
+    # ------------------------------------------------------------- tracing
+    def enable_trace(self):
+        """Record device timestamps (%globaltimer, ns) of every step: the step's start
+        (``trace_begin``), each bucket's ready point on the compute stream and its
+        all-reduce's start and end on the comm stream, and the join in ``finish()``.
+        The stamps are kernels too, so they are captured with a CUDA graph and
+        refreshed by every replay.  ``trace_report()`` reads the last step."""
+        if self.gpu:
+            self._trace = torch.zeros(3 * len(self.buckets) + 3, dtype=torch.int64, device=self.pg.device)
+
+    def _stamp(self, slot: int):
+        if self._trace is not None:
+            from ..ops._ext import lib
+            lib().stamp(self._trace, slot)
+
+    def trace_begin(self):
+        self._stamp(3 * len(self.buckets))
+
+    def trace_report(self) -> dict | None:
+        if self._trace is None:
+            return None
+        nb = len(self.buckets)
+        t = self._trace.cpu().tolist()
+        t0 = t[3 * nb]
+        ms = lambda v: round((v - t0) / 1e6, 4) if v else None  # noqa: E731
+        rep = {"join_ms": ms(t[3 * nb + 1])}
+        if self.overlap:
+            rows = [(ms(t[3 * i]), ms(t[3 * i + 1]), ms(t[3 * i + 2])) for i in range(nb)]
+            rep["buckets_ready_start_end_ms"] = rows
+            rep["backward_end_ms"] = max(r[0] for r in rows)
+            rep["comm_busy_ms"] = round(sum(r[2] - r[1] for r in rows), 4)
+            rep["exposed_after_backward_ms"] = round(rep["join_ms"] - rep["backward_end_ms"], 4)
+        else:
+            rep["backward_end_ms"] = ms(t[3 * nb + 2])
+            rep["exposed_after_backward_ms"] = round(rep["join_ms"] - rep["backward_end_ms"], 4)
+        return rep
+
     def _launch(self, b: _Bucket):
         if self.gpu:
             g = self.flat.grad[b.lo:b.hi]
-            if self.overlap:
-                b.work = self.pg.allreduce_async(g, self.algo, scale=1.0 / self.pg.world, method=self.method)
+            if self._trace is not None:
+                self._stamp(3 * b.index)
+                kw_trace = dict(stamps=(self._trace, 3 * b.index + 1, 3 * b.index + 2))
             else:
-                self.pg.allreduce(g, self.algo, scale=1.0 / self.pg.world, method=self.method)
+                kw_trace = {}
+            if self.method == "oneshot":
+                kw = dict(method="oneshot")
+            else:
+                kw = dict(method="twoshot", blocks=b.blocks, lean=b.lean,
+                          sq=(self._sq_pad, b.sq_base, self._sq_stride) if self.fused_norm else None)
+            if self.overlap:
+                b.work = self.pg.allreduce_async(g, self.algo, scale=1.0 / self.pg.world, **kw, **kw_trace)
+            else:
+                self.pg.allreduce(g, self.algo, scale=1.0 / self.pg.world, **kw)
         else:
             if self.overlap:
                 b.work = self.pg.allreduce_async(b.buf, self.algo)
@@ -123,7 +221,7 @@ class DDP:
                 self.pg.allreduce(b.buf, self.algo)
 
     def _on_grad(self, p):
-        if not self._sync:
+        if not self._sync or self._single_gpu:
             return
         bi, pi = self._where[id(p)]
         b = self.buckets[bi]
@@ -140,6 +238,14 @@ class DDP:
     def finish(self):
         """Complete gradient synchronisation; call after the last backward of a step."""
         t0 = time.perf_counter()
+        if self._single_gpu:
+            for p in self.params:
+                if p.grad is None:
+                    self.flat.grad_view(p).zero_()
+                elif not self.flat.owns_grad(p):
+                    self.flat.grad_view(p).copy_(p.grad)
+                    p.grad = self.flat.grad_view(p)
+            return
         if self.gpu and not self.overlap:
             self._finish_flat()
             self.comm_wait_s += time.perf_counter() - t0
@@ -163,10 +269,15 @@ class DDP:
                 self._launch(b)
         for b in self.buckets:
             if b.work is not None:
+                # the handle (and its event) is kept until the bucket's next launch:
+                # inside a graph capture nothing may be destroyed mid-capture
                 b.work.wait()
-                b.work = None
         self.comm_wait_s += time.perf_counter() - t0
         if self.gpu:
+            self._stamp(3 * len(self.buckets) + 1)
+            if self.fused_norm:
+                self.pg.sq_total(self._sq_pad, self.sq_norm, self._sq_stride, self._sq_lo_buckets,
+                                 self._sq_hi_buckets)
             for p in self.params:
                 if not self.flat.owns_grad(p):
                     p.grad = self.flat.grad_view(p)
@@ -181,19 +292,25 @@ class DDP:
             b.pending = len(b.params)
 
     def _finish_flat(self):
-        """GPU without overlap: every gradient already sits in the one peer-mapped flat
-        buffer, so the whole buffer is averaged by a single all-reduce after the
-        backward pass.  The buckets only matter for overlap; one collective pays the
-        cross-rank synchronisation once instead of once per bucket, and no collective
-        CTA competes with the backward kernels for SMs (measured faster than per-bucket
-        overlap on B200: the comm CTAs that wait on peers steal SMs from the
-        persistent GEMMs)."""
+        """GPU without overlap (``overlap=False``): every gradient already sits in the
+        one peer-mapped flat buffer, so the whole buffer is averaged by a single
+        full-width all-reduce after the backward pass (which also yields the
+        gradient's sum of squares)."""
         for p in self.params:
             if p.grad is None:
                 self.flat.grad_view(p).zero_()
             elif not self.flat.owns_grad(p):
                 self.flat.grad_view(p).copy_(p.grad)
-        self.pg.allreduce(self.flat.grad, self.algo, scale=1.0 / self.pg.world, method=self.method)
+        self._stamp(3 * len(self.buckets) + 2)
+        if self.method == "oneshot":
+            self.pg.allreduce(self.flat.grad, self.algo, scale=1.0 / self.pg.world, method="oneshot")
+        else:
+            self.pg.allreduce(self.flat.grad, self.algo, scale=1.0 / self.pg.world, method="twoshot",
+                              blocks=self._flat_blocks,
+                              sq=(self._sq_pad, self._sq_lo_flat, self._sq_stride) if self.fused_norm else None)
+        self._stamp(3 * len(self.buckets) + 1)
+        if self.fused_norm:
+            self.pg.sq_total(self._sq_pad, self.sq_norm, self._sq_stride, self._sq_lo_flat, self._sq_hi_flat)
         for p in self.params:
             if not self.flat.owns_grad(p):
                 p.grad = self.flat.grad_view(p)

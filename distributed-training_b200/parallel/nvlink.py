@@ -19,10 +19,16 @@ master and working-copy buffers here, so their collectives never copy.
 Ordering and failure.  Collectives are stream-ordered on the caller's current
 stream (``allreduce_async`` uses a dedicated comm stream and returns a handle
 whose ``wait()`` makes the current stream wait on it, like NCCL).  Every rank
-must issue the same collectives in the same order; each kernel synchronises with
-its peers through per-CTA epoch flags, and every wait gives up after ``timeout``
-seconds, writing an error code to a host-mapped status word.  ``check()`` turns a
-non-zero status into ``CommError``.
+must issue the same collectives in the same order, and one group's collectives
+never run concurrently with each other; each kernel synchronises with its peers
+through per-CTA epoch flags, and every wait gives up after ``timeout`` seconds,
+writing an error code to a host-mapped status word.  ``check()`` turns a non-zero
+status into ``CommError``.
+
+Graph capture.  The flag epochs come from a counter on the device that each
+collective advances itself, so a collective's launch is the same every time:
+collectives can be captured in a CUDA graph (DDP captures its per-bucket
+all-reduces inside the backward it replays) and mixed freely with eager calls.
 """
 from __future__ import annotations
 
@@ -42,9 +48,10 @@ ORDER_RANK, ORDER_CYCLIC = 0, 1
 ALGO_ONESHOT, ALGO_TWOSHOT = 0, 1
 # [max CTAs][max ranks] uint32 flags, then a ring of 16 uint64 collective descriptors
 _SIG_BYTES = 8192
-# "auto" picks one-shot only below this size: its out-of-place result costs a copy
-# back, and measured on 8 B200s the two-shot kernel was as fast down to 4 KB.
-_ONESHOT_MAX_BYTES = 0
+# "auto" picks one-shot at or below this size and two-shot above it.  One-shot
+# moves W times the data but needs one cross-rank barrier fewer; its result is
+# written out of place and copied back.
+ONESHOT_MAX_BYTES = int(os.environ.get("DTB_ONESHOT_MAX_BYTES", 64 * 1024))
 
 
 class FdExchange:
@@ -247,8 +254,9 @@ class NVLinkGroup:
     # ------------------------------------------------------------ plumbing
     @property
     def epoch(self) -> int:
-        """Next device flag epoch (advances identically on every rank)."""
-        return int(self._eng.epoch)
+        """Last flag epoch this rank's collectives used (read from the device counter,
+        synchronously; it advances identically on every rank)."""
+        return int(self._eng.device_epoch())
 
     @property
     def timeout(self) -> float:
@@ -286,8 +294,8 @@ class NVLinkGroup:
     def _sigs(self):
         return self._sig.ptrs
 
-    def _advance(self, used: int):
-        self._eng.advance(int(used))
+    def _issued(self):
+        self._eng.note_issued()
         self.seq += 1
 
     def _stage(self, nbytes: int) -> SymmetricBuffer:
@@ -316,13 +324,19 @@ class NVLinkGroup:
     def _order(self, algo: str) -> int:
         return ORDER_CYCLIC if algo == "ring" else ORDER_RANK
 
-    def allreduce(self, t: torch.Tensor, algo: str = "ring", scale: float = 1.0, method: str = "auto"):
+    def allreduce(self, t: torch.Tensor, algo: str = "ring", scale: float = 1.0, method: str = "auto",
+                  blocks: int = 0, lean: bool = False, sq=None):
         """In-place sum (times ``scale``) over ranks.
 
         ``algo`` selects the summation order: "ring" (dtrain ring order) or
         "direct" (rank order).  ``method`` selects the data movement: "oneshot"
         (every rank reduces everything: latency-optimal), "twoshot" (reduce-scatter
-        + all-gather: bandwidth-optimal) or "auto" (one-shot up to 1 MiB).
+        + all-gather: bandwidth-optimal) or "auto" (one-shot up to
+        ``ONESHOT_MAX_BYTES``, two-shot above).  Two-shot on a peer-mapped tensor
+        also takes ``blocks`` (CTA count, 0: by size), ``lean`` (128-thread CTAs
+        that share SMs with running GEMMs) and ``sq = (pad, base, stride)``: CTA b
+        writes the sum of squares of the scaled values it reduced into slot
+        ``rank * stride + base + b`` of every rank's fp64 ``pad`` (peer-mapped).
         """
         if self.world == 1:
             if scale != 1.0:
@@ -335,12 +349,16 @@ class NVLinkGroup:
         n = t.numel()
         nbytes = n * t.element_size()
         if method == "auto":
-            method = "oneshot" if nbytes <= _ONESHOT_MAX_BYTES else "twoshot"
+            method = "oneshot" if (nbytes <= ONESHOT_MAX_BYTES and not lean and sq is None) else "twoshot"
         if method == "twoshot" and self._eng.contains(t):
             # fast path: one native call, in place on the peer-mapped tensor
-            self._eng.allreduce_inplace(t, self._order(algo), scale)
+            pad, base, stride = sq if sq is not None else (None, 0, 0)
+            self._eng.allreduce_inplace(t, self._order(algo), scale, int(blocks or self.blocks), bool(lean), pad,
+                                        int(base), int(stride))
             self.seq += 1
             return t
+        if lean or sq is not None:
+            raise ValueError("lean / sum-of-squares all-reduce needs a peer-mapped tensor and method='twoshot'")
         buf, off = self._locate(t)
         staged = buf is None
         # one-shot writes out of place: it needs scratch for the result (and for the
@@ -355,16 +373,27 @@ class NVLinkGroup:
             if stage is buf and not staged:
                 raise RuntimeError("one-shot scratch aliases the input")
             out = stage.tensor(n, t.dtype, nbytes if staged else 0)
-            used = C.allreduce(self._sigs, self.rank, self.epoch, buf.ptrs, off, n, DT[t.dtype], out.data_ptr(),
-                               DT[t.dtype], ALGO_ONESHOT, self._order(algo), scale, self.timeout, self.blocks)
+            C.allreduce(self._sigs, self.rank, buf.ptrs, off, n, DT[t.dtype], out.data_ptr(), DT[t.dtype],
+                        ALGO_ONESHOT, self._order(algo), scale, self.timeout, int(blocks or self.blocks), False, [], 0,
+                        0)
             t.reshape(-1).copy_(out)
         else:
-            used = C.allreduce(self._sigs, self.rank, self.epoch, buf.ptrs, off, n, DT[t.dtype], 0, DT[t.dtype],
-                               ALGO_TWOSHOT, self._order(algo), scale, self.timeout, self.blocks)
+            C.allreduce(self._sigs, self.rank, buf.ptrs, off, n, DT[t.dtype], 0, DT[t.dtype], ALGO_TWOSHOT,
+                        self._order(algo), scale, self.timeout, int(blocks or self.blocks), False, [], 0, 0)
             if staged:
                 t.reshape(-1).copy_(buf.tensor(n, t.dtype))
-        self._advance(used)
+        self._issued()
         return t
+
+    def collective_blocks(self, nbytes: int, lean: bool = False) -> int:
+        """CTAs an all-reduce of ``nbytes`` launches (``blocks=0``, this group's cap applied)."""
+        return int(lib().collective_blocks(int(nbytes), int(self.blocks), bool(lean)))
+
+    def sq_total(self, pad: torch.Tensor, out: torch.Tensor, stride: int, lo: int, hi: int) -> torch.Tensor:
+        """``out[0]`` = sum of ``pad[r * stride + s]`` over ranks r and slots lo <= s < hi,
+        in a fixed order (the same bits on every rank)."""
+        lib().sq_total(pad, out, self.world, int(stride), int(lo), int(hi))
+        return out
 
     def reduce_scatter(self, flat: torch.Tensor, scale: float = 1.0, sq_parts: torch.Tensor | None = None):
         """Sum over ranks (ring order); this rank's partition then holds the total.
@@ -412,10 +441,9 @@ class NVLinkGroup:
             raise TypeError("broadcast cast_to needs a float32 source")
         c16 = cast_to.data_ptr() if cast_to is not None else 0
         src = buf.ptr + off  # every rank's copy of the payload after the first phase
-        used = lib().broadcast(self._sigs, self.rank, self.epoch, buf.ptrs, off, nbytes, root,
-                               src if cast_to is not None else 0, c16, t.numel() if cast_to is not None else 0,
-                               self.timeout, self.blocks)
-        self._advance(used)
+        lib().broadcast(self._sigs, self.rank, buf.ptrs, off, nbytes, root, src if cast_to is not None else 0, c16,
+                        t.numel() if cast_to is not None else 0, self.timeout, self.blocks)
+        self._issued()
         if staged and self.rank != root:
             t.reshape(-1).view(torch.uint8).copy_(buf.tensor(nbytes, torch.uint8))
         return t
@@ -425,15 +453,26 @@ class NVLinkGroup:
         self.seq += 1
 
     def allreduce_async(self, t: torch.Tensor, algo: str = "ring", scale: float = 1.0,
-                        method: str = "auto") -> GPUWork:
-        """Launch on the comm stream after the work already queued on the current stream."""
+                        method: str = "auto", **kw) -> GPUWork:
+        """Launch on the comm stream after the work already queued on the current stream
+        (also inside a CUDA-graph capture: the comm stream forks from the capturing
+        stream and ``wait()`` joins it back).  ``kw``: ``blocks``, ``lean``, ``sq`` as
+        for ``allreduce``; ``stamps = (buf, before, after)`` writes device timestamps
+        into the int64 ``buf`` around the kernel, on the comm stream."""
+        stamps = kw.pop("stamps", None)
         cur = torch.cuda.current_stream(self.device)
         self.comm_stream.wait_stream(cur)
         with torch.cuda.stream(self.comm_stream):
-            self.allreduce(t, algo, scale, method)
+            if stamps is not None:
+                lib().stamp(stamps[0], stamps[1])
+            self.allreduce(t, algo, scale, method, **kw)
+            if stamps is not None:
+                lib().stamp(stamps[0], stamps[2])
             ev = torch.cuda.Event()
             ev.record(self.comm_stream)
-        t.record_stream(self.comm_stream)
+        if not self._eng.contains(t):
+            # allocator-owned memory: keep it alive until the comm stream is done
+            t.record_stream(self.comm_stream)
         return GPUWork(ev, self)
 
     def close(self):

@@ -167,14 +167,14 @@ class ZeroAdamW:
         if W > 1 and self.fuse_rs:
             # one kernel: reduce-scatter + norm exchange + clip + AdamW + all-gather
             opt.t += 1
-            used = lib().zero_rs_adamw(
-                pg._sigs, pg.rank, pg.epoch, self._ptrs_of(self.gflat), sq_ptrs, self.flat, opt.m[0], opt.v[0],
+            lib().zero_rs_adamw(
+                pg._sigs, pg.rank, self._ptrs_of(self.gflat), sq_ptrs, self.flat, opt.m[0], opt.v[0],
                 [self._ptrs_of(fp.work)[r] if fp.work is not None else 0 for r in range(W)],
                 self._ptrs_of(self.flat), self.n, opt.lr, opt.b1, opt.b2, opt.eps, opt.wd, opt.t, 1.0 / W,
                 float(self.max_grad_norm or 0.0), self._sq_total, bool(self.gather_master), pg.timeout, nparts,
                 self.plan.keep if self.plan is not None else None,
                 self.plan.gen_word if self.plan is not None else None)
-            pg._advance(used)
+            pg._issued()
             return
         if W > 1:
             pg.reduce_scatter(self.gflat, scale=1.0 / W, sq_parts=self._sq_parts)
@@ -185,14 +185,14 @@ class ZeroAdamW:
             K.grad_sqnorm(self.gflat, self._sq_parts[:1])
             nparts = 1
         opt.t += 1
-        used = lib().zero_adamw_allgather(
-            pg._sigs, pg.rank, pg.epoch, sq_ptrs, nparts, self.flat, self.gflat, opt.m[0], opt.v[0],
+        lib().zero_adamw_allgather(
+            pg._sigs, pg.rank, sq_ptrs, nparts, self.flat, self.gflat, opt.m[0], opt.v[0],
             [self._ptrs_of(fp.work)[r] if fp.work is not None else 0 for r in range(W)],
             self._ptrs_of(self.flat), self.n, opt.lr, opt.b1, opt.b2, opt.eps, opt.wd, opt.t,
             float(self.max_grad_norm or 0.0), self._sq_total, bool(self.gather_master), pg.timeout, 0,
             self.plan.keep if self.plan is not None else None,
             self.plan.gen_word if self.plan is not None else None)
-        pg._advance(used)
+        pg._issued()
 
     def _ptrs_of(self, t: torch.Tensor):
         buf, off = self.pg._locate(t)

@@ -68,7 +68,8 @@ def parse(argv=None):
                          "fused into the GEMM) instead of gathering every parameter in the optimizer kernel")
     ap.add_argument("--cuda-graph", action="store_true",
                     help="GPU: capture forward+backward of a step in a CUDA graph and replay it (removes the "
-                         "per-kernel host launch cost; the gradient sync and the optimizer run eagerly)")
+                         "per-kernel host launch cost); under DDP the bucket all-reduces launched from the "
+                         "grad-ready hooks are captured with it; the optimizer runs eagerly")
     ap.add_argument("--ckpt-dir", default=None)
     ap.add_argument("--ckpt-every", type=int, default=0)
     ap.add_argument("--async-ckpt", action="store_true",
@@ -133,10 +134,7 @@ class Trainer:
             pass
         if a.mode == "ddp":
             from .parallel.ddp import DDP
-            # a captured backward cannot launch per-bucket collectives (their flag epochs
-            # advance every call), so graph mode syncs the flat gradient after replay
-            overlap = not a.no_overlap and not (getattr(a, "cuda_graph", False) and self.gpu)
-            self.ddp = DDP(self.model, pg, bucket_mb=a.bucket_mb, overlap=overlap, algo=a.algo,
+            self.ddp = DDP(self.model, pg, bucket_mb=a.bucket_mb, overlap=not a.no_overlap, algo=a.algo,
                            method=a.ar_method)
         elif a.mode == "zero":
             from .parallel.zero import ZeroAdamW
@@ -154,6 +152,9 @@ class Trainer:
         # CUDA-graph state (--cuda-graph): static inputs, the captured forward+backward,
         # its loss output, and how many of this extension's kernels one replay launches
         self.use_graph = bool(getattr(a, "cuda_graph", False)) and self.gpu
+        # GPU DDP: the gradient sync (bucket all-reduces launched from the grad-ready
+        # hooks, their join and the gradient norm) is captured with forward+backward
+        self.sync_in_graph = self.use_graph and self.ddp is not None and self.ddp.gpu
         self._graph = None
         self._graph_key = None
         self._static_in: list = []
@@ -186,6 +187,8 @@ class Trainer:
 
     def _fwd_bwd(self, batches_dev, n_micro: int):
         """Forward and backward over all micro-batches (device tensors); returns the mean loss."""
+        if self.ddp is not None and self.gpu:
+            self.ddp.trace_begin()
         loss_acc = torch.zeros((), dtype=torch.float64, device=self.device)
         for mi, vrs in enumerate(batches_dev):
             last = mi == len(batches_dev) - 1
@@ -217,13 +220,19 @@ class Trainer:
                 for _ in range(2):
                     self.model.zero_grad()
                     self._fwd_bwd(self._static_in, n_micro)
+                    if self.sync_in_graph:
+                        self.ddp.finish()
             torch.cuda.current_stream(self.device).wait_stream(side)
             torch.cuda.synchronize(self.device)
+            if self.pg is not None and self.gpu:
+                self.pg.check()
             self.model.zero_grad()
             g = torch.cuda.CUDAGraph()
             before = K.launch_count()
             with torch.cuda.graph(g):
                 self._static_loss = self._fwd_bwd(self._static_in, n_micro)
+                if self.sync_in_graph:
+                    self.ddp.finish()
             self.graph_launches = K.launch_count() - before
             self._graph, self._graph_key = g, key
         for mi, vrs in enumerate(batches):
@@ -237,6 +246,8 @@ class Trainer:
 
     def _eager_fwd_bwd(self, batches):
         """Forward and backward over host or device micro-batches, kernels launched eagerly."""
+        if self.ddp is not None and self.gpu:
+            self.ddp.trace_begin()
         n_micro = sum(len(v) for v in batches)
         loss_acc = torch.zeros((), dtype=torch.float64, device=self.device) if self.gpu else 0.0
         for mi, vrs in enumerate(batches):
@@ -261,10 +272,11 @@ class Trainer:
         """``batches``: list over micro-steps of lists over virtual ranks of (x, y)."""
         a = self.a
         if self.use_graph:
-            with _nvtx("forward+backward (graph replay)"):
+            with _nvtx("forward+backward+gradient sync (graph replay)" if self.sync_in_graph
+                       else "forward+backward (graph replay)"):
                 loss_acc = self._step_graph(batches)
             with _nvtx("gradient sync"):
-                if self.ddp is not None:
+                if self.ddp is not None and not self.sync_in_graph:
                     before = self.ddp.comm_wait_s
                     self.ddp.finish()
                     self.comm_wait = self.ddp.comm_wait_s - before
@@ -295,8 +307,12 @@ class Trainer:
         a = self.a
         fp = self.model.flat
         if self.gpu and fp is not None and fp.work is not None:
-            from .ops import kernels as K
-            K.grad_sqnorm(fp.grad, self._sq)
+            if self.ddp is not None and self.ddp.gpu and self.ddp.fused_norm:
+                # the all-reduce kernels already summed the squares of the averaged gradient
+                self._sq = self.ddp.sq_norm
+            else:
+                from .ops import kernels as K
+                K.grad_sqnorm(fp.grad, self._sq)
             self.opt.step([fp.grad], sq_norm=self._sq, max_norm=a.clip if a.clip else 0.0)
             return
         grads = [p.grad for p in self.params]

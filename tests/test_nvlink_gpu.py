@@ -349,3 +349,57 @@ def test_ddp_gradients_match_single_process_and_agree_across_ranks(bucket_mb, ov
     ref = torch.cat([p.grad.reshape(-1) for p in m.parameters()]).cpu().numpy()
     err = np.linalg.norm(res[0] - ref) / np.linalg.norm(ref)
     assert err < 1e-2, err
+
+
+def _ddp_trainer_runs(pg):
+    """Three DDP training steps through the Trainer, for each way of synchronising
+    the gradient: per-bucket all-reduces launched from the grad-ready hooks during
+    backward (lean CTAs) or one flat all-reduce after it, each eager or captured
+    in the CUDA graph with forward+backward."""
+    import torch
+    from dtrain_b200 import train as T
+    from dtrain_b200.models.gpt import GPTConfig
+    from dtrain_b200.utils.data import SyntheticData
+    out = {}
+    for algo, clip in (("direct", "0"), ("ring", "1.0")):
+        for overlap in (True, False):
+            for graph in (True, False):
+                argv = ["--mode", "ddp", "--dtype", "bfloat16", "--batch", "2", "--ctx", "128", "--dim", "128",
+                        "--heads", "2", "--layers", "2", "--vocab", "512", "--data", "synthetic", "--algo", algo,
+                        "--clip", clip, "--bucket-mb", "0.05", "--lr", "3e-3"]
+                argv += ([] if overlap else ["--no-overlap"]) + (["--cuda-graph"] if graph else [])
+                a = T.parse(argv)
+                cfg = GPTConfig(vocab=512, ctx=128, dim=128, heads=2, layers=2, dtype="bfloat16")
+                tr = T.Trainer(a, cfg, pg.device, pg)
+                data = SyntheticData(512)
+                losses = [tr.step([[data.rank_batch(s, 0, 2, 128, 0, pg.rank, pg.world)]]) for s in range(3)]
+                pg.synchronize()
+                fp = tr.model.flat
+                # numpy, not torch tensors: the queue would share CPU tensors by file descriptor
+                out[(algo, overlap, graph)] = (fp.master.cpu().numpy().copy(), fp.grad.cpu().numpy().copy(),
+                                               tr.grad_norm(), losses, len(tr.ddp.buckets))
+                tr._graph = None
+                torch.cuda.synchronize()
+    return out
+
+
+@needs2
+def test_ddp_overlap_in_cuda_graph_matches_flat_allreduce_bit_for_bit():
+    res = _run(2, _ddp_trainer_runs)
+    for r in range(2):
+        o = res[r]
+        assert o[("direct", True, True)][4] > 4, "the test model must span several buckets"
+        base = o[("direct", False, False)]
+        # rank-order sums do not depend on how the gradient is cut into buckets
+        for key in [("direct", True, True), ("direct", True, False), ("direct", False, True)]:
+            assert np.array_equal(o[key][0], base[0]), key
+            assert np.array_equal(o[key][1], base[1]), key
+            assert o[key][3] == base[3], key
+            assert abs(o[key][2] - base[2]) <= 1e-12 * base[2]
+        # same buckets, same kernels: graph replay is bit-equal to eager launches, clip included
+        for overlap in (True, False):
+            a, b = o[("ring", overlap, True)], o[("ring", overlap, False)]
+            assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1]) and a[2] == b[2] and a[3] == b[3]
+    for key in res[0]:
+        assert np.array_equal(res[0][key][0], res[1][key][0]), ("ranks differ", key)
+        assert np.array_equal(res[0][key][1], res[1][key][1]), ("ranks differ", key)
