@@ -126,3 +126,17 @@ def max_param_diff(a: dict, b: dict) -> float:
     assert a is not None and b is not None, "a run saved no parameters"
     assert a.keys() == b.keys()
     return max(float(np.max(np.abs(a[k] - b[k]))) for k in a)
+
+
+def launch_script(workdir, world: int, script: str, args, tag: str, timeout: float = 600.0):
+    """Runs ``benchmarks/<script>`` on ``world`` CPU ranks through the launcher, with a
+    fresh gloo rendezvous file; raises with the tail of the output on failure."""
+    init = os.path.join(str(workdir), f"rdv-{tag}")
+    cmd = [PY, "-m", "dtrain_b200.launch", "--nproc", str(world), "--timeout", "60", "--",
+           PY, os.path.join(ROOT, "benchmarks", script), "--torch-init", init, *args]
+    env = dict(os.environ, OMP_NUM_THREADS="1", OPENBLAS_NUM_THREADS="1", MKL_NUM_THREADS="1",
+               PYTHONPATH=ROOT + os.pathsep + os.environ.get("PYTHONPATH", ""))
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=timeout, cwd=ROOT)
+    if r.returncode != 0:
+        raise RankError(f"{script} on {world} ranks failed:\n{r.stdout[-2000:]}\n{r.stderr[-3000:]}")
+    return r

@@ -1,171 +1,138 @@
-"""Host collectives across real processes (2, 3 and 4 ranks) over TCP loopback.
+"""Host (TCP) collectives across real processes on loopback, 2 to 4 ranks.
 
-Mirrors the reference's collective tests and adds bit-equality with the
-reference's own algorithms (run from baseline/_ref on the same inputs).
+Pinned behaviours (the reference's collective tests, tests/test_comm.py there):
+all-reduce equals the fp64 sum and is bit-identical on every rank, for ring and
+direct orders and awkward sizes (empty, single element, not divisible by the
+world); reduce-scatter leaves each rank its partition of the total and all-gather
+restores the whole buffer; broadcast copies the root's buffer; asynchronous
+all-reduces complete in issue order; a peer that dies mid-collective makes the
+survivor raise CommError instead of hanging.  Added here: bit-equality with the
+reference's own algorithms on the same inputs, torch tensors as buffers, the
+partition rule, and the store's wire compatibility with the reference's.
 """
-import multiprocessing as mp
 import os
 import sys
+import time
 
 import numpy as np
 import pytest
+from harness import HAVE_REF, REF, run_ranks
 
-from dtrain_b200.parallel.comm import CommError, ProcessGroup, StoreServer, partition
+from dtrain_b200.parallel.comm import CommError, StoreServer, partition
 
-ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-REF = os.path.join(ROOT, "baseline", "_ref")
-
-
-def _entry(rank, world, addr, fn, args, q, use_ref):
-    try:
-        if use_ref:
-            sys.path.insert(0, REF)
-            from dtrain.comm import ProcessGroup as RefPG
-            pg = RefPG(rank, world, addr, timeout=30)
-        else:
-            pg = ProcessGroup(rank, world, addr, timeout=30)
-        res = fn(pg, *args)
-        pg.close()
-        q.put((rank, res))
-    except BaseException as e:  # noqa: BLE001
-        q.put((rank, e))
+SIZES = [0, 1, 4, 9, 31, 257, 4099, 20000]
 
 
-def _run(world, fn, *args, timeout=90, use_ref=False):
-    srv = StoreServer()
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    ps = [ctx.Process(target=_entry, args=(r, world, srv.address, fn, args, q, use_ref)) for r in range(world)]
-    for p in ps:
-        p.start()
-    out = {}
-    for _ in range(world):
-        r, res = q.get(timeout=timeout)
-        out[r] = res
-    for p in ps:
-        p.join(timeout)
-    srv.close()
-    errs = [v for v in out.values() if isinstance(v, BaseException)]
-    if errs:
-        raise errs[0]
-    return [out[r] for r in range(world)]
+def _rank_data(rank: int, n: int, tag: int, dtype=np.float64) -> np.ndarray:
+    return np.random.default_rng([tag, rank]).standard_normal(n).astype(dtype)
 
 
-def _allreduce(pg, sizes, algo, dtype):
+def _allreduce_sizes(pg, algo, dtype):
     out = []
-    for i, n in enumerate(sizes):
-        x = np.random.default_rng(1000 * i + pg.rank).standard_normal(n).astype(dtype)
+    for tag, n in enumerate(SIZES):
+        x = _rank_data(pg.rank, n, tag, dtype)
         pg.allreduce(x, algo)
         out.append(x)
     return out
 
 
-SIZES = [0, 1, 2, 3, 5, 7, 64, 1000, 12345]
+@pytest.mark.parametrize("algo", ["ring", "direct"])
+@pytest.mark.parametrize("world", [2, 3, 4])
+def test_allreduce_is_the_sum_and_identical_on_every_rank(world, algo):
+    res = run_ranks(world, _allreduce_sizes, algo, np.float64)
+    for tag, n in enumerate(SIZES):
+        total = np.sum([_rank_data(r, n, tag) for r in range(world)], axis=0) if n else np.zeros(0)
+        for r in range(world):
+            assert res[r][tag].shape == (n,)
+            np.testing.assert_allclose(res[r][tag], total, rtol=1e-12, atol=1e-12)
+            assert res[r][tag].tobytes() == res[0][tag].tobytes(), (world, algo, n, r)
+
+
+@pytest.mark.skipif(not HAVE_REF, reason="reference not installed in baseline/_ref")
+@pytest.mark.parametrize("algo", ["ring", "direct"])
+def test_allreduce_bits_equal_the_reference_algorithms(algo):
+    ours = run_ranks(3, _allreduce_sizes, algo, np.float32)
+    ref = run_ranks(3, _allreduce_sizes, algo, np.float32, group="reference")
+    for a, b in zip(ours, ref):
+        for x, y in zip(a, b):
+            assert x.tobytes() == y.tobytes()
+
+
+def _scatter_then_gather(pg, n):
+    data = (np.arange(n, dtype=np.float64) % 97) * (pg.rank + 2)  # small integers: exact sums
+    mine = np.array(pg.reduce_scatter(data), copy=True)
+    b = partition(n, pg.world)
+    rebuilt = np.full(n, np.nan)
+    rebuilt[b[pg.rank]:b[pg.rank + 1]] = mine
+    pg.all_gather(rebuilt)
+    return mine, rebuilt
 
 
 @pytest.mark.parametrize("world", [2, 3, 4])
-@pytest.mark.parametrize("algo", ["ring", "direct"])
-def test_allreduce_matches_numpy_sum(world, algo):
-    res = _run(world, _allreduce, SIZES, algo, np.float64)
-    for i, n in enumerate(SIZES):
-        expect = sum(np.random.default_rng(1000 * i + r).standard_normal(n) for r in range(world))
-        for r in range(world):
-            np.testing.assert_allclose(res[r][i], expect, rtol=1e-12, atol=1e-12)
-            assert np.array_equal(res[r][i], res[0][i])
-
-
-@pytest.mark.skipif(not os.path.isdir(os.path.join(REF, "dtrain")), reason="reference not installed in baseline/_ref")
-@pytest.mark.parametrize("algo", ["ring", "direct"])
-def test_allreduce_bit_equal_to_reference_algorithms(algo):
-    sizes = [1, 7, 1000, 12345]
-    ours = _run(3, _allreduce, sizes, algo, np.float32)
-    ref = _run(3, _allreduce, sizes, algo, np.float32, use_ref=True)
-    for a, b in zip(ours, ref):
-        for x, y in zip(a, b):
-            assert np.array_equal(x, y)
-
-
-def _rs_ag(pg, n):
-    flat = np.arange(n, dtype=np.float64) * (pg.rank + 1)
-    mine = np.array(pg.reduce_scatter(flat), copy=True)
-    b = partition(n, pg.world)
-    full = np.zeros(n)
-    full[b[pg.rank]:b[pg.rank + 1]] = mine
-    pg.all_gather(full)
-    return mine, full
-
-
-@pytest.mark.parametrize("world", [2, 4])
-@pytest.mark.parametrize("n", [1, 3, 10, 1001])
-def test_reduce_scatter_and_all_gather(world, n):
-    res = _run(world, _rs_ag, n)
-    total = np.arange(n, dtype=np.float64) * sum(range(1, world + 1))
+@pytest.mark.parametrize("n", [1, 5, 17, 2049])
+def test_reduce_scatter_then_all_gather_rebuilds_the_total(world, n):
+    total = (np.arange(n, dtype=np.float64) % 97) * sum(r + 2 for r in range(world))
     b = partition(n, world)
-    for r, (mine, full) in enumerate(res):
+    for r, (mine, rebuilt) in enumerate(run_ranks(world, _scatter_then_gather, n)):
         np.testing.assert_array_equal(mine, total[b[r]:b[r + 1]])
-        np.testing.assert_array_equal(full, total)
+        np.testing.assert_array_equal(rebuilt, total)
 
 
-def _bcast_async(pg):
-    x = np.full(100, float(pg.rank))
-    pg.broadcast(x, root=1)
-    works = [pg.allreduce_async(np.full(10, float(i + pg.rank))) for i in range(5)]
-    for w in works:
+def _broadcast_and_fifo(pg, k):
+    x = np.arange(64, dtype=np.float64) + 100 * pg.rank
+    pg.broadcast(x, root=pg.world - 1)
+    bufs = [np.full(8, float(i * 10 + pg.rank)) for i in range(k)]
+    works = [pg.allreduce_async(b) for b in bufs]
+    for w in reversed(works):  # waiting out of order must not reorder the collectives
         w.wait()
-    return x
+    return x, [b[0] for b in bufs]
 
 
-def test_broadcast_and_async_order():
-    for x in _run(3, _bcast_async):
-        np.testing.assert_array_equal(x, np.ones(100))
+def test_broadcast_and_async_allreduces_complete_in_issue_order():
+    world, k = 3, 6
+    for x, firsts in run_ranks(world, _broadcast_and_fifo, k):
+        np.testing.assert_array_equal(x, np.arange(64, dtype=np.float64) + 100 * (world - 1))
+        assert firsts == [float(world * i * 10 + sum(range(world))) for i in range(k)]
 
 
-def _torch_fn(pg):
+def _sum_torch(pg):
     import torch
-    t = torch.full((17,), float(pg.rank + 1), dtype=torch.float64)
-    pg.allreduce(t, "ring")
+    t = torch.arange(11, dtype=torch.float64) * (pg.rank + 1)
+    pg.allreduce(t, "direct")
     return t.numpy().copy()
 
 
-def test_torch_tensors_are_accepted():
-    for x in _run(2, _torch_fn):
-        np.testing.assert_array_equal(x, np.full(17, 3.0))
+def test_torch_tensors_are_reduced_in_place():
+    for x in run_ranks(2, _sum_torch):
+        np.testing.assert_array_equal(x, np.arange(11, dtype=np.float64) * 3)
 
 
-def test_partition_matches_reference_rule():
+def test_partition_gives_the_remainder_to_the_lowest_ranks():
     assert partition(10, 4) == [0, 3, 6, 8, 10]
     assert partition(3, 4) == [0, 1, 2, 3, 3]
     assert partition(0, 2) == [0, 0, 0]
+    assert partition(7, 1) == [0, 7]
 
 
-def _dies(pg):
+def _die_or_wait(pg):
     if pg.rank == 1:
-        os._exit(3)  # crash without closing cleanly
-    x = np.ones(1000)
+        os._exit(3)  # gone without closing its sockets cleanly
+    t0 = time.monotonic()
     try:
-        pg.allreduce(x)
+        pg.allreduce(np.ones(4096))
     except CommError as e:
-        return e
-    return None
+        return ("commerror", time.monotonic() - t0, str(e)[:60])
+    return ("no error", time.monotonic() - t0, "")
 
 
-def test_peer_failure_raises_commerror_not_hang():
-    srv = StoreServer()
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    ps = [ctx.Process(target=_entry, args=(r, 2, srv.address, _dies, (), q, False)) for r in range(2)]
-    for p in ps:
-        p.start()
-    r, res = q.get(timeout=60)
-    assert r == 0 and isinstance(res, CommError)
-    for p in ps:
-        p.join(10)
-    srv.close()
+def test_dead_peer_raises_commerror_instead_of_hanging():
+    (kind, waited, _), = run_ranks(2, _die_or_wait, expect=[0], timeout=20.0)
+    assert kind == "commerror"
+    assert waited < 20.0
 
 
-def test_store_wire_compatible_with_reference():
-    if not os.path.isdir(os.path.join(REF, "dtrain")):
-        pytest.skip("reference not installed")
+@pytest.mark.skipif(not HAVE_REF, reason="reference not installed in baseline/_ref")
+def test_store_wire_format_interoperates_with_the_reference():
     sys.path.insert(0, REF)
     try:
         from dtrain.comm import Store as RefStore
@@ -173,15 +140,17 @@ def test_store_wire_compatible_with_reference():
     finally:
         sys.path.remove(REF)
     from dtrain_b200.utils.store import Store
-    ours_srv, ref_srv = StoreServer(), RefServer()
+    servers = [StoreServer(), RefServer()]
     try:
-        for srv_addr in (ours_srv.address, ref_srv.address):
-            a, b = Store(srv_addr), RefStore(srv_addr)
-            a.set("k", b"v1")
-            assert b.get("k") == b"v1"
-            assert a.add("n", 5) == 5 and b.add("n", 2) == 7
-            a.close()
-            b.close()
+        for srv in servers:
+            ours, theirs = Store(srv.address), RefStore(srv.address)
+            ours.set("key", b"value")
+            assert theirs.get("key") == b"value"
+            theirs.set("back", b"\x00\x01")
+            assert ours.get("back") == b"\x00\x01"
+            assert ours.add("ctr", 5) == 5 and theirs.add("ctr", 2) == 7
+            ours.close()
+            theirs.close()
     finally:
-        ours_srv.close()
-        ref_srv.close()
+        for srv in servers:
+            srv.close()

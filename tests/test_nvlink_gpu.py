@@ -8,10 +8,6 @@ reference's summation orders ("ring": chunk c summed from rank c cyclically;
 the host; its peer's device-side wait must time out into CommError with the
 CUDA context still usable - no GPU fault or hang.
 """
-import multiprocessing as mp
-import os
-import traceback
-
 import numpy as np
 import pytest
 import torch
@@ -23,45 +19,10 @@ WORLD = min(4, NGPU)
 needs2 = pytest.mark.skipif(NGPU < 2, reason="needs at least 2 GPUs")
 
 
-def _entry(rank, world, addr, fn, args, q):
-    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-    try:
-        import torch
-        from dtrain_b200.parallel.nvlink import NVLinkGroup, store_exchange
-        from dtrain_b200.utils.store import Store
-        torch.cuda.set_device(rank)
-        store = Store(addr, 60)
-        pg = NVLinkGroup(rank, world, torch.device("cuda", rank), store_exchange(store, rank, world), timeout=20.0)
-        res = fn(pg, *args)
-        pg.close()
-        q.put((rank, res))
-    except BaseException as e:  # noqa: BLE001
-        q.put((rank, RuntimeError(f"rank {rank}: {e!r}\n{traceback.format_exc()}")))
-
-
 def _run(world, fn, *args, timeout=240):
-    from dtrain_b200.utils.store import StoreServer
-    srv = StoreServer()
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    ps = [ctx.Process(target=_entry, args=(r, world, srv.address, fn, args, q)) for r in range(world)]
-    for p in ps:
-        p.start()
-    out = {}
-    try:
-        for _ in range(world):
-            r, res = q.get(timeout=timeout)
-            out[r] = res
-    finally:
-        for p in ps:
-            p.join(30)
-            if p.is_alive():
-                p.kill()
-        srv.close()
-    errs = [v for v in out.values() if isinstance(v, BaseException)]
-    if errs:
-        raise errs[0]
-    return [out[r] for r in range(world)]
+    """Ranks as spawned processes, each with an NVLinkGroup on GPU ``rank`` (tests/harness.py)."""
+    from harness import run_ranks
+    return run_ranks(world, fn, *args, group="nvlink", timeout=20.0, wait_s=timeout)
 
 
 def _inputs(rank, n, seed, dtype):
