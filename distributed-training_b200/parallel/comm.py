@@ -158,8 +158,11 @@ class _Link:
         if nbytes:
             self._recv_into(memoryview(out).cast("B"))
 
-    def close(self):
+    def close(self, wait: float = 5.0):
+        # the sender finishes what it holds, then exits; it is joined so no thread of
+        # this link is still running when the interpreter shuts down
         self._jobs.put(None)
+        self._thread.join(wait)
         try:
             self.sock.close()
         except OSError:
@@ -361,6 +364,8 @@ class ProcessGroup:
 
     def close(self):
         self._fifo.put(None)
+        if self._worker is not threading.current_thread():
+            self._worker.join(self.timeout)
         for link in self.links.values():
             link.close()
         self.store.close()
