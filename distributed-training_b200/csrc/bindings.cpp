@@ -29,8 +29,9 @@ torch::Tensor layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, 
 void bias_grad(torch::Tensor g, torch::Tensor db, bool accumulate);
 // embed_xent.cu
 torch::Tensor embed_fwd(torch::Tensor idx, torch::Tensor tok, torch::Tensor pos, torch::Tensor bad_flag);
-void embed_bwd(torch::Tensor sorted_ids, torch::Tensor perm, torch::Tensor dx, torch::Tensor dtok,
-               torch::Tensor dpos, int64_t B, int64_t T, bool accumulate);
+void embed_bwd(torch::Tensor idx, torch::Tensor dx, torch::Tensor dtok, torch::Tensor dpos, int64_t B, int64_t T,
+               bool accumulate);
+std::vector<torch::Tensor> sort_ids(torch::Tensor idx, int64_t V);
 std::vector<torch::Tensor> xent_fwd(torch::Tensor logits, torch::Tensor tgt);
 std::vector<torch::Tensor> xent_from_parts(torch::Tensor part, torch::Tensor logits, torch::Tensor tgt);
 void xent_bwd(torch::Tensor logits, torch::Tensor tgt, torch::Tensor lse, torch::Tensor gscale);
@@ -129,6 +130,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("bias_grad", &bias_grad);
   m.def("embed_fwd", &embed_fwd);
   m.def("embed_bwd", &embed_bwd);
+  m.def("sort_ids", &sort_ids);
   m.def("xent_fwd", &xent_fwd);
   m.def("xent_bwd", &xent_bwd);
   m.def("adamw_step", &adamw_step);

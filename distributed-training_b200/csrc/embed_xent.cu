@@ -62,6 +62,135 @@ __global__ void embed_fwd_kernel(const int64_t* __restrict__ idx, const bf16* __
   st8f(out + r * C + c, a);
 }
 
+// ---------------------------------------------------------- stable id sort
+// LSD radix sort of the token ids with 8-bit digits (two passes for vocabularies
+// up to 65536), carrying each token's position.  Every pass is three small
+// kernels: per-block digit histograms, one scan that turns them into each
+// block's first output slot per digit, and a scatter that ranks equal digits
+// inside a block in position order (warp match + per-warp counts), so the sort
+// is stable and its output depends only on the ids: equal ids stay in position
+// order, which fixes the summation order of the embedding gradient below.
+constexpr int kSortBlock = 1024;  // elements (and threads) per block
+constexpr int kSortBins = 256;
+
+__device__ __forceinline__ int sort_key(long i, long n, const int64_t* key64, const int* key32, int vclamp) {
+  if (i >= n) return -1;
+  long k = key64 ? key64[i] : (long)key32[i];
+  return (k < 0 || k > vclamp) ? vclamp : (int)k;  // ids outside [0, V) sort last and match no row
+}
+
+__global__ void __launch_bounds__(kSortBlock)
+    sort_hist_kernel(const int64_t* key64, const int* key32, long n, int vclamp, int shift, int* ghist) {
+  __shared__ int h[kSortBins];
+  for (int k = threadIdx.x; k < kSortBins; k += blockDim.x) h[k] = 0;
+  __syncthreads();
+  const int key = sort_key((long)blockIdx.x * kSortBlock + threadIdx.x, n, key64, key32, vclamp);
+  if (key >= 0) atomicAdd(&h[(key >> shift) & 255], 1);
+  __syncthreads();
+  for (int k = threadIdx.x; k < kSortBins; k += blockDim.x) ghist[(long)blockIdx.x * kSortBins + k] = h[k];
+}
+
+// goff[b][k] = (number of keys with digit < k) + (keys with digit k in blocks < b)
+__global__ void __launch_bounds__(kSortBins) sort_scan_kernel(const int* ghist, int nblk, int* goff) {
+  __shared__ int tot[kSortBins];
+  const int k = threadIdx.x;
+  int t = 0;
+  for (int b = 0; b < nblk; ++b) t += ghist[(long)b * kSortBins + k];
+  tot[k] = t;
+  __syncthreads();
+  int base = 0;
+  for (int j = 0; j < k; ++j) base += tot[j];
+  for (int b = 0; b < nblk; ++b) {
+    goff[(long)b * kSortBins + k] = base;
+    base += ghist[(long)b * kSortBins + k];
+  }
+}
+
+template <bool FINAL>
+__global__ void __launch_bounds__(kSortBlock)
+    sort_scatter_kernel(const int64_t* key64, const int* key32, const int* val_in, long n, int vclamp, int shift,
+                        const int* goff, int* key_out, int* val_out, int64_t* key_out64, int64_t* val_out64) {
+  constexpr int kWarps = kSortBlock / 32;
+  __shared__ int wcount[kWarps][kSortBins];
+  for (int i = threadIdx.x; i < kWarps * kSortBins; i += blockDim.x) (&wcount[0][0])[i] = 0;
+  __syncthreads();
+  const long i = (long)blockIdx.x * kSortBlock + threadIdx.x;
+  const int key = sort_key(i, n, key64, key32, vclamp);
+  const int digit = key >= 0 ? (key >> shift) & 255 : kSortBins;  // kSortBins: no element
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const unsigned same = __match_any_sync(0xffffffffu, digit);
+  const int rank_in_warp = __popc(same & ((1u << lane) - 1u));
+  if (digit < kSortBins && rank_in_warp == 0) wcount[warp][digit] = __popc(same);
+  __syncthreads();
+  // exclusive scan of every digit's count over the warps (in warp order)
+  for (int k = threadIdx.x; k < kSortBins; k += blockDim.x) {
+    int run = 0;
+    for (int w = 0; w < kWarps; ++w) {
+      const int c = wcount[w][k];
+      wcount[w][k] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+  if (digit < kSortBins) {
+    const long dst = goff[(long)blockIdx.x * kSortBins + digit] + wcount[warp][digit] + rank_in_warp;
+    const int val = val_in ? val_in[i] : (int)i;
+    if (FINAL) {
+      key_out64[dst] = key;
+      val_out64[dst] = val;
+    } else {
+      key_out[dst] = key;
+      val_out[dst] = val;
+    }
+  }
+}
+
+// Stable sort of idx (int64 [n], values in [0, V)): returns (sorted ids, positions) as int64.
+std::vector<torch::Tensor> sort_ids(torch::Tensor idx, int64_t V) {
+  TORCH_CHECK(idx.is_cuda() && idx.scalar_type() == at::kLong && idx.is_contiguous(), "sort_ids: int64 CUDA ids");
+  TORCH_CHECK(V >= 1 && V < (1L << 24), "sort_ids: vocabulary must be below 2^24");
+  TORCH_CHECK(idx.numel() < (1L << 31), "sort_ids: too many ids");
+  c10::cuda::CUDAGuard guard(idx.device());
+  const long n = idx.numel();
+  auto opt32 = idx.options().dtype(at::kInt);
+  auto sorted = torch::empty({n}, idx.options());
+  auto perm = torch::empty({n}, idx.options());
+  if (n == 0) return {sorted, perm};
+  const int nblk = (int)((n + kSortBlock - 1) / kSortBlock);
+  auto hist = torch::empty({2, (long)nblk * kSortBins}, opt32);
+  auto ka = torch::empty({n}, opt32), va = torch::empty({n}, opt32);
+  auto kb = torch::empty({n}, opt32), vb = torch::empty({n}, opt32);
+  const int vclamp = (int)V;  // out-of-range ids become V
+  int passes = 1;
+  while (passes < 3 && (vclamp >> (8 * passes)) > 0) ++passes;
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  const int64_t* k64 = idx.data_ptr<int64_t>();
+  const int* kin = nullptr;
+  const int* vin = nullptr;
+  int* gh = hist[0].data_ptr<int>();
+  int* go = hist[1].data_ptr<int>();
+  for (int p = 0; p < passes; ++p) {
+    const int shift = 8 * p;
+    const bool last = p == passes - 1;
+    int* kout = (p % 2 == 0) ? ka.data_ptr<int>() : kb.data_ptr<int>();
+    int* vout = (p % 2 == 0) ? va.data_ptr<int>() : vb.data_ptr<int>();
+    sort_hist_kernel<<<nblk, kSortBlock, 0, st>>>(p == 0 ? k64 : nullptr, kin, n, vclamp, shift, gh);
+    sort_scan_kernel<<<1, kSortBins, 0, st>>>(gh, nblk, go);
+    if (last)
+      sort_scatter_kernel<true><<<nblk, kSortBlock, 0, st>>>(p == 0 ? k64 : nullptr, kin, vin, n, vclamp, shift, go,
+                                                             nullptr, nullptr, sorted.data_ptr<int64_t>(),
+                                                             perm.data_ptr<int64_t>());
+    else
+      sort_scatter_kernel<false><<<nblk, kSortBlock, 0, st>>>(p == 0 ? k64 : nullptr, kin, vin, n, vclamp, shift, go,
+                                                              kout, vout, nullptr, nullptr);
+    count_launch(3);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    kin = kout;
+    vin = vout;
+  }
+  return {sorted, perm};
+}
+
 // dtok[v] = sum over sorted positions p in [lo(v), hi(v)) of dx[perm[p]]  (one warp per v)
 __global__ void embed_bwd_tok_kernel(const int64_t* __restrict__ sorted_ids, const int64_t* __restrict__ perm,
                                      long ntok, const bf16* __restrict__ dx, float* __restrict__ dtok, int V, int C,
@@ -310,13 +439,19 @@ torch::Tensor embed_fwd(torch::Tensor idx, torch::Tensor tok, torch::Tensor pos,
   return out;
 }
 
-// sorted_ids/perm: stable sort of idx.flatten(); dtok [V,C] fp32, dpos [>=T,C] fp32
-void embed_bwd(torch::Tensor sorted_ids, torch::Tensor perm, torch::Tensor dx, torch::Tensor dtok,
-               torch::Tensor dpos, int64_t B, int64_t T, bool accumulate) {
+// idx [B*T] int64 token ids; dtok [V,C] fp32, dpos [>=T,C] fp32.  The ids are
+// stably sorted by sort_ids() (this file's radix sort) so each vocabulary row sums
+// its positions in increasing order.
+void embed_bwd(torch::Tensor idx, torch::Tensor dx, torch::Tensor dtok, torch::Tensor dpos, int64_t B, int64_t T,
+               bool accumulate) {
   TORCH_CHECK(dx.scalar_type() == at::kBFloat16 && dx.is_contiguous(), "embed_bwd: dx");
   TORCH_CHECK(dtok.scalar_type() == at::kFloat && dpos.scalar_type() == at::kFloat, "embed_bwd: fp32 grads");
+  TORCH_CHECK(idx.numel() == B * T, "embed_bwd: B*T ids expected");
   c10::cuda::CUDAGuard guard(dx.device());
   const int V = (int)dtok.size(0), C = (int)dtok.size(1);
+  auto sp = sort_ids(idx.reshape({-1}).contiguous(), V);
+  const torch::Tensor& sorted_ids = sp[0];
+  const torch::Tensor& perm = sp[1];
   TORCH_CHECK(C % 4 == 0, "embed_bwd: C % 4");
   const long ntok = B * T;
   cudaStream_t st = at::cuda::getCurrentCUDAStream();

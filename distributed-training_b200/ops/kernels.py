@@ -87,9 +87,16 @@ def embed_fwd(idx: torch.Tensor, tok16: torch.Tensor, pos16: torch.Tensor, bad: 
 
 def embed_bwd(idx: torch.Tensor, dx: torch.Tensor, dtok: torch.Tensor, dpos: torch.Tensor,
               accumulate: bool = False) -> None:
+    """dtok[v] += sum of dx over the positions holding token v (in position order:
+    the ids are sorted by the extension's own stable radix sort), dpos[t] += sum over
+    the batch; written instead of added unless ``accumulate``."""
     B, T = idx.shape
-    sorted_ids, perm = torch.sort(idx.reshape(-1), stable=True)
-    lib().embed_bwd(sorted_ids, perm, dx, dtok, dpos, B, T, accumulate)
+    lib().embed_bwd(idx.reshape(-1), dx, dtok, dpos, B, T, accumulate)
+
+
+def sort_ids(idx: torch.Tensor, vocab: int):
+    """Stable sort of int64 token ids in [0, vocab): (sorted ids, positions), int64."""
+    return lib().sort_ids(idx.reshape(-1).contiguous(), int(vocab))
 
 
 def xent_fwd(logits: torch.Tensor, targets: torch.Tensor):

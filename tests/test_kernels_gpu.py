@@ -198,6 +198,22 @@ def test_embedding():
     assert _rel(dtok, ref_tok) < 1e-4
     assert _rel(dpos, dx.float().sum(0)) < 1e-4
     assert bad.item() == 0
+    again = torch.empty_like(dtok)
+    K.embed_bwd(idx, dx, again, torch.empty_like(dpos))
+    assert torch.equal(again, dtok)  # fixed summation order: the same bits every time
+
+
+@pytest.mark.parametrize("n,V", [(1, 65), (1000, 65), (16384, 50304), (70001, 50304), (5000, 70000)])
+def test_id_sort_is_stable_and_matches_torch(n, V):
+    """The embedding backward's radix sort (2 passes below 65536 ids, 3 above) against
+    torch's stable sort: same sorted ids and the same positions for equal ids."""
+    g = torch.Generator(device="cuda").manual_seed(n)
+    idx = torch.randint(0, V, (n,), device="cuda", generator=g)
+    idx[: n // 3] = idx[0]  # a long run of one id
+    ids, perm = K.sort_ids(idx, V)
+    want_ids, want_perm = torch.sort(idx, stable=True)
+    assert torch.equal(ids, want_ids)
+    assert torch.equal(perm, want_perm)
 
 
 @pytest.mark.parametrize("rows,V", [(64, 65), (256, 50304), (33, 1000)])
