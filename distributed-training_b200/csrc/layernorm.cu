@@ -18,6 +18,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "dtb_noalloc.h"
 
 namespace dtb {
 
@@ -460,76 +461,71 @@ DTB_DEFINE_STATUS_READER(status_layernorm)
 // ============================================================================
 // dtb_layernorm_bwd_noalloc: allocation-free LayerNorm backward (C entry point)
 // ============================================================================
-// This entry point has no counterpart in the reference project.
-//
-// Who it is for: callers that must not allocate device memory while they run.
-// Examples are host runtimes that reserve the whole GPU in their own pool before
-// training starts (a cudaMalloc would fail, or fragment their pool), and
-// latency-sensitive loops that cannot afford cudaMalloc/cudaFree, which may
-// synchronise the whole device.  It is also usable from plain C, without torch.
+// This entry point has no counterpart in the reference project.  Declaration,
+// return codes, limits and rules: dtb_noalloc.h (included so the compiler checks
+// this definition against it).
 //
 // What it computes: exactly what layernorm_bwd() above computes - dx (bf16),
 // plus dw and db (fp32, written or accumulated) - with the same kernels and the
 // same deterministic two-stage reduction.  The difference is where the per-block
 // partial sums live: instead of a workspace from the caching allocator they go
-// to the file-scope device array below.  The caller still passes every input and
-// output; this function allocates nothing (no cudaMalloc, no cudaFree, no torch).
-//
-// Limits and rules:
-//   * Scratch holds kLnNoAllocScratchFloats floats (4 MiB) per device, resident
-//     on every GPU that loads this library until the process exits.  A call needs
-//     2 * ceil(rows / 64) * C floats; larger calls are rejected (return
-//     DTB_NOALLOC_TOO_LARGE, with a message on stderr) before anything launches.
-//     At C = 768 that is up to 43,690 rows (rows * C <= 32 Mi elements).
-//   * C must be a multiple of 8 and at most 2048; all pointers 16-byte aligned
-//     except mean/rstd/dw/db (4-byte).
-//   * Every call on a device shares the one scratch array, and the array keeps
-//     the previous call's contents.  Nothing in it needs to start at zero (each
-//     call overwrites every partial it later reads), but two calls that overlap on
-//     the GPU - on different streams, or from different host threads without
-//     ordering - race on it.  Serialise calls on one device.
-//   * Set-up: the first call on each device looks up the array's device address
-//     with cudaGetSymbolAddress (with that device current) and caches it; in host
-//     code the array's name is only a host-side stand-in, so it is never passed
-//     to a kernel directly.  Make that first call before any stream capture.
-//
-// Returns 0 on success or a negative DTB_NOALLOC_* code.
-constexpr long kLnNoAllocScratchFloats = 1L << 20;  // 4 MiB of fp32 partials per device
+// to the file-scope device array below, so nothing is allocated.
+constexpr long kLnNoAllocScratchFloats = DTB_LN_NOALLOC_SCRATCH_FLOATS;
 
-// The scratch array itself (one copy per device that loads this library).
+// The scratch array itself (one copy per device that loads this library).  In
+// host code its name is only a host-side stand-in for the symbol: kernels get the
+// device address that cudaGetSymbolAddress returns.
 static __device__ __align__(256) float g_ln_noalloc_scratch[kLnNoAllocScratchFloats];
 
 namespace {
 
 constexpr int kNoAllocMaxDevices = 64;
 
-enum : int {
-  DTB_NOALLOC_OK = 0,
-  DTB_NOALLOC_BAD_ARGUMENT = -1,
-  DTB_NOALLOC_TOO_LARGE = -2,
-  DTB_NOALLOC_SETUP_FAILED = -3,
-  DTB_NOALLOC_LAUNCH_FAILED = -4,
+struct ScratchEntry {
+  CUcontext ctx;  // context the address belongs to
+  float* ptr;
 };
-
 std::mutex g_noalloc_mu;
-float* g_noalloc_scratch_ptr[kNoAllocMaxDevices] = {nullptr};
+ScratchEntry g_noalloc_scratch[kNoAllocMaxDevices] = {};
 
-// Device address of the scratch array on the current device (looked up once per device).
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+CtxGetCurrentFn ctx_get_current() {
+  static CtxGetCurrentFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return (CtxGetCurrentFn) nullptr;
+    return reinterpret_cast<CtxGetCurrentFn>(p);
+  }();
+  return fn;
+}
+
+// Device address of the scratch array in the current device's context.  Looked up
+// with cudaGetSymbolAddress once per device and cached together with the context
+// handle; a different context on the device (after cudaDeviceReset, say) is looked
+// up again instead of reusing an address that belonged to the old one.
 int noalloc_scratch(float** out) {
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return DTB_NOALLOC_SETUP_FAILED;
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (g_noalloc_scratch_ptr[dev] == nullptr) {
+  CtxGetCurrentFn get = ctx_get_current();
+  CUcontext ctx = nullptr;
+  if (get) get(&ctx);
+  ScratchEntry& e = g_noalloc_scratch[dev];
+  if (e.ptr == nullptr || ctx == nullptr || e.ctx != ctx) {
     void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_ln_noalloc_scratch);
-    if (e != cudaSuccess || p == nullptr) {
+    const cudaError_t err = cudaGetSymbolAddress(&p, g_ln_noalloc_scratch);
+    if (err != cudaSuccess || p == nullptr) {
       std::fprintf(stderr, "dtb_layernorm_bwd_noalloc: cudaGetSymbolAddress failed on device %d: %s\n", dev,
-                   cudaGetErrorString(e));
+                   cudaGetErrorString(err));
       return DTB_NOALLOC_SETUP_FAILED;
     }
-    g_noalloc_scratch_ptr[dev] = static_cast<float*>(p);
+    if (get && ctx == nullptr) get(&ctx);  // the lookup bound the primary context
+    e.ptr = static_cast<float*>(p);
+    e.ctx = ctx;
   }
-  *out = g_noalloc_scratch_ptr[dev];
+  *out = e.ptr;
   return DTB_NOALLOC_OK;
 }
 
@@ -548,11 +544,13 @@ extern "C" __attribute__((visibility("default"))) int dtb_layernorm_bwd_noalloc(
   const long need = 2 * nblk * (long)C;
   if (need > kLnNoAllocScratchFloats) {
     std::fprintf(stderr,
-                 "dtb_layernorm_bwd_noalloc: rows=%d, C=%d needs %ld scratch floats, more than the fixed %ld "
-                 "(rows * C must stay within about 32 Mi elements)\n",
-                 rows, C, need, kLnNoAllocScratchFloats);
+                 "dtb_layernorm_bwd_noalloc: rows=%d, C=%d needs %ld scratch floats (2 * ceil(rows / %d) * C), "
+                 "more than the fixed %ld\n",
+                 rows, C, need, kLnBwdRowsPerBlock, kLnNoAllocScratchFloats);
     return DTB_NOALLOC_TOO_LARGE;
   }
+  // an error left by earlier work is the caller's, not this call's: report it without clearing it
+  if (cudaPeekAtLastError() != cudaSuccess) return DTB_NOALLOC_PRIOR_ERROR;
   float* scratch = nullptr;
   if (noalloc_scratch(&scratch) != DTB_NOALLOC_OK) return DTB_NOALLOC_SETUP_FAILED;
   float* pw = scratch;
@@ -568,8 +566,10 @@ extern "C" __attribute__((visibility("default"))) int dtb_layernorm_bwd_noalloc(
     auto k = ln_bwd_kernel<NC>;                                                                                   \
     const size_t smem = ln_bwd_smem(NC);                                                                          \
     if (smem > 48 * 1024 && cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=     \
-                                cudaSuccess)                                                                      \
+                                cudaSuccess) {                                                                    \
+      cudaGetLastError();                                                                                         \
       return DTB_NOALLOC_LAUNCH_FAILED;                                                                           \
+    }                                                                                                             \
     k<<<(unsigned)nblk, kLnBwdWarps * 32, smem, stream>>>(dyp, xp, wp, mean, rstd, drp, dxp, pw, pb, nullptr, rows, \
                                                           C);                                                     \
   }
@@ -582,6 +582,8 @@ extern "C" __attribute__((visibility("default"))) int dtb_layernorm_bwd_noalloc(
     default: DTB_LNB_NOALLOC(8); break;
   }
 #undef DTB_LNB_NOALLOC
+  // the column sums must not run on partials the first kernel never wrote
+  if (cudaGetLastError() != cudaSuccess) return DTB_NOALLOC_LAUNCH_FAILED;
   ColsumJobs jobs{};
   jobs.part[0] = pw;
   jobs.out[0] = dw;
@@ -592,6 +594,4 @@ extern "C" __attribute__((visibility("default"))) int dtb_layernorm_bwd_noalloc(
   return DTB_NOALLOC_OK;
 }
 
-namespace dtb {
 
-}  // namespace dtb
