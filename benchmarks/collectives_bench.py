@@ -1,16 +1,19 @@
 """Collective sweep: this package's NVLink kernels vs NCCL on one node.
 
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \
-        --master-port P benchmarks/collectives_bench.py [--out results.jsonl] [--max-mb 1024]
+        --master-port P benchmarks/collectives_bench.py [--out results.jsonl] [--md table.md] [--max-mb 1024]
 
-Ops: all-reduce (one-shot, two-shot, auto), reduce-scatter, all-gather and
-broadcast on fp32 and bf16 buffers from 4 KB to 1 GB (powers of 2 for the fp32
-all-reduce, powers of 4 otherwise).  Each rank fills its buffer with N(0,1)
-values seeded by its rank.  Every measurement is CUDA-event timed on the
-launching stream after warm-up, and the reported time is the max over ranks.
-Bus bandwidth: all-reduce 2(W-1)/W * bytes / t; reduce-scatter and all-gather
-(W-1)/W * bytes / t (bytes = full buffer); broadcast bytes / t.  For the
-all-reduce the result is checked to be bit-identical on every rank.
+Ops: all-reduce (one-shot, two-shot and the size-based choice), reduce-scatter,
+all-gather and broadcast, on fp32 and bf16 buffers of every power of two from
+4 KB to 1 GB.  Each rank fills its buffer with N(0,1) values seeded by its rank.
+Every measurement is CUDA-event timed on the launching stream after warm-up (the
+same buffer each call: sizes below the 126 MB L2 are L2-warm, as in NCCL's own
+tests), and the reported time is the max over ranks.  Bus bandwidth: all-reduce
+2(W-1)/W * bytes / t; reduce-scatter and all-gather (W-1)/W * bytes / t (bytes =
+full buffer); broadcast bytes / t.  ``frac_peer_copy`` divides it by the 770 GB/s
+peer-copy bandwidth measured on this pool.  Bit identity across ranks is checked
+for every op on fresh data: the all-reduce result, the buffer that reduce-scatter
+followed by all-gather leaves on every rank, and the broadcast copy.
 """
 import argparse
 import datetime
@@ -26,6 +29,16 @@ import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 
 from dtrain_b200.parallel.nvlink import NVLinkGroup, torch_exchange  # noqa: E402
+
+
+PEER_COPY_GBS = 770.0  # measured peer-copy bandwidth per direction on this pool's B200s
+
+
+def same_on_all_ranks(t: torch.Tensor, world: int) -> bool:
+    h = hashlib.sha256(t.contiguous().view(torch.uint8).cpu().numpy().tobytes()).hexdigest()[:16]
+    hs = [None] * world
+    dist.all_gather_object(hs, h)
+    return len(set(hs)) == 1
 
 
 def timed(fn, iters, world):
@@ -48,6 +61,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", default=None)
     ap.add_argument("--max-mb", type=int, default=1024)
+    ap.add_argument("--md", default=None, help="write a Markdown summary table here (rank 0)")
     ap.add_argument("--blocks", type=int, default=0, help="CTAs per collective kernel (0 = size-based default)")
     ap.add_argument("--memory", choices=["ipc", "vmm"], default="ipc",
                     help="peer memory: cudaMalloc + IPC handles, or CUDA VMM allocations shared by file descriptor")
@@ -67,11 +81,13 @@ def main():
         big[dt].copy_(torch.randn(big[dt].numel(), generator=gen, device=dev).to(dt))
         ref[dt].copy_(big[dt])
     out = open(a.out, "a") if (a.out and rank == 0) else None
+    rows = []
     fac_ar = 2 * (world - 1) / world
     fac_rs = (world - 1) / world
 
     def emit(rec):
-        rec.update(world=world)
+        rec.update(world=world, frac_peer_copy=round(rec["busbw_GBs"] / PEER_COPY_GBS, 3))
+        rows.append(rec)
         if rank == 0:
             print(json.dumps(rec), flush=True)
             if out:
@@ -86,7 +102,7 @@ def main():
 
     for dt, name in ((torch.float32, "fp32"), (torch.bfloat16, "bf16")):
         esz = torch.tensor([], dtype=dt).element_size()
-        for nbytes in sizes(pow2=(dt == torch.float32)):
+        for nbytes in sizes(pow2=True):
             n = nbytes // esz
             iters = max(5, min(200, (2 << 30) // nbytes))
             x = big[dt][:n]
@@ -102,13 +118,11 @@ def main():
             x.copy_(torch.randn(n, generator=torch.Generator(device=dev).manual_seed(7 + rank), device=dev).to(dt))
             pg.allreduce(x, "ring")
             torch.cuda.synchronize()
-            h = hashlib.sha256(x.view(torch.uint8).cpu().numpy().tobytes()).hexdigest()[:16]
-            hs = [None] * world
-            dist.all_gather_object(hs, h)
+            same = same_on_all_ranks(x, world)
             for k, us in res.items():
                 emit({"op": "allreduce", "impl": k, "dtype": name, "bytes": nbytes, "us": round(us, 2),
-                      "busbw_GBs": round(fac_ar * nbytes / us / 1e3, 2), "bit_identical": len(set(hs)) == 1})
-        for nbytes in sizes(pow2=False):
+                      "busbw_GBs": round(fac_ar * nbytes / us / 1e3, 2), "bit_identical": same})
+        for nbytes in sizes(pow2=True):
             n = nbytes // esz
             if n % world:
                 continue
@@ -123,16 +137,58 @@ def main():
             t_bc = timed(lambda: pg.broadcast(x, root=0), iters, world)
             t_bc_n = timed(lambda: dist.broadcast(y, src=0), iters, world)
             pg.check()
-            for op, us, fac in (("reduce_scatter", t_rs, fac_rs), ("all_gather", t_ag, fac_rs),
-                                ("broadcast", t_bc, 1.0)):
+            # bit identity on fresh data: reduce-scatter then all-gather, then a broadcast
+            x.copy_(torch.randn(n, generator=torch.Generator(device=dev).manual_seed(11 + rank), device=dev).to(dt))
+            pg.reduce_scatter(x)
+            pg.all_gather(x)
+            torch.cuda.synchronize()
+            same_rsag = same_on_all_ranks(x, world)
+            x.copy_(torch.randn(n, generator=torch.Generator(device=dev).manual_seed(13 + rank), device=dev).to(dt))
+            pg.broadcast(x, root=0)
+            torch.cuda.synchronize()
+            same_bc = same_on_all_ranks(x, world)
+            for op, us, fac, same in (("reduce_scatter", t_rs, fac_rs, same_rsag), ("all_gather", t_ag, fac_rs, same_rsag),
+                                      ("broadcast", t_bc, 1.0, same_bc)):
                 emit({"op": op, "impl": "ours", "dtype": name, "bytes": nbytes, "us": round(us, 2),
-                      "busbw_GBs": round(fac * nbytes / us / 1e3, 2)})
+                      "busbw_GBs": round(fac * nbytes / us / 1e3, 2), "bit_identical": same})
             for op, us, fac in (("reduce_scatter", t_rs_n, fac_rs), ("all_gather", t_ag_n, fac_rs),
                                 ("broadcast", t_bc_n, 1.0)):
                 emit({"op": op, "impl": "nccl", "dtype": name, "bytes": nbytes, "us": round(us, 2),
                       "busbw_GBs": round(fac * nbytes / us / 1e3, 2)})
+    if rank == 0 and a.md:
+        with open(a.md, "w") as f:
+            f.write(markdown(rows, world))
     pg.close()
     dist.destroy_process_group()
+
+
+def _fmt_size(b: int) -> str:
+    return f"{b >> 30} GiB" if b >= 1 << 30 else f"{b >> 20} MiB" if b >= 1 << 20 else f"{b >> 10} KiB"
+
+
+def markdown(rows: list, world: int) -> str:
+    """One table per op and dtype: ours (best all-reduce method per size) vs NCCL."""
+    out = [f"## W = {world}", ""]
+    for op in ("allreduce", "reduce_scatter", "all_gather", "broadcast"):
+        for dt in ("fp32", "bf16"):
+            sel = [r for r in rows if r["op"] == op and r["dtype"] == dt]
+            if not sel:
+                continue
+            out += [f"### {op} {dt}", "", "| size | ours GB/s | method | NCCL GB/s | ours/NCCL | ours frac of 770 | "
+                    "bit-identical |", "|---|---|---|---|---|---|---|"]
+            for nb in sorted({r["bytes"] for r in sel}):
+                mine = [r for r in sel if r["bytes"] == nb and r["impl"] != "nccl"]
+                nccl = [r for r in sel if r["bytes"] == nb and r["impl"] == "nccl"]
+                if op == "allreduce":
+                    auto = [r for r in mine if r["impl"] == "ours_auto"]
+                    best = auto[0] if auto else max(mine, key=lambda r: r["busbw_GBs"])
+                else:
+                    best = mine[0]
+                n = nccl[0]["busbw_GBs"] if nccl else float("nan")
+                out.append(f"| {_fmt_size(nb)} | {best['busbw_GBs']:.1f} | {best['impl']} | {n:.1f} | "
+                           f"{best['busbw_GBs'] / n:.2f} | {best['frac_peer_copy']:.2f} | {best.get('bit_identical')} |")
+            out.append("")
+    return "\n".join(out)
 
 
 if __name__ == "__main__":

@@ -427,9 +427,31 @@ def make_group(a, device):
     return init_from_env()
 
 
+class _StopRequest:
+    """SIGTERM (the launcher stopping an attempt) becomes a flag checked between
+    steps.  Python runs the handler only once the current call returns, so a worker
+    blocked on the GPU - e.g. in a collective waiting for a peer that is gone - exits
+    after that wait has timed out, not with its kernels still running."""
+
+    def __init__(self):
+        self.requested = False
+
+    def install(self):
+        import signal
+
+        def handler(signum, frame):
+            self.requested = True
+
+        signal.signal(signal.SIGTERM, handler)
+        return self
+
+
 def main(argv=None):
     a = parse(argv)
+    stop = _StopRequest()
     device = _default_device(a)
+    if device.type == "cuda":
+        stop.install()  # CPU workers keep the default: nothing of theirs runs on a GPU
     if a.data == "synthetic":
         data = SyntheticData(a.vocab)
         vocab = a.vocab
@@ -463,6 +485,11 @@ def main(argv=None):
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
     for step in range(start, a.steps):
+        if stop.requested:
+            if tr.gpu:
+                torch.cuda.synchronize()  # every queued kernel is bounded: this returns
+            print(f"[rank {rank}] stopping at step {step} (SIGTERM)", file=sys.stderr, flush=True)
+            return 143
         if step == a.fail_at_step and rank == a.fail_rank and restarts == 0:
             if tr.gpu:
                 torch.cuda.synchronize()  # leave between steps, nothing in flight
