@@ -4,7 +4,7 @@
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \
         --master-port P bench.py --gpus N --steps K --warmup W
 
-Config (BASELINE.json, GPT-2-small DDP): 12 layers, d_model 768, 12 heads,
+Config (GPT-2-small DDP): 12 layers, d_model 768, 12 heads,
 context 1024, vocab 50304, 16 sequences per GPU of iid uniform random tokens,
 bf16 compute with fp32 grads and master weights, AdamW with global-norm clip
 1.0, 25 MiB gradient buckets (``--bucket-mb 1`` for the config's other size),
@@ -53,7 +53,7 @@ import torch  # noqa: E402
 METRIC = "GPT tokens/s at 1/2/4/8 B200 (DDP, ZeRO-1) vs ref NCCL; all-reduce busbw GB/s"
 MODEL = dict(vocab=50304, ctx=1024, dim=768, heads=12, layers=12)
 SEQ_PER_GPU = 16
-# BASELINE.json configs runnable with --config (the flagship is the default)
+# benchmark configurations runnable with --config (the flagship is the default)
 CONFIGS = {
     "gpt2-small-ddp": dict(model=MODEL, seq=SEQ_PER_GPU, mode="ddp", accum=1,
                            name="GPT-2-small (12L, d768, 12H, ctx 1024, vocab 50304)"),
@@ -433,7 +433,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--bucket-mb", type=float, default=25.0,
-                    help="DDP gradient bucket size in MiB, both arms (BASELINE config 3 names 1 and 25; 25 is torch "
+                    help="DDP gradient bucket size in MiB, both arms (the configuration names 1 and 25; 25 is torch "
                          "DDP's default and measured faster here: fewer per-bucket cross-GPU barriers)")
     ap.add_argument("--algo", choices=["ring", "direct"], default="ring")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="gpt2-small-ddp")
