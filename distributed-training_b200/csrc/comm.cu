@@ -87,12 +87,15 @@ struct SqOut {
 };
 
 // After the flags, each rank's signal pad holds a ring of kDescSlots 64-bit
-// descriptors (epoch << 32 | tag) of its own recent collectives, then two 32-bit
-// counters: the last epoch used and the CTAs of the running collective that exited.
+// descriptors (epoch << 32 | tag) of its own recent collectives, then three 32-bit
+// words: the last epoch used, the CTAs of the running collective that exited, and
+// a "failed" flag that a timed-out wait sets (device memory, so every later wait
+// can check it cheaply and give up at once instead of waiting out its own timeout).
 constexpr int kFlagWords = kMaxCommBlocks * kMaxRanks;
 constexpr int kDescSlots = 16;
 constexpr int kCtrWord = kFlagWords + 2 * kDescSlots;
-constexpr int kSigBytesUsed = (kCtrWord + 2) * 4;
+constexpr int kFailWord = kCtrWord + 2;
+constexpr int kSigBytesUsed = (kCtrWord + 3) * 4;
 static_assert(kSigBytesUsed <= 8192, "signal pad layout exceeds the 8 KB pad");
 
 // Copies pointer arrays from kernel parameters into shared memory with static
@@ -158,6 +161,15 @@ __device__ __forceinline__ uint64_t ld_acquire_sys64(const uint64_t* p) {
   return v;
 }
 
+__device__ __forceinline__ bool group_failed(const CommCtx& c) {
+  return *reinterpret_cast<volatile const uint32_t*>(c.sp->p[c.rank] + kFailWord) != 0u;
+}
+__device__ __forceinline__ void mark_failed(const CommCtx& c) {
+  atomicExch(c.sp->p[c.rank] + kFailWord, 1u);
+  atomicCAS(c.host_status, 0, kStatusPeerTimeout);
+  set_status(kStatusPeerTimeout);
+}
+
 // CTA-level barrier across ranks.  Returns false if a peer did not arrive in time.
 __device__ bool cta_barrier(const CommCtx& c, uint32_t epoch) {
   __shared__ int failed;
@@ -181,10 +193,11 @@ __device__ bool cta_barrier(const CommCtx& c, uint32_t epoch) {
       if ((i & 31u) == 0u) {
         const uint64_t now = globaltimer_ns();
         if (t0 == 0) t0 = now;
-        else if (now - t0 > c.timeout_ns) {
+        // a collective of this group already failed (a peer is gone): give up now
+        // rather than wait out another full timeout in every queued collective
+        if (group_failed(c) || (t0 != now && now - t0 > c.timeout_ns)) {
           atomicExch(&failed, 1);
-          atomicCAS(c.host_status, 0, kStatusPeerTimeout);
-          set_status(kStatusPeerTimeout);
+          mark_failed(c);
           break;
         }
       }
@@ -218,6 +231,7 @@ __device__ bool cta_enter(const CommCtx& c) {
     if (ld_acquire_sys64(ring + (c.epoch % kDescSlots)) != mine) {
       atomicExch(&mismatch, 1);
       atomicCAS(c.host_status, 0, kStatusSeqMismatch);
+      atomicExch(c.sp->p[c.rank] + kFailWord, 1u);
       set_status(kStatusSeqMismatch);
     }
   }
@@ -797,10 +811,9 @@ __device__ bool grid_barrier(const CommCtx& c, uint32_t epoch) {
         if (*reinterpret_cast<volatile int*>(&failed)) break;
         const uint64_t now = globaltimer_ns();
         if (t0 == 0) t0 = now;
-        else if (now - t0 > c.timeout_ns) {
+        if (group_failed(c) || (t0 != now && now - t0 > c.timeout_ns)) {
           atomicExch(&failed, 1);
-          atomicCAS(c.host_status, 0, kStatusPeerTimeout);
-          set_status(kStatusPeerTimeout);
+          mark_failed(c);
           break;
         }
       }
