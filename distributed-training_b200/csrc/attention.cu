@@ -527,6 +527,16 @@ std::vector<torch::Tensor> attn_fwd(torch::Tensor qkv, int64_t B, int64_t T, int
   return {out, lse};
 }
 
+// delta = rowsum(dout * out) [B*H, T] for head dim 64 (one warp per row).
+void attn_delta64(torch::Tensor out, torch::Tensor dout, torch::Tensor delta, int64_t B, int64_t T, int64_t H) {
+  const long warps = B * T * H;
+  attn::delta_kernel<64><<<(unsigned)((warps * 32 + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const bf16*>(out.data_ptr()), reinterpret_cast<const bf16*>(dout.data_ptr()),
+      delta.data_ptr<float>(), (int)B, (int)T, (int)H);
+  count_launch();
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 // Returns dqkv [B*T, 3*H*D] bf16.
 void attn_bwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torch::Tensor lse, torch::Tensor delta,
                  torch::Tensor dqkv, int64_t B, int64_t T, int64_t H);

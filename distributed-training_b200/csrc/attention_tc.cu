@@ -28,6 +28,9 @@
 
 #include <mutex>
 
+#include <cstdlib>
+#include <string>
+
 #include "common.cuh"
 
 namespace dtb {
@@ -104,55 +107,10 @@ __device__ __forceinline__ void fsub2(float& a0, float& a1, float b0, float b1) 
       "sub.rn.f32x2 xa, xa, xb;\n\tmov.b64 {%0, %1}, xa;\n\t}"
       : "+f"(a0), "+f"(a1) : "f"(b0), "f"(b1));
 }
-
-// 2^x for x <= 9 on the FMA pipe, two values at a time, so part of the softmax
-// exponentials leave the special-function unit (the forward's bottleneck).
-// Range reduction x = n + f with n = rint(x) from the 1.5*2^23 shifter and
-// f in [-0.5, 0.5]; 2^f from a degree-3 polynomial whose coefficients were fitted
-// here by the Remez exchange algorithm on the relative error (max 7.5e-5, well
-// under bf16's 2^-9); 2^n is added to the exponent field.  x is clamped at -126
-// so the exponent never wraps: masked (-inf) scores give 2^-126 ~ 1e-38.
-__device__ __forceinline__ void exp2_poly2(float& x0, float& x1) {
-  constexpr float kShift = 12582912.f;  // 1.5 * 2^23
-  constexpr float c0 = 0.99992805719f, c1 = 0.69326096773f, c2 = 0.24261112511f, c3 = 0.05517166853f;
-  x0 = fmaxf(x0, -126.f);
-  x1 = fmaxf(x1, -126.f);
-  float j0 = x0, j1 = x1;
-  fadd2(j0, j1, kShift, kShift);    // low mantissa bits of j hold rint(x)
-  float n0 = j0, n1 = j1;
-  fsub2(n0, n1, kShift, kShift);    // rint(x)
-  float f0 = x0, f1 = x1;
-  fsub2(f0, f1, n0, n1);            // f = x - rint(x)
-  float p0 = c3, p1 = c3;
-  ffma2(p0, p1, f0, f1, c2, c2);
-  ffma2(p0, p1, f0, f1, c1, c1);
-  ffma2(p0, p1, f0, f1, c0, c0);
-  // bits(j) << 23 == rint(x) << 23 (the shifter's own bits leave the word)
-  x0 = __int_as_float(__float_as_int(p0) + __float_as_int(j0) * 8388608);
-  x1 = __int_as_float(__float_as_int(p1) + __float_as_int(j1) * 8388608);
-}
-
-// bf16x2 pack of two non-negative finite floats with integer rounding (half up)
-// on the integer pipe instead of the conversion unit.
-__device__ __forceinline__ uint32_t pack_bf16x2_pos(float lo, float hi) {
-  const uint32_t a = __float_as_uint(lo) + 0x8000u, b = __float_as_uint(hi) + 0x8000u;
-  uint32_t r;
-  asm("prmt.b32 %0, %1, %2, 0x7632;" : "=r"(r) : "r"(a), "r"(b));
-  return r;
-}
-
-#ifndef DTB_ATTN_POLY_EVERY
-#define DTB_ATTN_POLY_EVERY 0
-#endif
-#ifndef DTB_ATTN_PACK_INT
-#define DTB_ATTN_PACK_INT 0
-#endif
-// One pair of columns in every kPolyEvery uses exp2_poly2 (0: none) and kPackInt
-// selects the integer bf16 packing.  Measured on B200 (B=16, T=1024, H=12): with
-// exponentials, packing and stores fused in one pass the plain ex2 + cvt version
-// is fastest (94 us; 1/4 polynomial 98 us, 1/2 polynomial 105 us), so both are off.
-constexpr int kPolyEvery = DTB_ATTN_POLY_EVERY;
-constexpr bool kPackInt = DTB_ATTN_PACK_INT != 0;
+// The softmax uses ex2 (special-function unit) and cvt-based bf16 packing.  Measured
+// on B200 (B=16, T=1024, H=12): with exponentials, packing and stores fused in one
+// pass this is faster than moving part of the exponentials to a polynomial on the
+// FMA pipe (1/4 of them: 98 vs 94 us; 1/2: 105 us) or packing on the integer pipe.
 
 struct Bars {
   uint64_t q_full;
@@ -357,14 +315,7 @@ __global__ void __maxnreg__(DTB_CORESIDENT_MAXNREG_ATTN)
 #pragma unroll
           for (int e = 0; e < 8; e += 2) ffma2(x[e], x[e + 1], sl2, sl2, nb, nb);
 #pragma unroll
-          for (int e = 0; e < 8; e += 2) {
-            if (kPolyEvery > 0 && (((ch * 8 + e) >> 1) % (kPolyEvery > 0 ? kPolyEvery : 1)) == kPolyEvery - 1) {
-              exp2_poly2(x[e], x[e + 1]);
-            } else {
-              x[e] = ex2_fast(x[e]);
-              x[e + 1] = ex2_fast(x[e + 1]);
-            }
-          }
+          for (int e = 0; e < 8; ++e) x[e] = ex2_fast(x[e]);
           fadd2(s0, s1, x[0], x[1]);
           fadd2(s2, s3, x[2], x[3]);
           fadd2(s0, s1, x[4], x[5]);
@@ -372,7 +323,7 @@ __global__ void __maxnreg__(DTB_CORESIDENT_MAXNREG_ATTN)
           uint32_t w[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e)
-            w[e] = kPackInt ? pack_bf16x2_pos(x[2 * e], x[2 * e + 1]) : pack_bf16x2(x[2 * e], x[2 * e + 1]);
+            w[e] = pack_bf16x2(x[2 * e], x[2 * e + 1]);
           tmem_st4(tmem + lane_off + TM_P + t * 64 + ch * 4, w[0], w[1], w[2], w[3]);
         }
         l = l * alpha + ((s0 + s1) + (s2 + s3));
@@ -503,8 +454,9 @@ __device__ __forceinline__ void put_row128(uint8_t* A, int r, const uint32_t* pk
 template <bool DKDV>
 __global__ void __maxnreg__(DTB_CORESIDENT_MAXNREG_ATTN)
     bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const __grid_constant__ CUtensorMap tmDO,
-                  const float* __restrict__ lse2, float* __restrict__ delta, const bf16* __restrict__ out,
-                  const bf16* __restrict__ dout, bf16* __restrict__ dqkv, int T, int H, float sl2, float scale) {
+                  const __grid_constant__ CUtensorMap tmDS, const float* __restrict__ lse2, float* __restrict__ delta,
+                  const bf16* __restrict__ out, const bf16* __restrict__ dout, bf16* __restrict__ dqkv, int T, int H,
+                  float sl2, float scale, int store_ds) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   BwBars* bars = reinterpret_cast<BwBars*>(smem + BW_OFF_BAR);
@@ -546,6 +498,7 @@ __global__ void __maxnreg__(DTB_CORESIDENT_MAXNREG_ATTN)
     fence_barrier_init();
     tma_prefetch_desc(&tmQKV);
     tma_prefetch_desc(&tmDO);
+    if (DKDV && store_ds) tma_prefetch_desc(&tmDS);
   }
   if (warp == 1) tmem_alloc(&bars->tmem_slot, 512);
   tc_fence_before();
@@ -669,7 +622,17 @@ __global__ void __maxnreg__(DTB_CORESIDENT_MAXNREG_ATTN)
           if (act) {
             if (!mbar_wait(&bars->ds_ready[t], k & 1, abort_flag)) { ok = false; break; }
             tc_fence_after();
+            if (DKDV && store_ds) {
+              // dS tile (queries of tile s x the sub-tile's 128 keys) -> global, for the dQ GEMM
+              const uint8_t* ds = smem + BW_OFF_P + t * PBYTES;
+              tma_store_3d(&tmDS, ds, (2 * pair + t) * 128, s * 128, bh);
+              tma_store_3d(&tmDS, ds + 16384, (2 * pair + t) * 128 + 64, s * 128, bh);
+              bulk_commit();
+            }
             issue_g(t, BW_G + t * 128, s0, k > 0);
+            // the element-wise warps overwrite the tile once ds_done arrives: the store
+            // must have read it by then
+            if (DKDV && store_ds) bulk_wait_read0();
             tc_commit(&bars->ds_done[t]);
           }
         }
@@ -677,6 +640,7 @@ __global__ void __maxnreg__(DTB_CORESIDENT_MAXNREG_ATTN)
         tc_commit(&bars->s0_empty[st]);
       }
       if (ok) tc_commit(&bars->done);
+      if (DKDV && store_ds) bulk_wait0();  // the dS stores are complete before the kernel ends
     }
   } else {
     // --------------------------------------------------------- element-wise
@@ -841,6 +805,107 @@ __global__ void __maxnreg__(DTB_CORESIDENT_MAXNREG_ATTN)
   }
 }
 
+// =============================================================================
+// dQ = scale * dS K from the dS tiles the dK/dV kernel stored (head dim 64).
+// CTA = (query tile i, batch*head); key tiles j <= i stream through a ring of
+// DQ_STAGES stages, each holding the dS tile (two 64-key atoms: the K-major A
+// operand, M = queries) and K_j (the MN-major B operand).  Warp 0 issues the TMA
+// loads, one thread of warp 1 the MMAs into a 64-column TMEM accumulator; warps
+// 2..5 read it back (one query row each), scale and store bf16.  The key tiles are
+// summed in increasing order, so the result does not depend on scheduling.
+// Reference math: dtrain/autograd.py:239-247 (gq = gs k).
+// =============================================================================
+constexpr int DQ_THREADS = 192;
+constexpr int DQ_STAGES = 4;
+constexpr int DQ_STAGE_BYTES = PBYTES + TILE;  // 32 KB dS + 16 KB K
+constexpr int DQ_OFF_BAR = DQ_STAGES * DQ_STAGE_BYTES;
+constexpr int DQ_SMEM = DQ_OFF_BAR + 256 + 1024;
+
+struct DqBars {
+  uint64_t full[DQ_STAGES], empty[DQ_STAGES];
+  uint64_t done;
+  uint32_t tmem_slot;
+  int abort_flag;
+};
+
+__global__ void __launch_bounds__(DQ_THREADS, 1)
+    dq_from_ds_kernel(const __grid_constant__ CUtensorMap tmDS, const __grid_constant__ CUtensorMap tmQKV,
+                      bf16* __restrict__ dqkv, int T, int H, float scale) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  DqBars* bars = reinterpret_cast<DqBars*>(smem + DQ_OFF_BAR);
+  volatile int* abort_flag = &bars->abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nt = (T + 127) / 128;
+  const int i = nt - 1 - (int)blockIdx.x;  // the longest query tiles first
+  const int bh = blockIdx.y, b = bh / H, h = bh % H;
+  const int C = H * D;
+  const int nj = i + 1;  // causal: key tiles 0..i
+
+  if (threadIdx.x == 0) {
+    for (int k = 0; k < DQ_STAGES; ++k) {
+      mbar_init(&bars->full[k], 1);
+      mbar_init(&bars->empty[k], 1);
+    }
+    mbar_init(&bars->done, 1);
+    bars->abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmDS);
+    tma_prefetch_desc(&tmQKV);
+  }
+  if (warp == 1) tmem_alloc(&bars->tmem_slot, 64);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int j = 0; j < nj; ++j) {
+        const int st = j % DQ_STAGES;
+        const uint32_t ph = ((j / DQ_STAGES) & 1) ^ 1;
+        if (!mbar_wait(&bars->empty[st], ph, abort_flag)) break;
+        uint8_t* stage = smem + st * DQ_STAGE_BYTES;
+        mbar_arrive_expect_tx(&bars->full[st], DQ_STAGE_BYTES);
+        tma_load_3d(&tmDS, stage, &bars->full[st], j * 128, i * 128, bh);
+        tma_load_3d(&tmDS, stage + 16384, &bars->full[st], j * 128 + 64, i * 128, bh);
+        tma_load_2d(&tmQKV, stage + PBYTES, &bars->full[st], C + h * D, b * T + j * 128);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16(128, D, false, true);  // A K-major (dS), B MN-major (K)
+      bool ok = true;
+      for (int j = 0; j < nj && ok; ++j) {
+        const int st = j % DQ_STAGES;
+        if (!mbar_wait(&bars->full[st], (j / DQ_STAGES) & 1, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t a = smem_u32(smem + st * DQ_STAGE_BYTES), kb = a + PBYTES;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          tc_mma_f16(tmem, make_sw128_desc(a + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
+                     make_sw128_desc(kb + kk * 2048, 8192, 1024), idesc, (j > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&bars->empty[st]);
+      }
+      if (ok) tc_commit(&bars->done);
+    }
+  } else {
+    const int q = warp & 3;  // TMEM lanes 32q .. 32q+31 belong to warps with warp % 4 == q
+    const int row = i * 128 + q * 32 + lane;
+    if (mbar_wait(&bars->done, 0, abort_flag)) {
+      tc_fence_after();
+      bf16* dst = dqkv + ((long)b * T + (row < T ? row : 0)) * 3L * C + h * D;
+      store_row64(tmem + ((uint32_t)(q * 32) << 16), dst, scale, row < T);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 64);
+  }
+}
+
 }  // namespace attn_tc
 
 typedef CUresult (*EncodeTiledFnA)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -891,6 +956,8 @@ void attn_fwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor lse, int64_
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+void attn_delta64(torch::Tensor out, torch::Tensor dout, torch::Tensor delta, int64_t B, int64_t T, int64_t H);
+
 static CUtensorMap attn_map(const torch::Tensor& t, long rows, long cols) {
   CUtensorMap m;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
@@ -904,10 +971,28 @@ static CUtensorMap attn_map(const torch::Tensor& t, long rows, long cols) {
   return m;
 }
 
-// tcgen05 backward for head dim 64: fills dqkv [B*T, 3*H*64] from qkv, dout
-// [B*T, H*64], lse2 [B*H, T] and delta = rowsum(dout * out) [B*H, T].
-// tcgen05 backward for head dim 64: dQ (and delta = rowsum(dO*O) into `delta`) first,
-// then dK/dV, both into dqkv [B*T, 3*H*64].
+// dS scratch [B*H][T][Tp] bf16 (Tp = T rounded up to 128 keys) as a 3-D tensor map
+// with 64-key x 128-query boxes: rows past T and keys past T clip (stores) or read
+// as zero (loads), and one (b, h) never spills into the next.
+static CUtensorMap ds_map(const torch::Tensor& ds, long BH, long T, long Tp) {
+  CUtensorMap m;
+  cuuint64_t dims[3] = {(cuuint64_t)Tp, (cuuint64_t)T, (cuuint64_t)BH};
+  cuuint64_t strides[2] = {(cuuint64_t)Tp * 2, (cuuint64_t)T * Tp * 2};
+  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode_fn_attn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, ds.data_ptr(), dims, strides, box, estr,
+                                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "attention: dS tensor map encode failed ", (int)r);
+  return m;
+}
+
+// tcgen05 backward for head dim 64, into dqkv [B*T, 3*H*64]:
+//   delta = rowsum(dO * O)                                   (delta_kernel)
+//   dK, dV, and every causal dS tile stored to a scratch      (bwd_tc_kernel<true>)
+//   dQ = scale * dS K                                          (dq_from_ds_kernel)
+// DTB_ATTN_DQ=recompute selects the older dQ kernel that recomputes P and dP
+// (bwd_tc_kernel<false>, which also writes delta) ahead of dK/dV instead.
 void attn_bwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torch::Tensor lse, torch::Tensor delta,
                  torch::Tensor dqkv, int64_t B, int64_t T, int64_t H) {
   using namespace attn_tc;
@@ -924,8 +1009,13 @@ void attn_bwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torch
   if (!attr) {
     cudaFuncSetAttribute(bwd_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, BW_SMEM);
     cudaFuncSetAttribute(bwd_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, BW_SMEM);
+    cudaFuncSetAttribute(dq_from_ds_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, DQ_SMEM);
     attr = true;
   }
+  static const bool recompute = [] {
+    const char* e = std::getenv("DTB_ATTN_DQ");
+    return e && std::string(e) == "recompute";
+  }();
   const int nt = (int)((T + 127) / 128);
   dim3 grid((unsigned)((nt + 1) / 2), (unsigned)(B * H));
   const float scale = 0.125f;                               // 1/sqrt(64)
@@ -934,10 +1024,25 @@ void attn_bwd_tc(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout, torch
   auto* dq = reinterpret_cast<bf16*>(dqkv.data_ptr());
   auto* o = reinterpret_cast<const bf16*>(out.data_ptr());
   auto* g = reinterpret_cast<const bf16*>(dout.data_ptr());
-  bwd_tc_kernel<false><<<grid, BW_THREADS, BW_SMEM, st>>>(mq, md, lse.data_ptr<float>(), delta.data_ptr<float>(), o,
-                                                          g, dq, (int)T, (int)H, sl2, scale);
-  bwd_tc_kernel<true><<<grid, BW_THREADS, BW_SMEM, st>>>(mq, md, lse.data_ptr<float>(), delta.data_ptr<float>(), o,
-                                                         g, dq, (int)T, (int)H, sl2, scale);
+  if (recompute) {
+    bwd_tc_kernel<false><<<grid, BW_THREADS, BW_SMEM, st>>>(mq, md, md, lse.data_ptr<float>(),
+                                                            delta.data_ptr<float>(), o, g, dq, (int)T, (int)H, sl2,
+                                                            scale, 0);
+    bwd_tc_kernel<true><<<grid, BW_THREADS, BW_SMEM, st>>>(mq, md, md, lse.data_ptr<float>(),
+                                                           delta.data_ptr<float>(), o, g, dq, (int)T, (int)H, sl2,
+                                                           scale, 0);
+    count_launch(2);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
+  const long Tp = (long)nt * 128;
+  auto ds = torch::empty({B * H, T, Tp}, qkv.options());
+  CUtensorMap mds = ds_map(ds, B * H, T, Tp);
+  attn_delta64(out, dout, delta, B, T, H);
+  bwd_tc_kernel<true><<<grid, BW_THREADS, BW_SMEM, st>>>(mq, md, mds, lse.data_ptr<float>(), delta.data_ptr<float>(),
+                                                         o, g, dq, (int)T, (int)H, sl2, scale, 1);
+  dq_from_ds_kernel<<<dim3((unsigned)nt, (unsigned)(B * H)), DQ_THREADS, DQ_SMEM, st>>>(mds, mq, dq, (int)T, (int)H,
+                                                                                        scale);
   count_launch(2);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
