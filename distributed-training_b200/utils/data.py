@@ -14,7 +14,9 @@ from __future__ import annotations
 
 import hashlib
 import os
+import tempfile
 import urllib.request
+from pathlib import Path
 
 import numpy as np
 
@@ -22,23 +24,38 @@ TINY_SHAKESPEARE = "https://raw.githubusercontent.com/karpathy/char-rnn/master/d
 TINY_SHAKESPEARE_SHA256 = "86c4e6aa9db7c042ec79f339dcb96d42b0075e16b8fc2e86bf0ca57e2dc565ed"
 
 
+def _fetch_verified(url: str, dest: str, sha256: str) -> None:
+    """Download ``url`` to ``dest`` through a private temporary file in the same folder.
+
+    The digest is computed while the bytes stream in; only a file whose digest
+    matches is renamed into place (an atomic rename), so ranks that fetch the
+    corpus at the same time never read a partial or unverified file.
+    """
+    folder = os.path.dirname(dest) or "."
+    os.makedirs(folder, exist_ok=True)
+    fd, tmp = tempfile.mkstemp(prefix=".fetch-", dir=folder)
+    digest = hashlib.sha256()
+    try:
+        with os.fdopen(fd, "wb") as out, urllib.request.urlopen(url) as src:
+            for block in iter(lambda: src.read(1 << 16), b""):
+                digest.update(block)
+                out.write(block)
+        if digest.hexdigest() != sha256:
+            raise ValueError(f"tiny shakespeare checksum mismatch: {digest.hexdigest()}")
+        os.replace(tmp, dest)
+    finally:
+        if os.path.exists(tmp):
+            os.remove(tmp)
+
+
 def load_text(path: str | None = None, cache_dir: str = "data") -> str:
-    """Read a text file, or tiny-shakespeare from ``cache_dir`` (downloaded and checked if missing)."""
-    if path:
-        with open(path, encoding="utf-8") as f:
-            return f.read()
-    p = os.path.join(cache_dir, "tinyshakespeare.txt")
-    if not os.path.exists(p):
-        os.makedirs(cache_dir, exist_ok=True)
-        urllib.request.urlretrieve(TINY_SHAKESPEARE, p + ".tmp")
-        with open(p + ".tmp", "rb") as f:
-            got = hashlib.sha256(f.read()).hexdigest()
-        if got != TINY_SHAKESPEARE_SHA256:
-            os.remove(p + ".tmp")
-            raise ValueError(f"tiny shakespeare checksum mismatch: {got}")
-        os.replace(p + ".tmp", p)
-    with open(p, encoding="utf-8") as f:
-        return f.read()
+    """Text of ``path``; without one, tiny-shakespeare cached under ``cache_dir``
+    (fetched and checksummed on first use)."""
+    if not path:
+        path = os.path.join(cache_dir, "tinyshakespeare.txt")
+        if not os.path.isfile(path):
+            _fetch_verified(TINY_SHAKESPEARE, path, TINY_SHAKESPEARE_SHA256)
+    return Path(path).read_text(encoding="utf-8")
 
 
 class CharData:
