@@ -230,13 +230,15 @@ def _grad_sync(tr, C, a, world) -> dict | str:
     if world == 1:
         return "one GPU: no collective (gradient norm kernel + AdamW)"
     d = tr.ddp
+    kind = "NVSwitch (multimem) reduction" if d.method == "nvls" else "two-shot"
+    order = "the switch's" if d.method == "nvls" else a.algo
     if not d.overlap:
-        return {"buckets": "unused", "method": "one two-shot all-reduce of the flat gradient after backward",
-                "order": a.algo, "grad_norm": "fused into the all-reduce"}
+        return {"buckets": "unused", "method": f"one {kind} all-reduce of the flat gradient after backward",
+                "order": order, "grad_norm": "fused into the all-reduce"}
     lean = sum(1 for b in d.buckets if b.lean)
     return {"buckets": len(d.buckets), "bucket_mb": a.bucket_mb,
-            "method": "two-shot per bucket, launched from the grad-ready hooks during backward",
-            "lean_buckets": lean, "full_width_buckets": len(d.buckets) - lean, "order": a.algo,
+            "method": f"{kind} per bucket, launched from the grad-ready hooks during backward",
+            "lean_buckets": lean, "full_width_buckets": len(d.buckets) - lean, "order": order,
             "grad_norm": "fused into the all-reduce"}
 
 
@@ -254,7 +256,7 @@ def run_ours(a, rank, world, local):
     if world > 1:
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
         pg = NVLinkGroup(rank, world, dev, torch_exchange(), timeout=120.0, blocks=a.comm_blocks,
-                         comm_priority=a.comm_priority)
+                         comm_priority=a.comm_priority, nvls=(a.ar_method == "nvls"))
     else:
         pg = NVLinkGroup(0, 1, dev, lambda k, p: [p], timeout=120.0)
     C = CONFIGS[a.config]
@@ -262,7 +264,7 @@ def run_ours(a, rank, world, local):
     args = T.parse(["--mode", C["mode"], "--dtype", "bfloat16", "--batch", str(seq), "--ctx", str(M["ctx"]),
                     "--dim", str(M["dim"]), "--heads", str(M["heads"]), "--layers", str(M["layers"]),
                     "--lr", "6e-4", "--clip", "1.0", "--bucket-mb", str(a.bucket_mb), "--data", "synthetic",
-                    "--vocab", str(M["vocab"]), "--algo", a.algo, "--accum", str(accum)]
+                    "--vocab", str(M["vocab"]), "--algo", a.algo, "--accum", str(accum), "--ar-method", a.ar_method]
                    + (["--no-overlap"] if a.no_overlap else []) + (["--cuda-graph"] if a.cuda_graph else [])
                    + (["--gather-gemm"] if a.gather_gemm else []))
     cfg = GPTConfig(dtype="bfloat16", **M)
@@ -437,6 +439,8 @@ def main():
                          "DDP's default and measured faster here: fewer per-bucket cross-GPU barriers)")
     ap.add_argument("--algo", choices=["ring", "direct"], default="ring")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="gpt2-small-ddp")
+    ap.add_argument("--ar-method", choices=["auto", "twoshot", "nvls"], default="auto",
+                    help="bucket all-reduce: fixed-order two-shot (auto) or NVSwitch reduction (nvls)")
     ap.add_argument("--comm-blocks", type=int, default=0, help="CTAs per collective kernel (0: by size)")
     ap.add_argument("--comm-priority", type=int, default=0, help="CUDA priority of the collective stream")
     ap.add_argument("--no-cuda-graph", dest="cuda_graph", action="store_false",

@@ -56,6 +56,12 @@ torch::Tensor tensor_from_ptr(int64_t ptr, std::vector<int64_t> sizes, c10::Scal
 std::tuple<int64_t, int64_t, int64_t> vmm_alloc(int64_t nbytes);
 int64_t vmm_import(int64_t fd, int64_t size);
 void vmm_free(int64_t va);
+bool mc_supported();
+int64_t mc_granularity(int64_t ndev);
+std::tuple<int64_t, int64_t> mc_create(int64_t size, int64_t ndev);
+int64_t mc_import(int64_t fd);
+int64_t mc_bind_map(int64_t mc, int64_t local_va, int64_t size, int64_t ndev);
+void mc_free(int64_t mc_va);
 int64_t comm_status();
 void comm_status_clear();
 int64_t allreduce(std::vector<int64_t> sigs, int64_t rank, std::vector<int64_t> bufs, int64_t byte_offset, int64_t n,
@@ -149,6 +155,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("vmm_alloc", &vmm_alloc);
   m.def("vmm_import", &vmm_import);
   m.def("vmm_free", &vmm_free);
+  m.def("mc_supported", &mc_supported);
+  m.def("mc_granularity", &mc_granularity);
+  m.def("mc_create", &mc_create);
+  m.def("mc_import", &mc_import);
+  m.def("mc_bind_map", &mc_bind_map);
+  m.def("mc_free", &mc_free);
   m.def("comm_status", &comm_status);
   m.def("comm_status_clear", &comm_status_clear);
   m.def("allreduce", &allreduce);
@@ -164,7 +176,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("comm_max_blocks", &comm_max_blocks);
   py::class_<CommEngine>(m, "CommEngine")
       .def(py::init<int64_t, int64_t, std::vector<int64_t>, double, int64_t>())
-      .def("register_buffer", &CommEngine::register_buffer)
+      .def("register_buffer", &CommEngine::register_buffer, py::arg("ptrs"), py::arg("nbytes"), py::arg("mc_ptr") = 0)
+      .def("has_multicast", &CommEngine::has_multicast)
+      .def("allreduce_nvls", &CommEngine::allreduce_nvls, py::arg("t"), py::arg("scale"), py::arg("blocks"),
+           py::arg("lean"), py::arg("sq_pad"), py::arg("sq_base"), py::arg("sq_stride"))
+      .def("reduce_scatter_nvls", &CommEngine::reduce_scatter_nvls)
       .def("forget_buffers", &CommEngine::forget_buffers)
       .def("contains", &CommEngine::contains)
       .def("peer_ptrs", &CommEngine::peer_ptrs)

@@ -5,7 +5,9 @@
 // per GPU; every rank allocates its buffers with cudaMalloc, exports them with
 // cudaIpcGetMemHandle and maps its peers' buffers (the handles travel through the
 // rendezvous store).  Kernels then read and write peer memory directly with
-// ordinary loads and stores over NVLink - no TMA, no multicast.
+// ordinary loads and stores over NVLink - no TMA.  The optional NVLS methods
+// (allreduce_nvls, reduce_scatter_nvls) use multimem instructions on an NVSwitch
+// multicast mapping instead (see the NVLS section).
 //
 // Summation orders are fixed so results are bit-identical on every rank:
 //   ORDER_RANK   : x_0 + x_1 + ... + x_{W-1}        (dtrain "direct", comm.py:374-391)
@@ -57,6 +59,11 @@ int64_t reduce_scatter(std::vector<int64_t> sigs, int64_t rank, std::vector<int6
 int64_t all_gather(std::vector<int64_t> sigs, int64_t rank, std::vector<int64_t> bufs,
                    int64_t byte_offset, int64_t n, int64_t dtype, double timeout_s, int64_t blocks);
 int64_t device_barrier(std::vector<int64_t> sigs, int64_t rank, double timeout_s);
+int64_t allreduce_nvls(std::vector<int64_t> sigs, int64_t rank, int64_t mc_ptr, int64_t byte_offset, int64_t n,
+                       int64_t dtype, double scale, double timeout_s, int64_t blocks, bool lean,
+                       std::vector<int64_t> sq_pads, int64_t sq_base, int64_t sq_stride);
+int64_t reduce_scatter_nvls(std::vector<int64_t> sigs, int64_t rank, int64_t mc_ptr, int64_t byte_offset, int64_t n,
+                            int64_t out_ptr, double scale, int64_t sq_part_ptr, double timeout_s, int64_t blocks);
 
 enum : int { ORDER_RANK = 0, ORDER_CYCLIC = 1 };
 enum : int { DT_F32 = 0, DT_BF16 = 1 };
@@ -593,6 +600,202 @@ __global__ void __maxnreg__(LEAN ? DTB_LEAN_COMM_MAXNREG : 128)
   collective_end(c, 3);
 }
 
+// ---------------------------------------------------------------- NVLS
+// Switch-side reduction through an NVSwitch multicast mapping (one address that
+// covers the same offset of every rank's buffer, see vmm.cpp):
+//   multimem.ld_reduce  returns the sum over all ranks of the values at that offset,
+//                       added in the switch (fp32; bf16 pairs with fp32 accumulation);
+//   multimem.st         writes a value to that offset of every rank's buffer.
+// All-reduce: each rank reduces its share of the buffer with ld_reduce and stores
+// the (scaled) sums back through the multicast address, so every element is summed
+// once and every rank receives the same bits.  Per GPU that moves about
+// (1 + 1/W) x size each way over NVLink, against 2 (W-1)/W x size for the two-shot
+// kernel: less from W = 4 up.  The order of the switch's additions is the
+// hardware's, not the ring or rank order, so this path is an opt-in method
+// (ranks still agree bit for bit).  Reduce-scatter: each rank reduces its own
+// partition with ld_reduce and stores it locally; only 1/W of the data enters
+// each GPU.
+__device__ __forceinline__ float4 mm_ld_add_v4f32(const void* p) {
+  float4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ float mm_ld_add_f32(const void* p) {
+  float v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint4 mm_ld_add_v4bf16x2(const void* p) {
+  uint4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ void mm_st_v4f32(void* p, float4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(v.x), "f"(v.y),
+               "f"(v.z), "f"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void mm_st_v4bf16x2(void* p, uint4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void mm_st_f32(void* p, float v) {
+  asm volatile("multimem.st.relaxed.sys.global.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
+}
+
+constexpr int kNvlsUnroll = 4;  // independent switch reductions in flight per thread
+
+// Scale one reduced 16-byte vector and add its squares to `s` (fp64).
+__device__ __forceinline__ float4 nvls_scale(float4 v, float scale, bool want_sq, double& s) {
+  v.x *= scale; v.y *= scale; v.z *= scale; v.w *= scale;
+  if (want_sq) s += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
+  return v;
+}
+__device__ __forceinline__ uint4 nvls_scale(uint4 v, float scale, bool want_sq, double& s) {
+  uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    float lo = __uint_as_float(w[e] << 16) * scale, hi = __uint_as_float(w[e] & 0xffff0000u) * scale;
+    if (want_sq) s += (double)lo * lo + (double)hi * hi;
+    w[e] = pack_bf16x2(lo, hi);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// All-reduce through the switch.  The buffer is split into 16-byte vectors; rank r
+// owns vectors chunk_bounds(nvec, W, r), and rank 0 also owns the fp32 elements
+// before the first and after the last whole vector (a buffer that does not start on
+// a 16-byte boundary; bf16 buffers must, and hold whole vectors).  `mc` is the
+// multicast address of the data.  With `sq` each CTA publishes the sum of squares
+// of the values it stored, as the two-shot kernel does.  LEAN: 128-thread CTAs that
+// fit beside a GEMM or attention CTA (buckets reduced during backward).
+template <typename T, bool LEAN>
+__global__ void __maxnreg__(LEAN ? DTB_LEAN_COMM_MAXNREG : 128)
+    allreduce_nvls_kernel(CommCtx c, char* mc, long n, float scale, SqOut sq) {
+  using V = typename std::conditional<std::is_same<T, float>::value, float4, uint4>::type;
+  constexpr int kPerVec = 16 / (int)sizeof(T);
+  DTB_SHARED_COPY(SqOut, s_sq, sq)
+  if (threadIdx.x == 0) {
+    s_sq.base = sq.base;
+    s_sq.stride = sq.stride;
+  }
+  collective_begin(c);
+  if (cta_enter(c)) {
+    const bool want_sq = s_sq.p[0] != nullptr;
+    // elements before the first 16-byte boundary (fp32 only), then whole vectors
+    const long head = min(n, (long)((16 - (reinterpret_cast<uintptr_t>(mc) & 15)) & 15) / (long)sizeof(T));
+    char* mv = mc + head * (long)sizeof(T);
+    const long nvec = (n - head) / kPerVec;
+    long lo, hi, a, b;
+    chunk_bounds(nvec, c.world, c.rank, lo, hi);
+    cta_slice(lo, hi, a, b);
+    double s = 0.0;
+    const long stride = (long)blockDim.x;
+    for (long v0 = a + threadIdx.x; v0 < b; v0 += kNvlsUnroll * stride) {
+      V x[kNvlsUnroll];
+#pragma unroll
+      for (int u = 0; u < kNvlsUnroll; ++u) {
+        const long v = v0 + u * stride;
+        if (v < b) {
+          if constexpr (std::is_same<T, float>::value) x[u] = mm_ld_add_v4f32(mv + v * 16);
+          else x[u] = mm_ld_add_v4bf16x2(mv + v * 16);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kNvlsUnroll; ++u) {
+        const long v = v0 + u * stride;
+        if (v < b) {
+          const V y = nvls_scale(x[u], scale, want_sq, s);
+          if constexpr (std::is_same<T, float>::value) mm_st_v4f32(mv + v * 16, y);
+          else mm_st_v4bf16x2(mv + v * 16, y);
+        }
+      }
+    }
+    if constexpr (std::is_same<T, float>::value) {
+      if (c.rank == 0 && blockIdx.x == 0) {
+        const long tail = head + nvec * kPerVec;
+        for (long i = threadIdx.x; i < head + (n - tail); i += stride) {
+          const long e = i < head ? i : tail + (i - head);
+          const float y = mm_ld_add_f32(mc + e * 4) * scale;
+          if (want_sq) s += (double)y * y;
+          mm_st_f32(mc + e * 4, y);
+        }
+      }
+    }
+    if (want_sq) publish_sq<LEAN ? kLeanThreads : kCommThreads>(c, s_sq, s);
+    cta_barrier(c, c.epoch + 1);
+  }
+  collective_end(c, 2);
+}
+
+// Reduce-scatter (fp32) through the switch: this rank's partition
+// chunk_bounds(n, W, rank) of the buffer is summed over ranks by ld_reduce, scaled
+// and stored into `out` (this rank's buffer, same index space).  The partition's
+// unaligned head and tail elements go through scalar reductions.  With sq_part,
+// CTA b writes the fp64 sum of squares of its slice to sq_part[b].
+__global__ void __launch_bounds__(kCommThreads)
+    reduce_scatter_nvls_kernel(CommCtx c, const char* mc, float* out, long n, float scale, double* sq_part) {
+  __shared__ double red[kCommThreads / 32];
+  collective_begin(c);
+  if (cta_enter(c)) {
+    long lo, hi;
+    chunk_bounds(n, c.world, c.rank, lo, hi);
+    const long vlo = (lo + 3) / 4, vhi = hi / 4;  // whole 16-byte vectors inside [lo, hi)
+    double s = 0.0;
+    const long stride = (long)blockDim.x;
+    if (vlo < vhi) {
+      long a, b;
+      cta_slice(vlo, vhi, a, b);
+      for (long v0 = a + threadIdx.x; v0 < b; v0 += kNvlsUnroll * stride) {
+        float4 x[kNvlsUnroll];
+#pragma unroll
+        for (int u = 0; u < kNvlsUnroll; ++u) {
+          const long v = v0 + u * stride;
+          if (v < b) x[u] = mm_ld_add_v4f32(mc + v * 16);
+        }
+#pragma unroll
+        for (int u = 0; u < kNvlsUnroll; ++u) {
+          const long v = v0 + u * stride;
+          if (v < b) *reinterpret_cast<float4*>(out + v * 4) = nvls_scale(x[u], scale, sq_part != nullptr, s);
+        }
+      }
+    }
+    if (blockIdx.x == 0) {
+      // elements of [lo, hi) outside the whole vectors (all of them if there are none)
+      const long h_end = vlo < vhi ? vlo * 4 : hi, t_beg = vlo < vhi ? vhi * 4 : hi;
+      for (long i = lo + threadIdx.x; i < h_end; i += stride) {
+        const float y = mm_ld_add_f32(mc + i * 4) * scale;
+        s += (double)y * y;
+        out[i] = y;
+      }
+      for (long i = t_beg + threadIdx.x; i < hi; i += stride) {
+        const float y = mm_ld_add_f32(mc + i * 4) * scale;
+        s += (double)y * y;
+        out[i] = y;
+      }
+    }
+    if (sq_part) {
+      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+        sq_part[blockIdx.x] = t;
+      }
+    }
+    cta_barrier(c, c.epoch + 1);
+  }
+  collective_end(c, 2);
+}
+
 // Sum of fp64 partials pad[r * stride + s] over ranks r < world and slots
 // lo <= s < hi, in a fixed order (thread t sums the linear indices t, t+1024, ...
 // of that range in order, then a fixed shuffle tree): the same bits on every rank.
@@ -1124,11 +1327,71 @@ int64_t allreduce(std::vector<int64_t> sigs, int64_t rank, std::vector<int64_t> 
       }
     }
   } else if (lean) {
-    DTB_TWOSHOT(bf16, 0, true);
+    switch (c.world) {
+      case 2: DTB_TWOSHOT(bf16, 2, true); break;
+      case 4: DTB_TWOSHOT(bf16, 4, true); break;
+      case 8: DTB_TWOSHOT(bf16, 8, true); break;
+      default: DTB_TWOSHOT(bf16, 0, true);
+    }
   } else {
-    DTB_TWOSHOT(bf16, 0, false);
+    switch (c.world) {
+      case 2: DTB_TWOSHOT(bf16, 2, false); break;
+      case 4: DTB_TWOSHOT(bf16, 4, false); break;
+      case 8: DTB_TWOSHOT(bf16, 8, false); break;
+      default: DTB_TWOSHOT(bf16, 0, false);
+    }
   }
 #undef DTB_TWOSHOT
+  count_launch();
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return nb;
+}
+
+// All-reduce through the switch (see allreduce_nvls_kernel): `mc_ptr` is the
+// multicast address of the buffer that holds the data at `byte_offset`.
+int64_t allreduce_nvls(std::vector<int64_t> sigs, int64_t rank, int64_t mc_ptr, int64_t byte_offset, int64_t n,
+                       int64_t dtype, double scale, double timeout_s, int64_t blocks, bool lean,
+                       std::vector<int64_t> sq_pads, int64_t sq_base, int64_t sq_stride) {
+  TORCH_CHECK(mc_ptr != 0, "allreduce_nvls: the buffer has no multicast mapping");
+  TORCH_CHECK(dtype == DT_F32 ? (mc_ptr + byte_offset) % 4 == 0 : ((mc_ptr + byte_offset) % 16 == 0 && n % 8 == 0),
+              "allreduce_nvls: fp32 data must be 4-byte aligned; bf16 data must start on a 16-byte boundary and "
+              "hold a multiple of 8 elements");
+  CommCtx c = make_ctx(sigs, rank, timeout_s, op_tag(8, n, dtype));
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  const long nbytes = n * (dtype == DT_F32 ? 4 : 2);
+  const int nb = lean ? lean_blocks(nbytes, blocks) : comm_blocks(nbytes, blocks);
+  const SqOut sq = make_sq(sq_pads, sq_base, sq_stride, c.world, nb);
+  char* mc = reinterpret_cast<char*>(mc_ptr) + byte_offset;
+  const float sc = (float)scale;
+  if (lean) {
+    if (dtype == DT_F32) {
+      prefer_max_shared(allreduce_nvls_kernel<float, true>);
+      allreduce_nvls_kernel<float, true><<<nb, kLeanThreads, 0, st>>>(c, mc, n, sc, sq);
+    } else {
+      prefer_max_shared(allreduce_nvls_kernel<bf16, true>);
+      allreduce_nvls_kernel<bf16, true><<<nb, kLeanThreads, 0, st>>>(c, mc, n, sc, sq);
+    }
+  } else if (dtype == DT_F32) {
+    allreduce_nvls_kernel<float, false><<<nb, kCommThreads, 0, st>>>(c, mc, n, sc, sq);
+  } else {
+    allreduce_nvls_kernel<bf16, false><<<nb, kCommThreads, 0, st>>>(c, mc, n, sc, sq);
+  }
+  count_launch();
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return nb;
+}
+
+// Reduce-scatter (fp32) through the switch into this rank's partition of `out_ptr`.
+int64_t reduce_scatter_nvls(std::vector<int64_t> sigs, int64_t rank, int64_t mc_ptr, int64_t byte_offset, int64_t n,
+                            int64_t out_ptr, double scale, int64_t sq_part_ptr, double timeout_s, int64_t blocks) {
+  TORCH_CHECK(mc_ptr != 0 && out_ptr != 0 && (mc_ptr + byte_offset) % 16 == 0 && out_ptr % 16 == 0,
+              "reduce_scatter_nvls: 16-byte aligned multicast data and output expected");
+  CommCtx c = make_ctx(sigs, rank, timeout_s, op_tag(9, n, DT_F32));
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  const int nb = comm_blocks(n * 4, blocks);
+  reduce_scatter_nvls_kernel<<<nb, kCommThreads, 0, st>>>(c, reinterpret_cast<const char*>(mc_ptr) + byte_offset,
+                                                          reinterpret_cast<float*>(out_ptr), n, (float)scale,
+                                                          reinterpret_cast<double*>(sq_part_ptr));
   count_launch();
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return nb;
@@ -1165,7 +1428,15 @@ int64_t reduce_scatter(std::vector<int64_t> sigs, int64_t rank, std::vector<int6
       default: reduce_scatter_kernel<float, float, 0><<<nb, kCommThreads, 0, st>>>(c, in, o, n, od, sc, sq);
     }
   } else {
-    reduce_scatter_kernel<bf16, bf16, 0><<<nb, kCommThreads, 0, st>>>(c, in, reinterpret_cast<bf16*>(out), n, (int)order, (float)scale, sq);
+    auto* o = reinterpret_cast<bf16*>(out);
+    const int od = (int)order;
+    const float sc = (float)scale;
+    switch (c.world) {
+      case 2: reduce_scatter_kernel<bf16, bf16, 2><<<nb, kCommThreads, 0, st>>>(c, in, o, n, od, sc, sq); break;
+      case 4: reduce_scatter_kernel<bf16, bf16, 4><<<nb, kCommThreads, 0, st>>>(c, in, o, n, od, sc, sq); break;
+      case 8: reduce_scatter_kernel<bf16, bf16, 8><<<nb, kCommThreads, 0, st>>>(c, in, o, n, od, sc, sq); break;
+      default: reduce_scatter_kernel<bf16, bf16, 0><<<nb, kCommThreads, 0, st>>>(c, in, o, n, od, sc, sq);
+    }
   }
   count_launch();
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -1306,16 +1577,57 @@ int64_t zero_rs_adamw(std::vector<int64_t> sigs, int64_t rank, std::vector<int64
 CommEngine::CommEngine(int64_t rank, int64_t world, std::vector<int64_t> sigs, double timeout_s, int64_t blocks)
     : rank_(rank), world_(world), sigs_(std::move(sigs)), timeout_(timeout_s), blocks_(blocks) {}
 
-int64_t CommEngine::register_buffer(std::vector<int64_t> ptrs, int64_t nbytes) {
+static int64_t dt_code(const torch::Tensor& t) {
+  if (t.scalar_type() == at::kFloat) return DT_F32;
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16, "NVLink collectives support float32 and bfloat16");
+  return DT_BF16;
+}
+
+int64_t CommEngine::register_buffer(std::vector<int64_t> ptrs, int64_t nbytes, int64_t mc_ptr) {
   TORCH_CHECK((int64_t)ptrs.size() == world_, "register_buffer: one pointer per rank expected");
   bufs_.push_back(std::move(ptrs));
   sizes_.push_back(nbytes);
+  mcs_.push_back(mc_ptr);
   return (int64_t)bufs_.size() - 1;
 }
 
 void CommEngine::forget_buffers() {
   bufs_.clear();
   sizes_.clear();
+  mcs_.clear();
+}
+
+bool CommEngine::has_multicast(torch::Tensor t) const {
+  int64_t id, off;
+  return locate(t, id, off) && mcs_[id] != 0;
+}
+
+int64_t CommEngine::allreduce_nvls(torch::Tensor t, double scale, int64_t blocks, bool lean,
+                                   c10::optional<torch::Tensor> sq_pad, int64_t sq_base, int64_t sq_stride) {
+  int64_t id, off;
+  TORCH_CHECK(t.is_contiguous() && locate(t, id, off) && mcs_[id] != 0,
+              "allreduce_nvls: tensor is not in a multicast-mapped buffer");
+  std::vector<int64_t> pads;
+  if (sq_pad && sq_pad->defined()) {
+    TORCH_CHECK(sq_pad->scalar_type() == at::kDouble, "allreduce_nvls: the sum-of-squares pad must be fp64");
+    pads = peer_ptrs(*sq_pad);
+    TORCH_CHECK(sq_pad->numel() >= world_ * sq_stride, "allreduce_nvls: sum-of-squares pad too small");
+  }
+  ++issued_;
+  return dtb::allreduce_nvls(sigs_, rank_, mcs_[id], off, t.numel(), dt_code(t), scale, timeout_,
+                             blocks > 0 ? blocks : blocks_, lean, pads, sq_base, sq_stride);
+}
+
+torch::Tensor CommEngine::reduce_scatter_nvls(torch::Tensor flat, double scale, int64_t sq_part_ptr, int64_t blocks) {
+  int64_t id, off;
+  TORCH_CHECK(flat.is_contiguous() && flat.scalar_type() == at::kFloat && locate(flat, id, off) && mcs_[id] != 0,
+              "reduce_scatter_nvls: fp32 tensor in a multicast-mapped buffer expected");
+  ++issued_;
+  dtb::reduce_scatter_nvls(sigs_, rank_, mcs_[id], off, flat.numel(), reinterpret_cast<int64_t>(flat.data_ptr()),
+                           scale, sq_part_ptr, timeout_, blocks > 0 ? blocks : blocks_);
+  const int64_t n = flat.numel(), base = n / world_, extra = n % world_;
+  const int64_t lo = rank_ * base + std::min(rank_, extra);
+  return flat.narrow(0, lo, base + (rank_ < extra ? 1 : 0));
 }
 
 bool CommEngine::locate(const torch::Tensor& t, int64_t& id, int64_t& off) const {
@@ -1335,12 +1647,6 @@ bool CommEngine::locate(const torch::Tensor& t, int64_t& id, int64_t& off) const
 bool CommEngine::contains(torch::Tensor t) const {
   int64_t id, off;
   return locate(t, id, off);
-}
-
-static int64_t dt_code(const torch::Tensor& t) {
-  if (t.scalar_type() == at::kFloat) return DT_F32;
-  TORCH_CHECK(t.scalar_type() == at::kBFloat16, "NVLink collectives support float32 and bfloat16");
-  return DT_BF16;
 }
 
 int64_t CommEngine::allreduce_inplace(torch::Tensor t, int64_t order, double scale, int64_t blocks, bool lean,

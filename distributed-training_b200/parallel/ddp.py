@@ -14,6 +14,10 @@ overlap=True, algo="ring")``, ``no_sync()``, ``finish()``, ``comm_wait_s``.
 * ``finish()`` zero-fills gradients of parameters that received none, waits
   for all reductions and leaves the averaged gradient in ``p.grad``.
 
+``method="nvls"`` (a group made with ``nvls=True``) reduces the buckets in the
+NVSwitch instead (multimem.ld_reduce / multimem.st): every rank still ends with the
+same bits, in the switch's summation order rather than ``algo``'s.
+
 GPU path (``pg`` is an ``NVLinkGroup``): the model's parameters and gradients
 are moved into flat peer-mapped buffers, so every bucket is a contiguous slice
 of the flat gradient that the backward kernels already wrote.  The bucket
@@ -131,7 +135,7 @@ class DDP:
         self._flat_blocks = pg.collective_blocks(self.flat.n * self.flat.grad.element_size(), lean=False)
         self._sq_lo_flat, self._sq_hi_flat = cur, cur + self._flat_blocks
         self._sq_stride = cur + self._flat_blocks
-        # the two-shot kernel publishes the sums of squares; one-shot (method="oneshot") does not
+        # the two-shot and NVLS kernels publish the sums of squares; one-shot does not
         self.fused_norm = pg.world > 1 and self.method != "oneshot"
         self._sq_pad = pg.alloc(pg.world * self._sq_stride, torch.float64) if self.fused_norm else None
         # global sum of squares of the averaged gradient, written by finish()
@@ -208,7 +212,7 @@ class DDP:
             if self.method == "oneshot":
                 kw = dict(method="oneshot")
             else:
-                kw = dict(method="twoshot", blocks=b.blocks, lean=b.lean,
+                kw = dict(method="nvls" if self.method == "nvls" else "twoshot", blocks=b.blocks, lean=b.lean,
                           sq=(self._sq_pad, b.sq_base, self._sq_stride) if self.fused_norm else None)
             if self.overlap:
                 b.work = self.pg.allreduce_async(g, self.algo, scale=1.0 / self.pg.world, **kw, **kw_trace)
@@ -305,8 +309,8 @@ class DDP:
         if self.method == "oneshot":
             self.pg.allreduce(self.flat.grad, self.algo, scale=1.0 / self.pg.world, method="oneshot")
         else:
-            self.pg.allreduce(self.flat.grad, self.algo, scale=1.0 / self.pg.world, method="twoshot",
-                              blocks=self._flat_blocks,
+            self.pg.allreduce(self.flat.grad, self.algo, scale=1.0 / self.pg.world,
+                              method="nvls" if self.method == "nvls" else "twoshot", blocks=self._flat_blocks,
                               sq=(self._sq_pad, self._sq_lo_flat, self._sq_stride) if self.fused_norm else None)
         self._stamp(3 * len(self.buckets) + 1)
         if self.fused_norm:

@@ -76,24 +76,18 @@ class FdExchange:
         self.calls = 0
         self.pending: dict[tuple[int, int], tuple[int, int]] = {}
 
-    def all_gather(self, fd: int, size: int) -> list[tuple[int, int] | None]:
-        """Returns, per rank, (received descriptor, size) - None at this rank's index.
-        The caller owns the received descriptors."""
-        tag = self.calls
-        self.calls += 1
+    def _send(self, p: int, tag: int, fd: int, size: int):
         hdr = struct.pack("<iiq", self.rank, tag, int(size))
-        for p in range(self.world):
-            if p == self.rank:
-                continue
-            with socket.socket(socket.AF_UNIX, socket.SOCK_STREAM) as c:
-                c.settimeout(self.timeout)
-                c.connect(self.names[p])
-                socket.send_fds(c, [hdr], [int(fd)])
-        out: list[tuple[int, int] | None] = [None] * self.world
-        need = {p for p in range(self.world) if p != self.rank}
+        with socket.socket(socket.AF_UNIX, socket.SOCK_STREAM) as c:
+            c.settimeout(self.timeout)
+            c.connect(self.names[p])
+            socket.send_fds(c, [hdr], [int(fd)])
+
+    def _collect(self, tag: int, need: set[int]) -> dict[int, tuple[int, int]]:
+        got: dict[int, tuple[int, int]] = {}
         for p in list(need):
             if (tag, p) in self.pending:
-                out[p] = self.pending.pop((tag, p))
+                got[p] = self.pending.pop((tag, p))
                 need.discard(p)
         while need:
             try:
@@ -107,14 +101,37 @@ class FdExchange:
                 raise CommError("descriptor exchange: malformed message")
             r, t, sz = struct.unpack("<iiq", msg)
             if t == tag and r in need:
-                out[r] = (fds[0], sz)
+                got[r] = (fds[0], sz)
                 need.discard(r)
             elif t > tag:
                 self.pending[(t, r)] = (fds[0], sz)
             else:
                 os.close(fds[0])
                 raise CommError(f"descriptor exchange: rank {r} sent call {t} during call {tag}")
-        return out
+        return got
+
+    def all_gather(self, fd: int, size: int) -> list[tuple[int, int] | None]:
+        """Returns, per rank, (received descriptor, size) - None at this rank's index.
+        The caller owns the received descriptors."""
+        tag = self.calls
+        self.calls += 1
+        for p in range(self.world):
+            if p != self.rank:
+                self._send(p, tag, fd, size)
+        got = self._collect(tag, {p for p in range(self.world) if p != self.rank})
+        return [got.get(p) for p in range(self.world)]
+
+    def broadcast(self, fd: int | None, size: int, root: int = 0) -> tuple[int, int] | None:
+        """``root`` sends its descriptor to every other rank; the others return
+        (received descriptor, size), which they own; the root returns None."""
+        tag = self.calls
+        self.calls += 1
+        if self.rank == root:
+            for p in range(self.world):
+                if p != root:
+                    self._send(p, tag, fd, size)
+            return None
+        return self._collect(tag, {root})[root]
 
     def close(self):
         self.sock.close()
@@ -126,14 +143,21 @@ class FdExchange:
 class SymmetricBuffer:
     """One peer-mapped allocation: a local tensor view plus every rank's base pointer."""
 
-    def __init__(self, group: "NVLinkGroup", nbytes: int):
+    def __init__(self, group: "NVLinkGroup", nbytes: int, multicast: bool = False):
         C = lib()
         self.nbytes = int(nbytes)
         self.vmm = group.memory == "vmm"
         self.ptrs = []
         self._opened = []
+        self.mc_ptr = 0  # NVSwitch multicast address of this buffer (0: none)
+        if multicast and not self.vmm:
+            raise ValueError("a multicast-mapped buffer needs memory='vmm'")
         if self.vmm:
-            ptr, fd, size = C.vmm_alloc(max(self.nbytes, 256))
+            want = max(self.nbytes, 256)
+            if multicast:  # the whole allocation is bound to the multicast object
+                g = group._mc_gran
+                want = (want + g - 1) // g * g
+            ptr, fd, size = C.vmm_alloc(want)
             self.ptr = int(ptr)
             try:
                 got = group._fdx.all_gather(fd, size)
@@ -153,6 +177,8 @@ class SymmetricBuffer:
                     os.close(pfd)
                 self.ptrs.append(p)
                 self._opened.append(p)
+            if multicast:
+                self.mc_ptr = self._map_multicast(group, int(size))
         else:
             ptr, handle = C.symm_alloc(max(self.nbytes, 256))
             self.ptr = int(ptr)
@@ -166,6 +192,27 @@ class SymmetricBuffer:
                     self.ptrs.append(p)
                     self._opened.append(p)
         self.device = group.device
+
+    def _map_multicast(self, group: "NVLinkGroup", size: int) -> int:
+        """Rank 0 creates an NVSwitch multicast object of ``size`` bytes and passes it
+        to the others by file descriptor; each rank binds this buffer's allocation to
+        it and maps it.  Returns the multicast address."""
+        C = lib()
+        if group.rank == 0:
+            mc, fd = C.mc_create(size, group.world)
+            try:
+                group._fdx.broadcast(fd, size, root=0)
+            finally:
+                os.close(fd)
+        else:
+            fd, psize = group._fdx.broadcast(None, 0, root=0)
+            try:
+                if psize != size:
+                    raise CommError(f"multicast: rank 0 made {psize} bytes, this rank needs {size}")
+                mc = C.mc_import(fd)
+            finally:
+                os.close(fd)
+        return int(C.mc_bind_map(mc, self.ptr, size, group.world))
 
     def tensor(self, numel: int, dtype: torch.dtype, byte_offset: int = 0) -> torch.Tensor:
         assert byte_offset + numel * torch.tensor([], dtype=dtype).element_size() <= self.nbytes
@@ -181,6 +228,9 @@ class SymmetricBuffer:
 
     def free(self):
         C = lib()
+        if self.mc_ptr:
+            C.mc_free(self.mc_ptr)
+            self.mc_ptr = 0
         for p in self._opened:
             if self.vmm:
                 C.vmm_free(p)
@@ -217,7 +267,7 @@ class NVLinkGroup:
     backend = "nvlink"
 
     def __init__(self, rank: int, world: int, device, exchange, timeout: float = 60.0, blocks: int = 0,
-                 comm_priority: int = 0, memory: str | None = None):
+                 comm_priority: int = 0, memory: str | None = None, nvls: bool | None = None):
         """``exchange(key, payload: bytes) -> list[bytes]`` is the bootstrap all-gather
         (over the rendezvous store or torch.distributed); it is used only at set-up.
         ``blocks`` caps the CTAs of one collective kernel (0: sized by the message);
@@ -225,7 +275,10 @@ class NVLinkGroup:
         collectives (lower is more urgent: -1 lets their CTAs take SMs ahead of queued
         compute work); ``memory`` is "ipc" (cudaMalloc + IPC handles, the default) or
         "vmm" (CUDA VMM allocations shared by file descriptor); the environment
-        variable DTB_PEER_MEMORY sets the default."""
+        variable DTB_PEER_MEMORY sets the default.  ``nvls`` (default: the
+        environment variable DTB_NVLS=1) also maps every buffer from ``alloc`` through
+        an NVSwitch multicast object, which enables ``method="nvls"`` (switch-side
+        reduction with multimem instructions); it implies ``memory="vmm"``."""
         if world > int(lib().comm_max_ranks()):
             raise ValueError(f"NVLinkGroup supports up to {lib().comm_max_ranks()} ranks per node")
         self.rank, self.world = int(rank), int(world)
@@ -233,9 +286,20 @@ class NVLinkGroup:
         self.blocks = int(blocks)
         self._exchange_fn = exchange
         self._nalloc = 0
-        self.memory = (memory or os.environ.get("DTB_PEER_MEMORY", "ipc")).lower()
+        self.nvls = bool(int(os.environ.get("DTB_NVLS", "0"))) if nvls is None else bool(nvls)
+        self.nvls = self.nvls and self.world > 1
+        self.memory = (memory or os.environ.get("DTB_PEER_MEMORY", "vmm" if self.nvls else "ipc")).lower()
         if self.memory not in ("ipc", "vmm"):
             raise ValueError(f"unknown peer memory kind {self.memory!r} (ipc or vmm)")
+        if self.nvls and self.memory != "vmm":
+            raise ValueError("NVLS collectives need memory='vmm' (multicast objects bind VMM allocations)")
+        self._mc_gran = 0
+        if self.nvls:
+            with torch.cuda.device(self.device):
+                if not lib().mc_supported():
+                    raise CommError("NVLS requested but this GPU does not support NVSwitch multicast")
+                self._mc_gran = int(lib().mc_granularity(self.world))
+        self._closes = 0
         self._fdx = FdExchange(self.rank, self.world, exchange, timeout) if self.memory == "vmm" else None
         self.seq = 0            # collectives issued
         self.buffers: list[SymmetricBuffer] = []
@@ -269,18 +333,19 @@ class NVLinkGroup:
     def _exchange(self, key: str, payload: bytes) -> list[bytes]:
         return self._exchange_fn(key, payload)
 
-    def _new_buffer(self, nbytes: int) -> SymmetricBuffer:
-        b = SymmetricBuffer(self, nbytes)
+    def _new_buffer(self, nbytes: int, multicast: bool = False) -> SymmetricBuffer:
+        b = SymmetricBuffer(self, nbytes, multicast=multicast)
         self.buffers.append(b)
         if self._eng is not None:
-            self._eng.register_buffer(b.ptrs, b.nbytes)
+            self._eng.register_buffer(b.ptrs, b.nbytes, b.mc_ptr)
         return b
 
     def alloc(self, numel: int, dtype: torch.dtype = torch.float32) -> torch.Tensor:
-        """Collective: a zero-filled peer-mapped tensor (same size on every rank)."""
+        """Collective: a zero-filled peer-mapped tensor (same size on every rank);
+        multicast-mapped too when the group was made with ``nvls``."""
         esz = torch.tensor([], dtype=dtype).element_size()
         with torch.cuda.device(self.device):
-            buf = self._new_buffer(int(numel) * esz)
+            buf = self._new_buffer(int(numel) * esz, multicast=self.nvls)
         return buf.tensor(numel, dtype)
 
     def _locate(self, t: torch.Tensor):
@@ -302,7 +367,7 @@ class NVLinkGroup:
         if self._staging is None or self._staging.nbytes < nbytes:
             # growth is collective: every rank stages the same sizes in the same order
             self.synchronize()
-            self._staging = self._new_buffer(max(nbytes, 1 << 20))
+            self._staging = self._new_buffer(max(nbytes, 1 << 20), multicast=self.nvls)
         return self._staging
 
     def check(self):
@@ -331,8 +396,12 @@ class NVLinkGroup:
         ``algo`` selects the summation order: "ring" (dtrain ring order) or
         "direct" (rank order).  ``method`` selects the data movement: "oneshot"
         (every rank reduces everything: latency-optimal), "twoshot" (reduce-scatter
-        + all-gather: bandwidth-optimal) or "auto" (one-shot up to
-        ``ONESHOT_MAX_BYTES``, two-shot above).  Two-shot on a peer-mapped tensor
+        + all-gather: bandwidth-optimal), "nvls" (sums formed in the NVSwitch by
+        multimem.ld_reduce and written to every rank by multimem.st: the least
+        NVLink traffic from 4 ranks up; needs a group made with ``nvls``; every rank
+        gets the same bits, but the order of the additions is the switch's, so
+        ``algo`` does not apply) or "auto" (one-shot up to ``ONESHOT_MAX_BYTES``,
+        two-shot above).  Two-shot on a peer-mapped tensor
         also takes ``blocks`` (CTA count, 0: by size), ``lean`` (128-thread CTAs
         that share SMs with running GEMMs) and ``sq = (pad, base, stride)``: CTA b
         writes the sum of squares of the scaled values it reduced into slot
@@ -350,6 +419,8 @@ class NVLinkGroup:
         nbytes = n * t.element_size()
         if method == "auto":
             method = "oneshot" if (nbytes <= ONESHOT_MAX_BYTES and not lean and sq is None) else "twoshot"
+        if method == "nvls":
+            return self._allreduce_nvls(t, scale, blocks, sq, lean)
         if method == "twoshot" and self._eng.contains(t):
             # fast path: one native call, in place on the peer-mapped tensor
             pad, base, stride = sq if sq is not None else (None, 0, 0)
@@ -385,6 +456,29 @@ class NVLinkGroup:
         self._issued()
         return t
 
+    def _allreduce_nvls(self, t: torch.Tensor, scale: float, blocks: int, sq, lean: bool = False):
+        if not self.nvls:
+            raise ValueError("method='nvls' needs a group made with nvls=True (DTB_NVLS=1)")
+        n, esz = t.numel(), t.element_size()
+        # fp32: any 4-byte aligned start; bf16: whole 16-byte vectors only
+        ok = t.dtype == torch.float32 or (t.data_ptr() % 16 == 0 and n % 8 == 0)
+        if self._eng.has_multicast(t) and ok:
+            pad, base, stride = sq if sq is not None else (None, 0, 0)
+            self._eng.allreduce_nvls(t, scale, int(blocks or self.blocks), bool(lean), pad, int(base), int(stride))
+            self.seq += 1
+            return t
+        if sq is not None or lean:
+            raise ValueError("a lean or sum-of-squares NVLS all-reduce needs a tensor from alloc()")
+        if not ok:  # bf16 that does not form whole 16-byte vectors
+            return self.allreduce(t, scale=scale, method="twoshot", blocks=blocks)
+        stage = self._stage(n * esz)
+        buf = stage.tensor(n, t.dtype)
+        buf.copy_(t.reshape(-1))
+        self._eng.allreduce_nvls(buf, scale, int(blocks or self.blocks), False, None, 0, 0)
+        self.seq += 1
+        t.reshape(-1).copy_(buf)
+        return t
+
     def collective_blocks(self, nbytes: int, lean: bool = False) -> int:
         """CTAs an all-reduce of ``nbytes`` launches (``blocks=0``, this group's cap applied)."""
         return int(lib().collective_blocks(int(nbytes), int(self.blocks), bool(lean)))
@@ -395,10 +489,13 @@ class NVLinkGroup:
         lib().sq_total(pad, out, self.world, int(stride), int(lo), int(hi))
         return out
 
-    def reduce_scatter(self, flat: torch.Tensor, scale: float = 1.0, sq_parts: torch.Tensor | None = None):
-        """Sum over ranks (ring order); this rank's partition then holds the total.
-        Returns a view of it.  With ``sq_parts`` (fp64, symmetric) the kernel also
-        writes per-CTA sums of squares of the reduced partition."""
+    def reduce_scatter(self, flat: torch.Tensor, scale: float = 1.0, sq_parts: torch.Tensor | None = None,
+                       method: str = "ring"):
+        """Sum over ranks; this rank's partition then holds the total.  Returns a view
+        of it.  ``method``: "ring" (dtrain's ring order, bit-equal to it) or "nvls"
+        (fp32 sums formed in the NVSwitch; a group made with ``nvls``).  With
+        ``sq_parts`` (fp64, symmetric) the kernel also writes per-CTA sums of squares
+        of the reduced partition."""
         n = flat.numel()
         b = partition(n, self.world)
         if self.world > 1:
@@ -406,6 +503,12 @@ class NVLinkGroup:
                 raise ValueError("reduce_scatter needs a tensor allocated with NVLinkGroup.alloc")
             sqp = sq_parts.data_ptr() if sq_parts is not None else 0
             self.seq += 1
+            if method == "nvls":
+                if not (self.nvls and self._eng.has_multicast(flat)):
+                    raise ValueError("method='nvls' needs a tensor from alloc() of a group made with nvls=True")
+                return self._eng.reduce_scatter_nvls(flat, scale, sqp, self._rs_blocks())
+            if method != "ring":
+                raise ValueError(f"unknown reduce-scatter method {method!r} (ring or nvls)")
             return self._eng.reduce_scatter(flat, ORDER_CYCLIC, scale, sqp, self._rs_blocks())
         elif scale != 1.0:
             flat.mul_(scale)
@@ -480,6 +583,11 @@ class NVLinkGroup:
             torch.cuda.synchronize(self.device)
         except Exception:  # noqa: BLE001 - closing after a failure must not raise
             pass
+        if any(b.mc_ptr for b in self.buffers):
+            # no rank unbinds its memory from a multicast object while another rank's
+            # multimem instructions may still reach it
+            self._closes += 1
+            self._exchange(f"nvls-close/{self._closes}", b"")
         for b in self.buffers:
             b.free()
         self.buffers = []
@@ -512,7 +620,7 @@ def torch_exchange():
     return ex
 
 
-def from_env(device=None, timeout: float | None = None) -> NVLinkGroup:
+def from_env(device=None, timeout: float | None = None, nvls: bool | None = None) -> NVLinkGroup:
     """NVLinkGroup from RANK / WORLD_SIZE / STORE_ADDR (the launcher) or torchrun's env."""
     t = timeout if timeout is not None else float(os.environ.get("DTRAIN_TIMEOUT", "60"))
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
@@ -523,8 +631,8 @@ def from_env(device=None, timeout: float | None = None) -> NVLinkGroup:
         from ..utils.store import Store
         store = Store(os.environ["STORE_ADDR"], t)
         return NVLinkGroup(rank, world, dev, store_exchange(store, rank, world, os.environ.get("DTRAIN_PREFIX", "")),
-                           timeout=t)
+                           timeout=t, nvls=nvls)
     import torch.distributed as dist
     if not dist.is_initialized():
         raise RuntimeError("no STORE_ADDR and torch.distributed is not initialised")
-    return NVLinkGroup(rank, world, dev, torch_exchange(), timeout=t)
+    return NVLinkGroup(rank, world, dev, torch_exchange(), timeout=t, nvls=nvls)

@@ -6,7 +6,7 @@
 
 Every reference flag is kept; additions: ``--dtype bfloat16`` (bf16 compute with
 fp32 masters/grads on the sm_100a kernels), ``--data synthetic`` with ``--vocab``,
-``--device``, ``--algo {ring,direct}`` plus ``--ar-method {auto,oneshot,twoshot}``.
+``--device``, ``--algo {ring,direct}`` plus ``--ar-method {auto,oneshot,twoshot,nvls}``.
 
 ``--mode single --emulate-world W`` runs the exact global batch of a W-rank job
 in one process (the reference for equivalence tests).  One JSON line per step
@@ -61,7 +61,8 @@ def parse(argv=None):
     ap.add_argument("--bucket-mb", type=float, default=1.0)
     ap.add_argument("--no-overlap", action="store_true")
     ap.add_argument("--algo", choices=["ring", "direct"], default="ring")
-    ap.add_argument("--ar-method", choices=["auto", "oneshot", "twoshot"], default="auto")
+    ap.add_argument("--ar-method", choices=["auto", "oneshot", "twoshot", "nvls"], default="auto",
+                    help="GPU all-reduce data movement; nvls reduces in the NVSwitch (multicast memory)")
     ap.add_argument("--device", default=None, help="cpu | cuda (default: cuda for bfloat16, else cpu)")
     ap.add_argument("--gather-gemm", action="store_true",
                     help="ZeRO on GPUs: let the forward GEMMs pull their weights from the other ranks (all-gather "
@@ -422,7 +423,7 @@ def make_group(a, device):
             if not dist.is_initialized():
                 dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=float(
                     os.environ.get("DTRAIN_TIMEOUT", "60"))))
-        return from_env(device)
+        return from_env(device, nvls=(a.ar_method == "nvls") or None)
     from .parallel.comm import init_from_env
     return init_from_env()
 

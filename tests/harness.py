@@ -3,7 +3,7 @@
 ``run_ranks(world, body, *args, group=...)`` starts a rendezvous store and one
 spawned process per rank; each builds a process group of the requested kind
 (this stack's TCP group, the reference's TCP group from ``baseline/_ref``, or
-this stack's NVLink group on GPU ``rank``), calls ``body(pg, *args)`` and sends
+this stack's NVLink group on GPU ``rank``, optionally with NVSwitch multicast), calls ``body(pg, *args)`` and sends
 the result back.  Results come back in rank order; the first rank that raised
 makes the call raise (with that rank's traceback).  A body may also end its
 process on purpose (a crash test); ``expect`` then names the ranks whose
@@ -43,7 +43,7 @@ def _make_group(kind: str, rank: int, world: int, addr: str, timeout: float):
         sys.path.insert(0, REF)
         from dtrain.comm import ProcessGroup as RefGroup
         return RefGroup(rank, world, addr, timeout=timeout)
-    if kind == "nvlink":
+    if kind in ("nvlink", "nvls"):
         os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         import torch
         from dtrain_b200.parallel.nvlink import NVLinkGroup, store_exchange
@@ -51,18 +51,28 @@ def _make_group(kind: str, rank: int, world: int, addr: str, timeout: float):
         torch.cuda.set_device(rank)
         store = Store(addr, 60)
         return NVLinkGroup(rank, world, torch.device("cuda", rank), store_exchange(store, rank, world),
-                           timeout=timeout)
+                           timeout=timeout, nvls=(kind == "nvls"))
     raise ValueError(kind)
 
 
 def _rank_main(rank, world, addr, kind, timeout, body, args, q):
+    pg = None
     try:
         pg = _make_group(kind, rank, world, addr, timeout)
         res = body(pg, *args)
         pg.close()
+        pg = None
         q.put((rank, "ok", res))
     except BaseException as e:  # noqa: BLE001 - everything goes back to the test
         q.put((rank, "error", f"{e!r}\n{traceback.format_exc()}"))
+    finally:
+        # a multicast-mapped group is always closed (all ranks barrier, then unbind):
+        # a process must not exit with its memory still bound to the switch
+        if pg is not None and kind == "nvls":
+            try:
+                pg.close()
+            except BaseException:  # noqa: BLE001
+                pass
 
 
 def run_ranks(world: int, body, *args, group: str = "tcp", timeout: float = 30.0, wait_s: float = 240.0,
