@@ -21,7 +21,6 @@ followed by all-gather leaves on every rank, and the broadcast copy.
 """
 import argparse
 import datetime
-import hashlib
 import json
 import os
 import sys
@@ -38,10 +37,17 @@ from dtrain_b200.parallel.nvlink import NVLinkGroup, torch_exchange  # noqa: E40
 PEER_COPY_GBS = 770.0  # measured peer-copy bandwidth per direction on this pool's B200s
 
 
+def _fingerprint(t: torch.Tensor) -> int:
+    """64-bit position-weighted sum of the buffer's 32-bit words, on the device (a
+    difference in any word changes it)."""
+    w = t.contiguous().view(torch.int32).reshape(-1).long()
+    idx = torch.arange(w.numel(), device=w.device, dtype=torch.int64)
+    return int((w * ((idx * 2654435761 + 40503) % 2147483647 * 2 + 1)).sum().item()) & ((1 << 64) - 1)
+
+
 def same_on_all_ranks(t: torch.Tensor, world: int) -> bool:
-    h = hashlib.sha256(t.contiguous().view(torch.uint8).cpu().numpy().tobytes()).hexdigest()[:16]
     hs = [None] * world
-    dist.all_gather_object(hs, h)
+    dist.all_gather_object(hs, _fingerprint(t))
     return len(set(hs)) == 1
 
 
@@ -142,6 +148,12 @@ def main():
             if nbytes >= (1 << 20):  # a wider grid than the size-based default
                 res["ours_twoshot_b128"] = timed(lambda: pg.allreduce(x, "direct", method="twoshot", blocks=128),
                                                  iters, world)
+                if nbytes <= (16 << 20):
+                    res["ours_oneshot_b128"] = timed(
+                        lambda: pg.allreduce(x, "direct", method="oneshot", blocks=128), iters, world)
+                if a.nvls:
+                    res["ours_nvls_b128"] = timed(lambda: pg.allreduce(x, "direct", method="nvls", blocks=128),
+                                                  iters, world)
             res["nccl"] = timed(lambda: dist.all_reduce(y), iters, world)
             pg.check()
             # bit-identity across ranks of one fresh all-reduce
@@ -157,7 +169,7 @@ def main():
             for k, us in res.items():
                 emit({"op": "allreduce", "impl": k, "dtype": name, "bytes": nbytes, "us": round(us, 2),
                       "busbw_GBs": round(fac_ar * nbytes / us / 1e3, 2),
-                      "bit_identical": same["nvls" if k == "ours_nvls" else "ring"]})
+                      "bit_identical": same["nvls" if "nvls" in k else "ring"]})
         for nbytes in sizes(pow2=True):
             n = nbytes // esz
             if n % world:
@@ -224,8 +236,9 @@ def markdown(rows: list, world: int, timing: str = "") -> str:
                 rule += "---|---|"
             out += [f"### {op} {dt}", "", head, rule]
             for nb in sorted({r["bytes"] for r in sel}):
-                mine = [r for r in sel if r["bytes"] == nb and r["impl"] not in ("nccl", "ours_nvls")]
-                nv = [r for r in sel if r["bytes"] == nb and r["impl"] == "ours_nvls"]
+                mine = [r for r in sel if r["bytes"] == nb and r["impl"] != "nccl" and "nvls" not in r["impl"]]
+                nv = sorted((r for r in sel if r["bytes"] == nb and "nvls" in r["impl"]),
+                            key=lambda r: -r["busbw_GBs"])
                 nccl = [r for r in sel if r["bytes"] == nb and r["impl"] == "nccl"]
                 if op == "allreduce":  # the fastest fixed-order method at this size
                     best = max(mine, key=lambda r: r["busbw_GBs"])

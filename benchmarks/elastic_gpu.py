@@ -10,7 +10,7 @@ flags: ZeRO-1, bf16 compute with fp32 masters, synthetic tokens, the forward+bac
 CUDA graph.  The second job also checkpoints every ``--ckpt-every`` steps (sharded,
 SHA-256 manifest, atomic LATEST) and its rank ``--fail-rank`` leaves at
 ``--fail-at-step`` (between steps, after synchronising its GPU); the launcher stops the
-group once the survivors' collectives have timed out (``--timeout``) and starts a
+group (its SIGTERM aborts the survivors' waiting collectives) and starts a
 second attempt that resumes from the latest checkpoint.  No NVLS / multicast memory is
 used (a rank leaves on purpose).
 
@@ -61,7 +61,8 @@ def main():
     ap.add_argument("--ckpt-every", type=int, default=50)
     ap.add_argument("--fail-at-step", type=int, default=120)
     ap.add_argument("--fail-rank", type=int, default=1)
-    ap.add_argument("--timeout", type=float, default=15.0, help="collective timeout (s) that ends the survivors")
+    ap.add_argument("--timeout", type=float, default=60.0,
+                    help="collective timeout (s); a stopped worker aborts its waits at once, so this only bounds skew")
     ap.add_argument("--skip", type=int, default=5, help="steps left out of the throughput median")
     ap.add_argument("--device", choices=["cuda", "cpu"], default="cuda")
     ap.add_argument("--workdir", default=None)

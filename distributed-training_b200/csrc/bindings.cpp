@@ -56,6 +56,8 @@ torch::Tensor tensor_from_ptr(int64_t ptr, std::vector<int64_t> sizes, c10::Scal
 std::tuple<int64_t, int64_t, int64_t> vmm_alloc(int64_t nbytes);
 int64_t vmm_import(int64_t fd, int64_t size);
 void vmm_free(int64_t va);
+void comm_abort_prepare();
+void comm_abort(int64_t own_sig_ptr);
 bool mc_supported();
 int64_t mc_granularity(int64_t ndev);
 std::tuple<int64_t, int64_t> mc_create(int64_t size, int64_t ndev);
@@ -163,6 +165,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mc_free", &mc_free);
   m.def("comm_status", &comm_status);
   m.def("comm_status_clear", &comm_status_clear);
+  m.def("comm_abort_prepare", &comm_abort_prepare);
+  m.def("comm_abort", &comm_abort);
   m.def("allreduce", &allreduce);
   m.def("collective_blocks", &collective_blocks);
   m.def("sq_total", &sq_total);

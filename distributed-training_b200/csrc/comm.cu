@@ -39,6 +39,9 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <map>
+#include <mutex>
+
 #include "comm_engine.h"
 #include "common.cuh"
 
@@ -1171,6 +1174,48 @@ int64_t comm_status() {
 void comm_status_clear() {
   ensure_status();
   *reinterpret_cast<volatile int*>(g_host_status) = 0;
+}
+
+// Host-side abort of a process group.  comm_abort_prepare() (called when the group is
+// made) keeps a pinned word holding 1 and a non-blocking stream; comm_abort() copies
+// that word into this rank's "failed" slot (kFailWord of its own signal pad) with the
+// copy engine, so collectives that are waiting - including one the calling process is
+// blocked on in another thread - see it at their next check and return instead of
+// waiting out their timeout.  It also records kStatusAborted for check().
+namespace {
+std::mutex g_abort_mu;
+std::map<int, std::pair<cudaStream_t, uint32_t*>> g_abort;  // device -> (stream, pinned 1)
+}  // namespace
+
+void comm_abort_prepare() {
+  ensure_status();
+  int dev = 0;
+  C10_CUDA_CHECK(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> g(g_abort_mu);
+  if (g_abort.count(dev)) return;
+  cudaStream_t s;
+  C10_CUDA_CHECK(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+  uint32_t* one = nullptr;
+  C10_CUDA_CHECK(cudaHostAlloc(&one, sizeof(uint32_t), cudaHostAllocPortable));
+  *one = 1u;
+  g_abort[dev] = {s, one};
+}
+
+void comm_abort(int64_t own_sig_ptr) {
+  TORCH_CHECK(own_sig_ptr != 0, "comm_abort: no signal pad");
+  int dev = 0;
+  C10_CUDA_CHECK(cudaGetDevice(&dev));
+  std::pair<cudaStream_t, uint32_t*> a;
+  {
+    std::lock_guard<std::mutex> g(g_abort_mu);
+    auto it = g_abort.find(dev);
+    TORCH_CHECK(it != g_abort.end(), "comm_abort: comm_abort_prepare() was not called on this device");
+    a = it->second;
+  }
+  __atomic_store_n(g_host_status, (int)kStatusAborted, __ATOMIC_SEQ_CST);
+  uint32_t* word = reinterpret_cast<uint32_t*>(own_sig_ptr) + kFailWord;
+  C10_CUDA_CHECK(cudaMemcpyAsync(word, a.second, sizeof(uint32_t), cudaMemcpyHostToDevice, a.first));
+  C10_CUDA_CHECK(cudaStreamSynchronize(a.first));
 }
 
 // Descriptor of a collective: its kind, element count and dtype, mixed into 32 bits.

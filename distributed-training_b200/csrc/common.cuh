@@ -28,6 +28,7 @@ enum : int {
   kStatusPeerTimeout = 2,    // a cross-GPU flag wait ran out (peer dead or desynchronised)
   kStatusSeqMismatch = 3,    // a peer's flag carried an unexpected sequence number
   kStatusBadArgument = 4,
+  kStatusAborted = 5,        // the host aborted the process group (comm_abort)
 };
 
 // One status word per translation unit (kernels are compiled without relocatable

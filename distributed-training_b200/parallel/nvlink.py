@@ -306,6 +306,7 @@ class NVLinkGroup:
         self._eng = None
         with torch.cuda.device(self.device):
             lib().comm_status_clear()
+            lib().comm_abort_prepare()
             self._sig = self._new_buffer(_SIG_BYTES)
             # native state: signal pads, registered buffers, flag epoch, timeout
             self._eng = lib().CommEngine(self.rank, self.world, self._sig.ptrs, float(timeout), self.blocks)
@@ -374,6 +375,8 @@ class NVLinkGroup:
         """Raise CommError if a collective kernel timed out waiting for a peer, or found
         that the ranks had issued different collectives (desynchronised ranks)."""
         code = int(lib().comm_status())
+        if code == 5:
+            raise CommError(f"NVLink process group aborted on rank {self.rank} (abort() was called)")
         if code == 3:
             raise CommError(f"NVLink collective failed on rank {self.rank} (device status 3): collective desync - "
                             "the ranks issued different collectives (kind, size or dtype) at the same point")
@@ -384,6 +387,15 @@ class NVLinkGroup:
     def synchronize(self):
         torch.cuda.synchronize(self.device)
         self.check()
+
+    def abort(self):
+        """Make every collective of this rank that is waiting, or that is still to run,
+        give up at once (its "failed" word is set through the copy engine); ``check()``
+        then raises CommError.  Safe to call from another thread while this process is
+        blocked on the GPU - the way a stopping worker ends a wait for a peer that is
+        gone without waiting out the timeout.  The group is unusable afterwards."""
+        with torch.cuda.device(self.device):
+            lib().comm_abort(self._sig.ptr)
 
     # ---------------------------------------------------------- collectives
     def _order(self, algo: str) -> int:

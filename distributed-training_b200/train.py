@@ -430,12 +430,16 @@ def make_group(a, device):
 
 class _StopRequest:
     """SIGTERM (the launcher stopping an attempt) becomes a flag checked between
-    steps.  Python runs the handler only once the current call returns, so a worker
-    blocked on the GPU - e.g. in a collective waiting for a peer that is gone - exits
-    after that wait has timed out, not with its kernels still running."""
+    steps.  Python runs a signal handler only once the current call returns, so a
+    worker blocked on the GPU - e.g. in a collective waiting for a peer that is gone -
+    would otherwise only stop after that wait timed out.  With a GPU process group the
+    signal also reaches a watcher thread (through ``signal.set_wakeup_fd``, written by
+    the C-level handler at once), which aborts the group: the waiting collective
+    kernels give up immediately and the blocked call returns."""
 
     def __init__(self):
         self.requested = False
+        self._pipe = None
 
     def install(self):
         import signal
@@ -445,6 +449,35 @@ class _StopRequest:
 
         signal.signal(signal.SIGTERM, handler)
         return self
+
+    def abort_on_signal(self, pg):
+        """Once the GPU process group exists: SIGTERM also aborts it (watcher thread)."""
+        import signal
+        import threading
+
+        if pg is not None and getattr(pg, "backend", "") == "nvlink":
+            r, w = os.pipe()
+            os.set_blocking(w, False)
+            signal.set_wakeup_fd(w, warn_on_full_buffer=False)
+            self._pipe = (r, w)
+
+            def watch():
+                while True:
+                    try:
+                        data = os.read(r, 64)
+                    except OSError:
+                        return
+                    if not data:
+                        return
+                    if signal.SIGTERM in data:
+                        self.requested = True
+                        try:
+                            pg.abort()
+                        except Exception:  # noqa: BLE001 - stopping anyway
+                            pass
+                        return
+
+            threading.Thread(target=watch, name="sigterm-abort", daemon=True).start()
 
 
 def main(argv=None):
@@ -463,6 +496,8 @@ def main(argv=None):
         batch_fn = lambda step, micro, r, w: rank_batch(cd.train, step, micro, a.batch, a.ctx, a.seed, r, w)  # noqa: E731
     cfg = GPTConfig(vocab=vocab, ctx=a.ctx, dim=a.dim, heads=a.heads, layers=a.layers, dtype=a.dtype)
     pg = make_group(a, device)
+    if device.type == "cuda":
+        stop.abort_on_signal(pg)
     tr = Trainer(a, cfg, device, pg)
     rank, world = tr.rank, tr.world
 

@@ -148,6 +148,38 @@ def test_peer_that_never_arrives_gives_commerror_not_a_hang():
     assert res[0][0] == "commerror" and res[0][2] == 20.0
 
 
+def _abort_while_blocked(pg):
+    import threading
+    import time
+
+    from dtrain_b200.utils.store import CommError
+    x = pg.alloc(1 << 16, torch.float32)
+    if pg.rank == 1:
+        pg._exchange("abort-test-done", b"")  # never joins the collective
+        return "skipped"
+    pg.timeout = 60.0
+    pg.allreduce(x, "ring", method="twoshot")
+    t0 = time.monotonic()
+    threading.Timer(1.0, pg.abort).start()  # e.g. the SIGTERM watcher of a stopping worker
+    out = "no error"
+    try:
+        pg.synchronize()  # blocked on the waiting kernel until the abort lands
+    except CommError as e:
+        y = torch.ones(10, device=x.device) * 2
+        out = ("commerror", "aborted" in str(e), time.monotonic() - t0, float(y.sum().item()))
+    pg._exchange("abort-test-done", b"")
+    return out
+
+
+@needs2
+def test_abort_ends_a_blocked_wait_long_before_the_timeout():
+    res = _run(2, _abort_while_blocked)
+    assert res[1] == "skipped"
+    kind, aborted, waited, ysum = res[0]
+    assert kind == "commerror" and aborted and ysum == 20.0
+    assert waited < 20.0  # the kernel's own timeout is 60 s
+
+
 def _desync(pg):
     import torch
     from dtrain_b200.utils.store import CommError
