@@ -133,6 +133,16 @@ __device__ __forceinline__ void load_row32(const bf16* rowp, int col, int N, flo
   }
 }
 
+// Staging slabs hold one 32x32 output chunk, one row per lane, in the layout of the
+// TMA store's swizzle mode, so that a warp's 16-byte stores hit distinct banks:
+//   bf16 rows (64 B, SWIZZLE_64B):   16-byte unit j of row r sits at unit j ^ ((r >> 1) & 3)
+//   fp32 rows (128 B, SWIZZLE_128B): 16-byte unit j of row r sits at unit j ^ (r & 7)
+// (unswizzled rows 64 / 128 B apart put 8 lanes of a store phase on 2 / 1 bank groups:
+// 4- and 8-way conflicts).  Slabs start on 2 KB boundaries, a multiple of both
+// patterns' periods (512 B and 1 KB), as the swizzled TMA store requires.
+__device__ __forceinline__ int slab_unit_bf16(int lane, int j) { return j ^ ((lane >> 1) & 3); }
+__device__ __forceinline__ int slab_unit_f32(int lane, int j) { return j ^ (lane & 7); }
+
 // Write 32 fp32 values as bf16 into this lane's 64-byte row of a slab.
 __device__ __forceinline__ void slab_put_bf16(uint8_t* slab, int lane, const float* v) {
   uint4* dst = reinterpret_cast<uint4*>(slab + lane * 64);
@@ -143,14 +153,15 @@ __device__ __forceinline__ void slab_put_bf16(uint8_t* slab, int lane, const flo
     u.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
     u.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
     u.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
-    dst[j] = u;
+    dst[slab_unit_bf16(lane, j)] = u;
   }
 }
 
 __device__ __forceinline__ void slab_put_f32(uint8_t* slab, int lane, const float* v) {
   float4* dst = reinterpret_cast<float4*>(slab + lane * 128);
 #pragma unroll
-  for (int j = 0; j < 8; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  for (int j = 0; j < 8; ++j)
+    dst[slab_unit_f32(lane, j)] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
 }
 
 // Epilogues whose chunk is one 32x32 bf16 tile (2 KB) stage alternate chunks in the
@@ -222,7 +233,7 @@ __device__ __forceinline__ void epi_chunk(const GemmArgs& a, const CUtensorMap* 
           v[8 * j + 2 * e] = __uint_as_float(u[e] << 16);
           v[8 * j + 2 * e + 1] = __uint_as_float(u[e] & 0xffff0000u);
         }
-        dst[j] = make_uint4(u[0], u[1], u[2], u[3]);
+        dst[slab_unit_bf16(lane, j)] = make_uint4(u[0], u[1], u[2], u[3]);
       }
       break;
     }
@@ -916,11 +927,13 @@ static CUtensorMap make_map(const void* base, long rows, long cols, long ld, int
   return m;
 }
 
-// Store map: [rows, cols] (optionally [depth, rows, cols]) row-major, 32x32 boxes, no swizzle.
+// Store map: [rows, cols] (optionally [depth, rows, cols]) row-major, 32x32 boxes, with
+// the staging slabs' swizzle (64B for bf16 rows, 128B for fp32 rows).
 static CUtensorMap make_store_map(void* base, bool f32, long rows, long cols, long ld, long depth = 0) {
   CUtensorMap m;
   const int esz = f32 ? 4 : 2;
   const CUtensorMapDataType dt = f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const CUtensorMapSwizzle sw = f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r;
   if (depth > 0) {
@@ -928,14 +941,14 @@ static CUtensorMap make_store_map(void* base, bool f32, long rows, long cols, lo
     cuuint64_t strides[2] = {(cuuint64_t)ld * esz, (cuuint64_t)ld * rows * esz};
     cuuint32_t box[3] = {32, 32, 1};
     r = get_encode_fn()(&m, dt, 3, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                        sw, CU_TENSOR_MAP_L2_PROMOTION_NONE,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   } else {
     cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)ld * esz};
     cuuint32_t box[2] = {32, 32};
     r = get_encode_fn()(&m, dt, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                        sw, CU_TENSOR_MAP_L2_PROMOTION_NONE,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   }
   TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (store) failed with code ", (int)r);
