@@ -265,26 +265,68 @@ __global__ void __launch_bounds__(kThreads)
 }
 
 // delta[bh, t] = sum_d dO[t, h, d] * O[t, h, d]
+// D/8 consecutive lanes share a row: each loads 16 bytes of O and of dO (8 values),
+// sums its 8 products in order, and the lanes then combine with a fixed shuffle tree.
+// Rows are numbered (b, h, t) with t fastest, so the delta writes of a warp are
+// contiguous; every thread walks two rows per iteration (four 16-byte loads in flight)
+// over a grid-stride loop.
 template <int D>
-__global__ void delta_kernel(const bf16* __restrict__ o, const bf16* __restrict__ dout, float* __restrict__ delta,
-                             int B, int T, int H) {
-  const long w = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;  // one warp per (b, t, h)
-  const int lane = threadIdx.x & 31;
-  if (w >= (long)B * T * H) return;
-  const int h = (int)(w % H);
-  const long bt = w / H;
-  const int b = (int)(bt / T), t = (int)(bt % T);
-  const bf16* op = o + bt * (long)H * D + (long)h * D;
-  const bf16* gp = dout + bt * (long)H * D + (long)h * D;
-  float s = 0.f;
-  for (int d = lane * 2; d < D; d += 64) {
-    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(op + d));
-    const float2 c = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(gp + d));
-    s += a.x * c.x + a.y * c.y;
-  }
+__global__ void __launch_bounds__(256)
+    delta_kernel(const bf16* __restrict__ o, const bf16* __restrict__ dout, float* __restrict__ delta, int B, int T,
+                 int H) {
+  constexpr int L = D / 8;  // lanes per row
+  const int sub = threadIdx.x % L;
+  const long nrows = (long)B * H * T;
+  const long groups = (long)gridDim.x * (blockDim.x / L);
+  const long stride = (long)H * D;  // elements between consecutive t of one (b, h)
+  auto row_ptr = [&](long r, const bf16* base) {
+    const long t = r % T, bh = r / T;
+    const long b = bh / H, h = bh % H;
+    return base + (b * T + t) * stride + h * D + sub * 8;
+  };
+  auto dot8 = [](const uint4& a, const uint4& g) {
+    const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, gw[4] = {g.x, g.y, g.z, g.w};
+    float acc = 0.f;
 #pragma unroll
-  for (int k = 16; k > 0; k >>= 1) s += __shfl_xor_sync(0xffffffffu, s, k);
-  if (lane == 0) delta[((long)b * H + h) * T + t] = s;
+    for (int e = 0; e < 4; ++e) {
+      acc = fmaf(__uint_as_float(aw[e] << 16), __uint_as_float(gw[e] << 16), acc);
+      acc = fmaf(__uint_as_float(aw[e] & 0xffff0000u), __uint_as_float(gw[e] & 0xffff0000u), acc);
+    }
+    return acc;
+  };
+  const long first = (long)blockIdx.x * (blockDim.x / L) + threadIdx.x / L;  // this lane's row group
+  const long in_warp = (threadIdx.x / L) % (32 / L);                         // its index inside the warp
+  // the loop runs on the warp's first row group, so every lane of a warp takes the same
+  // number of iterations and the shuffles below always see the whole warp
+  for (long w0 = first - in_warp; w0 < nrows; w0 += 2 * groups) {
+    const long r = w0 + in_warp, r2 = r + groups;
+    const bool ok = r < nrows, ok2 = r2 < nrows;
+    uint4 a{}, g{}, a2{}, g2{};
+    if (ok) {
+      a = *reinterpret_cast<const uint4*>(row_ptr(r, o));
+      g = *reinterpret_cast<const uint4*>(row_ptr(r, dout));
+    }
+    if (ok2) {
+      a2 = *reinterpret_cast<const uint4*>(row_ptr(r2, o));
+      g2 = *reinterpret_cast<const uint4*>(row_ptr(r2, dout));
+    }
+    float s = dot8(a, g), s2 = dot8(a2, g2);
+#pragma unroll
+    for (int k = L / 2; k > 0; k >>= 1) {
+      s += __shfl_xor_sync(0xffffffffu, s, k);
+      s2 += __shfl_xor_sync(0xffffffffu, s2, k);
+    }
+    if (sub == 0) {
+      if (ok) delta[r] = s;
+      if (ok2) delta[r2] = s2;
+    }
+  }
+}
+
+// Grid of the delta kernel: enough 256-thread blocks for every SM to keep a few resident.
+inline unsigned delta_grid(long nrows, int D) {
+  const long rows_per_block = 256 / (D / 8);
+  return (unsigned)std::max<long>(1, std::min<long>((nrows + 2 * rows_per_block - 1) / (2 * rows_per_block), 148 * 8));
 }
 
 // dK, dV for one 64-key tile; warps own 16 keys each.
@@ -530,7 +572,7 @@ std::vector<torch::Tensor> attn_fwd(torch::Tensor qkv, int64_t B, int64_t T, int
 // delta = rowsum(dout * out) [B*H, T] for head dim 64 (one warp per row).
 void attn_delta64(torch::Tensor out, torch::Tensor dout, torch::Tensor delta, int64_t B, int64_t T, int64_t H) {
   const long warps = B * T * H;
-  attn::delta_kernel<64><<<(unsigned)((warps * 32 + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+  attn::delta_kernel<64><<<attn::delta_grid(warps, 64), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const bf16*>(out.data_ptr()), reinterpret_cast<const bf16*>(dout.data_ptr()),
       delta.data_ptr<float>(), (int)B, (int)T, (int)H);
   count_launch();
@@ -569,7 +611,7 @@ torch::Tensor attn_bwd(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout,
   const long warps = B * T * H;
   dim3 grid((unsigned)((T + 63) / 64), (unsigned)(B * H));
   if (D == 64) {
-    attn::delta_kernel<64><<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(o, g, delta.data_ptr<float>(),
+    attn::delta_kernel<64><<<attn::delta_grid(warps, 64), 256, 0, st>>>(o, g, delta.data_ptr<float>(),
                                                                                  (int)B, (int)T, (int)H);
     const int smem_kv = 6 * 64 * 64 * 2 + 4 * 64 * 4;
     const int smem_q = 6 * 64 * 64 * 2;
@@ -582,7 +624,7 @@ torch::Tensor attn_bwd(torch::Tensor qkv, torch::Tensor out, torch::Tensor dout,
     k2<<<grid, attn::kThreads, smem_q, st>>>(q, g, lse.data_ptr<float>(), delta.data_ptr<float>(), dq, (int)T,
                                              (int)H, sl2, scale);
   } else {
-    attn::delta_kernel<128><<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(o, g, delta.data_ptr<float>(),
+    attn::delta_kernel<128><<<attn::delta_grid(warps, 128), 256, 0, st>>>(o, g, delta.data_ptr<float>(),
                                                                                   (int)B, (int)T, (int)H);
     const int smem_kv = 6 * 64 * 128 * 2 + 4 * 64 * 4;
     const int smem_q = 6 * 64 * 128 * 2;
