@@ -411,6 +411,7 @@ struct BwBars {
   uint64_t fixed_full;
   uint64_t s0_full[2], s0_empty[2], s1_full[2], s1_empty[2];
   uint64_t s_full[2], x_free[2], p_ready[2], dp_full[2], pv_done[2], x_free2[2], ds_ready[2], ds_done[2];
+  uint64_t ds_free[2];  // dK/dV with dS stores: the store of sub-tile t's dS tile has read it
   uint64_t done;
   uint32_t tmem_slot;
   int abort_flag;
@@ -492,6 +493,7 @@ __global__ void __maxnreg__(DTB_CORESIDENT_MAXNREG_ATTN)
       mbar_init(&bars->x_free2[k], 4);
       mbar_init(&bars->ds_ready[k], 4);
       mbar_init(&bars->ds_done[k], 1);
+      mbar_init(&bars->ds_free[k], 1);
     }
     mbar_init(&bars->done, 1);
     bars->abort_flag = 0;
@@ -574,10 +576,25 @@ __global__ void __maxnreg__(DTB_CORESIDENT_MAXNREG_ATTN)
             tc_commit(&bars->s_full[t]);
           }
       }
+      // dS tile stores issued in the previous iteration have long read their source by
+      // the next one: confirm that there and release the tiles (ds_free) to the
+      // element-wise warps, which write the next P into them - so waiting for a store
+      // never holds up the MMA issue
+      bool store_pending[2] = {false, false};
+      auto release_stored = [&]() {
+        if (!(store_pending[0] || store_pending[1])) return;
+        bulk_wait_read0();
+        for (int t = 0; t < 2; ++t)
+          if (store_pending[t]) {
+            mbar_arrive(&bars->ds_free[t]);
+            store_pending[t] = false;
+          }
+      };
       for (int s = s_lo; s <= s_hi && ok; ++s) {
         const int it = s - s_lo, st = it & 1;
         const uint32_t ph = (it >> 1) & 1;
         const uint32_t s0 = S0 + st * TILE, s1 = S1 + st * TILE;
+        if (DKDV && store_ds) release_stored();
         if (!mbar_wait(&bars->s1_full[st], ph, abort_flag)) { ok = false; break; }
         // dP_t = dO . V^T into X_t once the element-wise warps have read the scores
         for (int t = 0; t < 2 && ok; ++t) {
@@ -630,10 +647,8 @@ __global__ void __maxnreg__(DTB_CORESIDENT_MAXNREG_ATTN)
               bulk_commit();
             }
             issue_g(t, BW_G + t * 128, s0, k > 0);
-            // the element-wise warps overwrite the tile once ds_done arrives: the store
-            // must have read it by then
-            if (DKDV && store_ds) bulk_wait_read0();
             tc_commit(&bars->ds_done[t]);
+            if (DKDV && store_ds) store_pending[t] = true;  // released at the top of the next iteration
           }
         }
         if (!ok) break;
@@ -727,6 +742,8 @@ __global__ void __maxnreg__(DTB_CORESIDENT_MAXNREG_ATTN)
         }
         if (DKDV) {  // P is the A operand of dV += P^T dO: the previous dS must have been consumed
           if (k > 0 && !mbar_wait(&bars->ds_done[t], (k - 1) & 1, abort_flag)) { ok = false; break; }
+          // ... and, when it is stored for the dQ GEMM, read by its store
+          if (k > 0 && store_ds && !mbar_wait(&bars->ds_free[t], (k - 1) & 1, abort_flag)) { ok = false; break; }
           tc_fence_after();
           put_row128(A, r, pk);
           fence_proxy_async_smem();
