@@ -48,10 +48,39 @@ ORDER_RANK, ORDER_CYCLIC = 0, 1
 ALGO_ONESHOT, ALGO_TWOSHOT = 0, 1
 # [max CTAs][max ranks] uint32 flags, then a ring of 16 uint64 collective descriptors
 _SIG_BYTES = 8192
-# "auto" picks one-shot at or below this size and two-shot above it.  One-shot
-# moves W times the data but needs one cross-rank barrier fewer; its result is
-# written out of place and copied back.
-ONESHOT_MAX_BYTES = int(os.environ.get("DTB_ONESHOT_MAX_BYTES", 64 * 1024))
+# One-shot moves (W-1) x the data into every rank but needs one cross-rank barrier
+# fewer than two-shot; its result is written out of place and copied back.
+# DTB_ONESHOT_MAX_BYTES overrides the size up to which "auto" picks it.
+_ONESHOT_ENV = os.environ.get("DTB_ONESHOT_MAX_BYTES")
+
+
+def auto_allreduce_plan(world: int, nbytes: int) -> tuple[str, int]:
+    """(method, CTA count; 0 = sized by the message) that ``method="auto"`` uses for an
+    all-reduce of ``nbytes`` over ``world`` ranks, from the CUDA-graph sweeps on B200
+    (benchmarks/collectives_bench.py at W = 2 and 4, fp32 and bf16):
+
+    * W = 2: one-shot moves the same bytes as two-shot and skips a barrier, so it wins
+      up to 16 MiB; above that two-shot with 128 CTAs (585 vs 510 GB/s for NCCL at 256 MiB).
+    * W = 3..4: one-shot up to 512 KiB, one-shot with 128 CTAs up to 4 MiB, two-shot
+      at 8 MiB, two-shot with 128 CTAs from 16 MiB.
+    * W > 4 (not measured): one-shot up to 256 KiB - its traffic grows with W - and
+      two-shot above, with 128 CTAs from 16 MiB.
+    Only the fixed-order methods are chosen (NVLS is opt-in).
+    """
+    mib = 1 << 20
+    if _ONESHOT_ENV is not None:
+        return ("oneshot", 0) if nbytes <= int(_ONESHOT_ENV) else ("twoshot", 128 if nbytes >= 16 * mib else 0)
+    if world <= 2:
+        return ("oneshot", 0) if nbytes <= 16 * mib else ("twoshot", 128)
+    if world <= 4:
+        if nbytes <= 512 * 1024:
+            return "oneshot", 0
+        if nbytes <= 4 * mib:
+            return "oneshot", 128
+        return ("twoshot", 0) if nbytes < 16 * mib else ("twoshot", 128)
+    if nbytes <= 256 * 1024:
+        return "oneshot", 0
+    return ("twoshot", 0) if nbytes < 16 * mib else ("twoshot", 128)
 
 
 class FdExchange:
@@ -412,8 +441,8 @@ class NVLinkGroup:
         multimem.ld_reduce and written to every rank by multimem.st: the least
         NVLink traffic from 4 ranks up; needs a group made with ``nvls``; every rank
         gets the same bits, but the order of the additions is the switch's, so
-        ``algo`` does not apply) or "auto" (one-shot up to ``ONESHOT_MAX_BYTES``,
-        two-shot above).  Two-shot on a peer-mapped tensor
+        ``algo`` does not apply) or "auto" (method and CTA count by size and world,
+        ``auto_allreduce_plan``).  Two-shot on a peer-mapped tensor
         also takes ``blocks`` (CTA count, 0: by size), ``lean`` (128-thread CTAs
         that share SMs with running GEMMs) and ``sq = (pad, base, stride)``: CTA b
         writes the sum of squares of the scaled values it reduced into slot
@@ -430,7 +459,12 @@ class NVLinkGroup:
         n = t.numel()
         nbytes = n * t.element_size()
         if method == "auto":
-            method = "oneshot" if (nbytes <= ONESHOT_MAX_BYTES and not lean and sq is None) else "twoshot"
+            if lean or sq is not None:
+                method = "twoshot"
+            else:
+                method, plan_blocks = auto_allreduce_plan(self.world, nbytes)
+                if not blocks and not self.blocks:
+                    blocks = plan_blocks
         if method == "nvls":
             return self._allreduce_nvls(t, scale, blocks, sq, lean)
         if method == "twoshot" and self._eng.contains(t):
