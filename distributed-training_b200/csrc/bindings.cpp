@@ -62,6 +62,8 @@ bool mc_supported();
 int64_t mc_granularity(int64_t ndev);
 std::tuple<int64_t, int64_t> mc_create(int64_t size, int64_t ndev);
 int64_t mc_import(int64_t fd);
+void mc_add_device(int64_t mc);
+void mc_release(int64_t mc);
 int64_t mc_bind_map(int64_t mc, int64_t local_va, int64_t size, int64_t ndev);
 void mc_free(int64_t mc_va);
 int64_t comm_status();
@@ -161,6 +163,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mc_granularity", &mc_granularity);
   m.def("mc_create", &mc_create);
   m.def("mc_import", &mc_import);
+  m.def("mc_add_device", &mc_add_device);
+  m.def("mc_release", &mc_release);
   m.def("mc_bind_map", &mc_bind_map);
   m.def("mc_free", &mc_free);
   m.def("comm_status", &comm_status);

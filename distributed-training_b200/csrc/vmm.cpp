@@ -296,10 +296,23 @@ int64_t mc_import(int64_t fd) {
   return (int64_t)h;
 }
 
-// Adds the current device to multicast object `mc`, binds this rank's VMM allocation
-// `local_va` (from vmm_alloc, `size` bytes) to it and maps the object (made for
-// `ndev` devices) for the current device.  Returns the multicast address: multimem instructions on it reach every
-// rank's allocation at the same offset.  On failure the object is released.
+// Adds the current device to multicast object `mc`.  Every rank must have done so
+// before any rank binds memory (the driver blocks a bind until the whole team has
+// joined), so the caller confirms that all ranks joined - over the host - before it
+// calls mc_bind_map; on failure it releases the object with mc_release.
+void mc_add_device(int64_t mc) {
+  const CUresult r = api().mcAddDevice((CUmemGenericAllocationHandle)mc, current_cu_device());
+  TORCH_CHECK(r == CUDA_SUCCESS, "vmm: cuMulticastAddDevice failed with code ", (int)r);
+}
+
+// Drops this process's reference to a multicast object that was never mapped.
+void mc_release(int64_t mc) { api().release((CUmemGenericAllocationHandle)mc); }
+
+// Binds this rank's VMM allocation `local_va` (from vmm_alloc, `size` bytes) to
+// multicast object `mc` (which every rank has joined, see mc_add_device) and maps the
+// object (made for `ndev` devices) for the current device.  Returns the multicast
+// address: multimem instructions on it reach every rank's allocation at the same
+// offset.  On failure the object is released.
 int64_t mc_bind_map(int64_t mc, int64_t local_va, int64_t size, int64_t ndev) {
   const VmmApi& A = api();
   const CUmemGenericAllocationHandle h = (CUmemGenericAllocationHandle)mc;
@@ -314,12 +327,7 @@ int64_t mc_bind_map(int64_t mc, int64_t local_va, int64_t size, int64_t ndev) {
     local = it->second;
   }
   const CUdevice d = current_cu_device();
-  CUresult r = A.mcAddDevice(h, d);
-  if (r != CUDA_SUCCESS) {
-    A.release(h);
-    TORCH_CHECK(false, "vmm: cuMulticastAddDevice failed with code ", (int)r);
-  }
-  r = A.mcBindMem(h, 0, local.handle, 0, (size_t)size, 0);
+  CUresult r = A.mcBindMem(h, 0, local.handle, 0, (size_t)size, 0);
   if (r != CUDA_SUCCESS) {
     A.release(h);
     TORCH_CHECK(false, "vmm: cuMulticastBindMem failed with code ", (int)r);

@@ -224,8 +224,10 @@ class SymmetricBuffer:
 
     def _map_multicast(self, group: "NVLinkGroup", size: int) -> int:
         """Rank 0 creates an NVSwitch multicast object of ``size`` bytes and passes it
-        to the others by file descriptor; each rank binds this buffer's allocation to
-        it and maps it.  Returns the multicast address."""
+        to the others by file descriptor; every rank joins it, the ranks confirm over
+        the host that all of them joined (the driver would block a bind forever on a
+        rank that could not), then each binds this buffer's allocation and maps the
+        object.  Returns the multicast address."""
         C = lib()
         if group.rank == 0:
             mc, fd = C.mc_create(size, group.world)
@@ -241,6 +243,17 @@ class SymmetricBuffer:
                 mc = C.mc_import(fd)
             finally:
                 os.close(fd)
+        err = ""
+        try:
+            C.mc_add_device(mc)
+        except RuntimeError as e:
+            err = str(e).splitlines()[0]
+        group._mc_joins += 1
+        votes = group._exchange(f"mc-join/{group._mc_joins}", err.encode())
+        if any(votes):
+            C.mc_release(mc)
+            bad = {r: v.decode() for r, v in enumerate(votes) if v}
+            raise CommError(f"multicast: ranks could not join the NVSwitch multicast object: {bad}")
         return int(C.mc_bind_map(mc, self.ptr, size, group.world))
 
     def tensor(self, numel: int, dtype: torch.dtype, byte_offset: int = 0) -> torch.Tensor:
@@ -323,6 +336,7 @@ class NVLinkGroup:
         if self.nvls and self.memory != "vmm":
             raise ValueError("NVLS collectives need memory='vmm' (multicast objects bind VMM allocations)")
         self._mc_gran = 0
+        self._mc_joins = 0
         if self.nvls:
             with torch.cuda.device(self.device):
                 if not lib().mc_supported():
