@@ -72,6 +72,11 @@ class DDP:
     def __init__(self, model, pg, bucket_mb: float = 1.0, overlap: bool = True, algo: str = "ring",
                  method: str = "auto"):
         self.model, self.pg, self.overlap, self.algo, self.method = model, pg, overlap, algo, method
+        if method not in ("auto", "oneshot", "twoshot", "nvls"):
+            raise ValueError(f"unknown DDP all-reduce method {method!r} (auto, oneshot, twoshot or nvls)")
+        if method == "nvls" and getattr(pg, "world", 1) > 1 and not getattr(pg, "nvls", False):
+            # checked here rather than at the first bucket launch, in the middle of backward
+            raise ValueError("method='nvls' needs an NVLinkGroup made with nvls=True (DTB_NVLS=1)")
         self.params = list(model.parameters())
         self.gpu = getattr(pg, "backend", "tcp") == "nvlink"
         # one GPU: the flat buffer already holds the averaged gradient, nothing to launch

@@ -34,3 +34,19 @@ def test_plan_is_monotone_in_size():
             m, _ = auto_allreduce_plan(world, 1 << k)
             seen_twoshot = seen_twoshot or m == "twoshot"
             assert not (seen_twoshot and m == "oneshot"), (world, k)
+
+
+def test_ddp_refuses_nvls_without_a_multicast_group_before_any_backward():
+    """An NVLS request on a group without multicast fails when the DDP wrapper is made,
+    not at the first bucket launch in the middle of a backward pass."""
+    import torch
+
+    from dtrain_b200.parallel.ddp import DDP
+
+    class HostGroup:
+        backend, world, rank, nvls = "tcp", 2, 0, False
+
+    with pytest.raises(ValueError, match="nvls=True"):
+        DDP(torch.nn.Linear(2, 2), HostGroup(), method="nvls")
+    with pytest.raises(ValueError, match="unknown DDP all-reduce method"):
+        DDP(torch.nn.Linear(2, 2), HostGroup(), method="ringz")
