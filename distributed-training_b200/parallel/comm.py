@@ -32,7 +32,8 @@ import numpy as np
 from ..utils.store import CommError, Store, StoreServer  # noqa: F401  (re-exported API)
 
 _HDR = struct.Struct("<QQ")       # sequence number, payload bytes
-_INLINE_MAX = 64 << 10            # sends up to this size go out on the caller's thread
+_INLINE_MIN = 64 << 10            # sends up to this size always go out on the caller's thread
+_INLINE_CAP = 1 << 20             # ... and up to this size when the socket buffers are large
 
 
 def partition(n: int, world: int) -> list[int]:
@@ -95,6 +96,16 @@ class _Link:
             except OSError:
                 pass
         sock.settimeout(timeout)
+        # A send that fits in the kernel's socket buffers returns without waiting for the
+        # reader, so it can go out on the caller's thread (no hand-off to the sender
+        # thread).  Up to W-1 such messages of a ring may sit unread on one connection,
+        # so the inline limit stays at an eighth of the smaller buffer.
+        try:
+            room = min(sock.getsockopt(socket.SOL_SOCKET, socket.SO_SNDBUF),
+                       sock.getsockopt(socket.SOL_SOCKET, socket.SO_RCVBUF))
+        except OSError:
+            room = 0
+        self.inline_max = max(_INLINE_MIN, min(_INLINE_CAP, room // 8))
         self.error: BaseException | None = None
         self._jobs: queue.SimpleQueue = queue.SimpleQueue()
         self._pending = 0
@@ -122,17 +133,21 @@ class _Link:
         hdr = _HDR.pack(seq, view.nbytes)
         with self._lock:
             idle = self._pending == 0
-            if not (idle and view.nbytes <= _INLINE_MAX):
+            if not (idle and view.nbytes <= self.inline_max):
                 self._pending += 1
-        if idle and view.nbytes <= _INLINE_MAX:
+        if idle and view.nbytes <= self.inline_max:
             # fits in the socket buffer: sendall returns without waiting for the reader
             try:
-                self.sock.sendall(hdr + view.tobytes())
+                if view.nbytes <= _INLINE_MIN:
+                    self.sock.sendall(hdr + view.tobytes())
+                else:  # no copy of a large payload just to prepend the header
+                    self.sock.sendall(hdr)
+                    self.sock.sendall(view)
             except BaseException as e:  # noqa: BLE001
                 self.error = e
             done.set()
             return done
-        self._jobs.put((hdr + view.tobytes() if view.nbytes <= _INLINE_MAX else _Chain(hdr, view), done))
+        self._jobs.put((hdr + view.tobytes() if view.nbytes <= _INLINE_MIN else _Chain(hdr, view), done))
         return done
 
     def _recv_into(self, view: memoryview):
