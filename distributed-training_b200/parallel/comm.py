@@ -99,13 +99,14 @@ class _Link:
         # A send that fits in the kernel's socket buffers returns without waiting for the
         # reader, so it can go out on the caller's thread (no hand-off to the sender
         # thread).  Up to W-1 such messages of a ring may sit unread on one connection,
-        # so the inline limit stays at an eighth of the smaller buffer.
+        # and Linux reports twice the usable buffer size, so the inline limit stays at a
+        # sixteenth of the smaller reported buffer (8 unread messages still fit).
         try:
             room = min(sock.getsockopt(socket.SOL_SOCKET, socket.SO_SNDBUF),
                        sock.getsockopt(socket.SOL_SOCKET, socket.SO_RCVBUF))
         except OSError:
             room = 0
-        self.inline_max = max(_INLINE_MIN, min(_INLINE_CAP, room // 8))
+        self.inline_max = max(_INLINE_MIN, min(_INLINE_CAP, room // 16))
         self.error: BaseException | None = None
         self._jobs: queue.SimpleQueue = queue.SimpleQueue()
         self._pending = 0
